@@ -1,0 +1,393 @@
+#!/usr/bin/env python
+"""Benchmark of the packed-KV hot path on B200 (one process per GPU).
+
+Workload (BASELINE config 3 at its 8K point, on a whole 32-layer cache): a
+SmolLM2-360M-shape cache (32 layers, 5 KV heads, 15 query heads, head_dim 64)
+holds P = 8128 packed history tokens in 64-token frames whose precision is drawn
+from the seeded 50/30/20 int4/int8/bf16 mix; keys carry 4 seeded 8x outlier
+channels. One STEP is the 64-token frame-append attention of all 32 layers
+(GPUCache.attend per layer: 64 queries over 8128 packed + 64 native tokens). The
+32 layers' caches (~185 MB) exceed the 126 MB L2, so every step streams its
+history from HBM. Each rank builds its own independent request (seed = rank):
+weak scaling, no collective on the data path.
+
+Printed (rank 0, one JSON line):
+  value      packed-KV attention HBM GB/s, algorithmic bytes of all ranks / max time
+             (device-resident inputs; the 32-layer sweep replayed as a CUDA graph)
+  e2e        same metric through the public API (GPUCache.attend) with pinned host
+             buffers: per layer H2D of q/k/v and D2H of the output inside the timing
+  frame_append_tokens_per_s  pack + attend of a 64-token frame on all 32 layers
+  roofline   dominant op (attention) vs measured HBM peak; roofline_tensor vs bf16
+  cpu_baseline  the reference CPU path (dequantise + torch SDPA, oracle port) on a
+             bounded sample of the same workload, all host cores
+`--impl reference` times only that CPU path and prints its own line.
+"""
+import argparse
+import datetime
+import json
+import os
+import random
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (str(ROOT), str(ROOT / 'dynamic-kv-cache_b200')):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+LAYERS, HEADS, GROUP, DIM = 32, 5, 3, 64
+PAST, NQ, FRAME = 8128, 64, 64
+MIX = ([4, 8, 16], [0.5, 0.3, 0.2])
+ROW_BYTES = {4: 32 + 8, 8: 64 + 8, 16: 128}  # code bytes + (offset, scale) per row
+METRIC = 'packed-KV attention HBM GB/s at 8K ctx'
+WORKLOAD = 'C3 frame-append attention, 8K ctx, 32-layer cache'
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=3000)
+    ap.add_argument('--warmup', type=int, default=5)
+    ap.add_argument('--impl', choices=['ours', 'reference'], default='ours')
+    ap.add_argument('--cpu-seconds', type=float, default=12.0, help='CPU-baseline sample budget')
+    ap.add_argument('--e2e-steps', type=int, default=30)
+    ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--layers', type=int, default=LAYERS,
+                    help='cache layers (the per-call workload is unchanged; fewer layers only shrink '
+                         'the set-up for profiler captures)')
+    args = ap.parse_args()
+    globals()['LAYERS'] = args.layers
+    return args
+
+
+def frame_plan(seed):
+    frames = (PAST + FRAME - 1) // FRAME
+    bits = random.Random(seed).choices(MIX[0], weights=MIX[1], k=frames)
+    sizes = [FRAME] * (frames - 1) + [PAST - FRAME * (frames - 1)]
+    return list(zip(bits, sizes))
+
+
+def attention_bytes(plan):
+    """Algorithmic HBM bytes of one attention call: each history row once (codes +
+    metadata), the 5-byte token map entry per history token, Q and the output
+    once, the native new K/V once."""
+    hist = sum(2 * HEADS * n * ROW_BYTES[b] for b, n in plan)
+    maps = 5 * PAST
+    q_out = 2 * NQ * HEADS * GROUP * DIM * 2
+    new_kv = 2 * NQ * HEADS * DIM * 2
+    return hist + maps + q_out + new_kv
+
+
+def attention_flops():
+    return 4 * HEADS * GROUP * DIM * (NQ * PAST + NQ * (NQ + 1) // 2)
+
+
+def pack_bytes(bits):
+    return 2 * HEADS * FRAME * DIM * 2 + 2 * HEADS * FRAME * ROW_BYTES[bits]
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms while running."""
+    FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
+              'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
+              'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, device_index):
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(
+                ['nvidia-smi', f'--query-gpu={self.FIELDS}', '--format=csv,noheader,nounits', '-lms', '200',
+                 '-i', str(device_index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {'sm_mhz': None, 'sm_max_mhz': None, 'reasons': ['nvidia-smi unavailable']}
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sm, smax, reasons = [], [], set()
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(',')]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower() == 'active':
+                    reasons.add(name)
+        return {'sm_mhz': statistics.median(sm) if sm else None, 'sm_max_mhz': max(smax) if smax else None,
+                'reasons': sorted(reasons), 'samples': len(sm)}
+
+
+def build_cache(seed, device):
+    from src.gpu_cache import GPUCache
+    gen = torch.Generator(device=device).manual_seed(seed)
+    outliers = torch.randperm(DIM, generator=torch.Generator().manual_seed(seed))[:4].to(device)
+    plan = frame_plan(seed)
+    cache = GPUCache(None, layers=LAYERS, heads=HEADS, device=device)
+    for f, (bits, n) in enumerate(plan):
+        cache.select(bits, f)
+        for layer in range(LAYERS):
+            k = torch.randn(1, HEADS, n, DIM, generator=gen, device=device)
+            k[..., outliers] *= 8
+            v = torch.randn(1, HEADS, n, DIM, generator=gen, device=device)
+            cache.append(k.bfloat16(), v.bfloat16(), layer)
+    for b in (4, 8, 16):  # room for the timed frame appends without growth
+        cache.reserve(b, cache.host_counts[b] + FRAME)
+    q = torch.randn(LAYERS, 1, HEADS * GROUP, NQ, DIM, generator=gen, device=device).bfloat16()
+    kn = torch.randn(LAYERS, 1, HEADS, NQ, DIM, generator=gen, device=device)
+    kn[..., outliers] *= 8
+    kn = kn.bfloat16()
+    vn = torch.randn(LAYERS, 1, HEADS, NQ, DIM, generator=gen, device=device).bfloat16()
+    cache.check()
+    return cache, plan, q, kn, vn
+
+
+def cpu_baseline(seconds, threads=None):
+    """Times the reference CPU path (oracle port: unpack every stored frame, keep
+    the current frame native, torch SDPA) on layers of the same workload."""
+    import numpy as np
+    from oracle import cpu_path, pools
+    threads = threads or os.cpu_count()
+    torch.set_num_threads(threads)
+    plan = frame_plan(0)
+    gen = torch.Generator().manual_seed(0)
+    outliers = torch.randperm(DIM, generator=gen)[:4]
+
+    def bits_np(t):
+        return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+    frames = []
+    for bits, n in plan:
+        k = torch.randn(1, HEADS, n, DIM, generator=gen)
+        k[..., outliers] *= 8
+        v = torch.randn(1, HEADS, n, DIM, generator=gen)
+        frames.append(pools.pack_frame(bits_np(k.bfloat16()), bits_np(v.bfloat16()), bits))
+    q = torch.randn(1, HEADS * GROUP, NQ, DIM, generator=gen).bfloat16().float()
+    kn = torch.randn(1, HEADS, NQ, DIM, generator=gen).bfloat16().float()
+    vn = torch.randn(1, HEADS, NQ, DIM, generator=gen).bfloat16().float()
+    cpu_path.cpu_cache_attention(frames, q, kn, vn)  # warm-up
+    calls, start = 0, time.perf_counter()
+    while True:
+        cpu_path.cpu_cache_attention(frames, q, kn, vn)
+        calls += 1
+        elapsed = time.perf_counter() - start
+        if elapsed >= seconds or calls >= 10000:
+            break
+    gbs = attention_bytes(plan) * calls / elapsed / 1e9
+    return {'value': gbs, 'unit': 'GB/s', 'cores': threads, 'kind': 'port',
+            'sample': f'{calls} single-layer calls (P={PAST}, n={NQ}, 15Q/5KV) of the reference CPU path '
+                      f'(unpack all frames + cat + torch SDPA) in {elapsed:.1f} s; ms/call {1e3 * elapsed / calls:.2f}'}
+
+
+def measured_peaks():
+    path = ROOT / 'MEASURED_PEAKS.json'
+    if path.exists():
+        d = json.loads(path.read_text())
+        return d['hbm_gbs'], d['bf16_tflops'], 'measured'
+    return 6650.0, 1590.0, 'fallback'
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    base = cpu_baseline(args.cpu_seconds)
+    line = {'impl': 'reference', 'metric': METRIC, 'value': base['value'], 'unit': 'GB/s', 'n_gpus': args.gpus,
+            'steps': args.steps, 'warmup': args.warmup, 'higher_is_better': True, 'scaling': 'weak',
+            'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic (seeded, BASELINE config 3 shapes)',
+            'config': {'workload': WORKLOAD + ' (CPU reference path)', 'past': PAST, 'nq': NQ,
+                       'layers_sampled': 'single-layer calls', 'heads': '15Q/5KV', 'head_dim': DIM},
+            'cpu_baseline': base,
+            'e2e': {'value': base['value'], 'unit': 'GB/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device('cuda', local))
+    if args.impl == 'reference':
+        run_reference(args, rank)
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+
+    device = torch.device('cuda', local)
+    torch.cuda.set_device(device)
+    cache, plan, q, kn, vn = build_cache(1000 + rank, device)
+    stream = torch.cuda.Stream(device)
+
+    # ---- 32-layer attention sweep, captured once and replayed ----
+    outs = [None] * LAYERS
+
+    def sweep():
+        for layer in range(LAYERS):
+            outs[layer] = cache.attend(q[layer], kn[layer], vn[layer], layer, PAST)
+
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            sweep()
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        sweep()
+    torch.cuda.synchronize(device)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            graph.replay()
+    barrier()
+    clocks = ClockSampler(device.index)
+    time.sleep(0.25)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        end.record(stream)
+    barrier()
+    clock = clocks.stop()
+    ms_total = start.elapsed_time(end)
+    t = torch.tensor([ms_total], device=device)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_total = float(t.item())
+    ms_step = ms_total / args.steps
+    bytes_call = attention_bytes(plan)
+    value = world * LAYERS * bytes_call * args.steps / (ms_total * 1e-3) / 1e9
+    us_call = 1e3 * ms_step / LAYERS
+
+    # ---- frame append (pack + attend on a fork, 32 layers), captured and replayed ----
+    branch = cache.fork()
+    branch.select(16)
+    fa_outs = [None] * LAYERS
+
+    def frame_sweep():
+        b = branch.fork()
+        b.select(16)
+        for layer in range(LAYERS):
+            p = b.append(kn[layer], vn[layer], layer)
+            fa_outs[layer] = b.attend(q[layer], kn[layer], vn[layer], layer, p)
+
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            frame_sweep()
+    torch.cuda.synchronize(device)
+    fgraph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(fgraph, stream=stream):
+        frame_sweep()
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            fgraph.replay()
+    barrier()
+    fsteps = max(1, args.steps // 2)
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(fsteps):
+            fgraph.replay()
+        end.record(stream)
+    barrier()
+    t = torch.tensor([start.elapsed_time(end)], device=device)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    fa_ms_step = float(t.item()) / fsteps
+    fa_tokens_s = world * FRAME / (fa_ms_step * 1e-3)
+
+    # ---- e2e through the public API with pinned host buffers ----
+    hq = q.cpu().pin_memory()
+    hk = kn.cpu().pin_memory()
+    hv = vn.cpu().pin_memory()
+    hout = torch.empty((LAYERS, 1, NQ, HEADS * GROUP, DIM), dtype=torch.bfloat16).pin_memory()
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(kn), torch.empty_like(vn)
+
+    def e2e_step():
+        for layer in range(LAYERS):
+            dq[layer].copy_(hq[layer], non_blocking=True)
+            dk[layer].copy_(hk[layer], non_blocking=True)
+            dv[layer].copy_(hv[layer], non_blocking=True)
+            out = cache.attend(dq[layer], dk[layer], dv[layer], layer, PAST)
+            hout[layer].copy_(out, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            e2e_step()
+    barrier()
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        end.record(stream)
+    barrier()
+    t = torch.tensor([start.elapsed_time(end)], device=device)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t.item()) / args.e2e_steps
+    e2e_value = world * LAYERS * bytes_call / (e2e_ms * 1e-3) / 1e9
+    h2d = LAYERS * (q[0].numel() + kn[0].numel() + vn[0].numel()) * 2
+    d2h = LAYERS * hout[0].numel() * 2
+    cache.check()
+
+    from src import gpu_kernels as K
+    launches_per_call = 2 if K.attention_workspace_bytes(PAST, NQ, HEADS, GROUP) else 1
+    hbm, tflops, peak_kind = measured_peaks()
+    achieved = bytes_call / (us_call * 1e-6) / 1e9
+    achieved_tf = attention_flops() / (us_call * 1e-6) / 1e12
+    line = {
+        'metric': METRIC, 'value': value, 'unit': 'GB/s', 'n_gpus': world, 'steps': args.steps,
+        'warmup': args.warmup, 'ms_per_step': ms_step, 'higher_is_better': True, 'scaling': 'weak',
+        'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic (seeded; BASELINE config 3 shapes and mix)',
+        'config': {'workload': WORKLOAD, 'layers': LAYERS, 'kv_heads': HEADS, 'q_heads': HEADS * GROUP,
+                   'head_dim': DIM, 'past': PAST, 'nq': NQ, 'mix': '50/30/20 int4/int8/bf16 per frame',
+                   'step': '32 x GPUCache.attend (one layer each), CUDA-graph replay',
+                   'l2': f'{LAYERS}-layer working set ~{LAYERS * bytes_call // 2**20} MB vs 126 MB L2 '
+                         '(larger than L2 at the default 32 layers: no flush needed)',
+                   'requests': f'one independent request per rank (seed 1000+rank)', 'parallelism': f'dp{world}'},
+        'us_per_layer_call': us_call,
+        'frame_append_tokens_per_s': fa_tokens_s,
+        'frame_append_ms_per_frame': fa_ms_step,
+        'e2e': {'value': e2e_value, 'unit': 'GB/s', 'h2d_bytes_per_step': h2d, 'd2h_bytes_per_step': d2h,
+                'ms_per_step': e2e_ms, 'api': 'GPUCache.attend with pinned-host q/k/v in, output out'},
+        'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': hbm, 'unit': 'GB/s', 'frac': achieved / hbm,
+                     'traffic': None, 'peak_kind': peak_kind,
+                     'bytes_per_launch': bytes_call, 'note': 'attention op (split kernel + combine) per layer call'},
+        'roofline_tensor': {'bound': 'tensor', 'achieved': achieved_tf, 'peak': tflops, 'unit': 'TFLOP/s',
+                            'frac': achieved_tf / tflops, 'peak_kind': peak_kind,
+                            'flops_per_launch': attention_flops()},
+        'gpu_launches': args.steps * LAYERS * launches_per_call,
+        'clocks': clock,
+    }
+    if rank == 0 and not args.no_cpu_baseline:
+        line['cpu_baseline'] = cpu_baseline(args.cpu_seconds)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del graph, fgraph
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == '__main__':
+    main()

@@ -1,0 +1,193 @@
+// extern "C" entry points of libdkv.so (declared in include/dkv.h).
+// Host-side argument validation mirrors the reference's ValueError conditions;
+// nothing here allocates, synchronises or retains pointers.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "attention.cuh"
+
+namespace dkv {
+cudaError_t launch_pack(const void* k, const void* v, void* p4, void* m4, void* p8, void* m8,
+                        void* p16, int64_t kh, int64_t kt, int64_t vh, int64_t vt, int layer,
+                        int64_t row_start, int n, int64_t cap, int heads, int bits,
+                        int32_t* status, cudaStream_t stream);
+cudaError_t launch_reconstruct(const Pools& P, const int32_t* rows, const uint8_t* codes, void* out,
+                               int layer, int n, int32_t* status, cudaStream_t stream);
+cudaError_t launch_map_fill(int32_t* rows, uint8_t* codes, int64_t start, int n, int64_t row, int bits,
+                            cudaStream_t stream);
+}  // namespace dkv
+
+namespace {
+
+thread_local char g_error[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_error, sizeof(g_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int ok() {
+  g_error[0] = '\0';
+  return DKV_OK;
+}
+
+int cuda_status(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) return fail(DKV_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+  return ok();
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// bf16 [1, heads, n, 64] operand with 16-byte aligned rows.
+bool rows_aligned(const void* p, int64_t hs, int64_t ts) {
+  return p != nullptr && aligned16(p) && (hs % 8) == 0 && (ts % 8) == 0;
+}
+
+int check_geometry(int32_t heads, int32_t dim, int32_t layers, int32_t layer) {
+  if (dim != dkv::kDim) return fail(DKV_EINVAL, "GPU kernel currently supports head_dim=64");
+  if (heads <= 0 || layers <= 0) return fail(DKV_EINVAL, "heads and layers must be positive");
+  if (layer < 0 || layer >= layers) return fail(DKV_EINVAL, "layer %d outside [0, %d)", layer, layers);
+  return DKV_OK;
+}
+
+int check_pools(const void* p4, const void* m4, const void* p8, const void* m8, const void* p16,
+                int64_t cap4, int64_t cap8, int64_t cap16) {
+  if (!p4 || !m4 || !p8 || !m8 || !p16) return fail(DKV_EINVAL, "null pool pointer");
+  if (!aligned16(p4) || !aligned16(p8) || !aligned16(p16) || !aligned16(m4) || !aligned16(m8))
+    return fail(DKV_EINVAL, "pools must be 16-byte aligned");
+  if (cap4 <= 0 || cap8 <= 0 || cap16 <= 0) return fail(DKV_EINVAL, "pool capacities must be positive");
+  if (cap4 > INT32_MAX || cap8 > INT32_MAX || cap16 > INT32_MAX)
+    return fail(DKV_EINVAL, "pool capacity exceeds int32 row index");
+  return DKV_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t dkv_version(void) { return DKV_VERSION; }
+
+const char* dkv_last_error(void) { return g_error; }
+
+int dkv_pack_rows(const void* k, const void* v, void* p4, void* m4, void* p8, void* m8, void* p16,
+                  int64_t kh, int64_t kt, int64_t vh, int64_t vt, int32_t layer, int64_t row_start,
+                  int32_t n, int64_t cap4, int64_t cap8, int64_t cap16, int32_t heads, int32_t dim,
+                  int32_t bits, int32_t layers, int32_t* status, void* stream) {
+  int rc = check_geometry(heads, dim, layers, layer);
+  if (rc) return rc;
+  if ((rc = check_pools(p4, m4, p8, m8, p16, cap4, cap8, cap16))) return rc;
+  if (bits != 4 && bits != 8 && bits != 16) return fail(DKV_EINVAL, "Supported bit widths: 4, 8, 16");
+  if (n < 0) return fail(DKV_EINVAL, "negative token count");
+  if (n == 0) return ok();
+  if (!rows_aligned(k, kh, kt) || !rows_aligned(v, vh, vt))
+    return fail(DKV_EINVAL, "k/v rows must be 16-byte aligned (head/token strides multiples of 8)");
+  const int64_t cap = bits == 4 ? cap4 : (bits == 8 ? cap8 : cap16);
+  if (row_start < 0 || row_start + n > cap)
+    return fail(DKV_ECAPACITY, "rows [%lld, %lld) exceed the %d-bit pool capacity %lld",
+                (long long)row_start, (long long)(row_start + n), bits, (long long)cap);
+  if (2LL * heads * n * 8 > INT32_MAX) return fail(DKV_EINVAL, "frame too large");
+  return cuda_status(dkv::launch_pack(k, v, p4, m4, p8, m8, p16, kh, kt, vh, vt, layer, row_start, n, cap,
+                                      heads, bits, status, static_cast<cudaStream_t>(stream)),
+                     "pack_rows launch");
+}
+
+size_t dkv_packed_attention_workspace(int32_t past, int32_t nq, int32_t heads, int32_t group, int32_t dim) {
+  if (past < 0 || nq <= 0 || heads <= 0 || group <= 0 || dim != dkv::kDim) return 0;
+  const dkv::AttnPlan p = dkv::make_plan(past, nq, heads, group);
+  return p.ws_o_bytes + p.ws_ml_bytes;
+}
+
+int dkv_packed_attention(const void* q, const void* knew, const void* vnew, const void* p4, const void* m4,
+                         const void* p8, const void* m8, const void* p16, const int32_t* rows,
+                         const uint8_t* codes, void* out, int64_t qh, int64_t qt, int64_t kh, int64_t kt,
+                         int64_t vh, int64_t vt, int32_t layer, int32_t past, int32_t nq, int64_t cap4,
+                         int64_t cap8, int64_t cap16, int32_t heads, int32_t group, int32_t dim,
+                         int32_t block_m, int32_t block_n, int32_t layers, void* workspace,
+                         size_t workspace_bytes, int32_t* status, void* stream) {
+  int rc = check_geometry(heads, dim, layers, layer);
+  if (rc) return rc;
+  if ((rc = check_pools(p4, m4, p8, m8, p16, cap4, cap8, cap16))) return rc;
+  if (group <= 0) return fail(DKV_EINVAL, "query heads must be a positive multiple of KV heads");
+  auto pow2 = [](int x) { return x >= 16 && x <= 256 && (x & (x - 1)) == 0; };
+  if (!pow2(block_m) || !pow2(block_n)) return fail(DKV_EINVAL, "block_m/block_n must be powers of two in [16, 256]");
+  if (past < 0 || nq < 0) return fail(DKV_EINVAL, "negative past or query length");
+  if (nq == 0) return ok();
+  if (past > 0 && (rows == nullptr || codes == nullptr)) return fail(DKV_EINVAL, "null token map");
+  if (!rows_aligned(q, qh, qt) || !rows_aligned(knew, kh, kt) || !rows_aligned(vnew, vh, vt))
+    return fail(DKV_EINVAL, "q/k/v rows must be 16-byte aligned (head/token strides multiples of 8)");
+  if (out == nullptr || !aligned16(out)) return fail(DKV_EINVAL, "out must be 16-byte aligned");
+  const dkv::AttnPlan p = dkv::make_plan(past, nq, heads, group);
+  const size_t need = p.ws_o_bytes + p.ws_ml_bytes;
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need || !aligned16(workspace)))
+    return fail(DKV_EWORKSPACE, "attention workspace needs %zu bytes, got %zu", need, workspace_bytes);
+  dkv::AttnArgs a{};
+  a.q = static_cast<const uint16_t*>(q);
+  a.knew = static_cast<const uint16_t*>(knew);
+  a.vnew = static_cast<const uint16_t*>(vnew);
+  a.P.p4 = static_cast<const uint8_t*>(p4);
+  a.P.m4 = static_cast<const float2*>(m4);
+  a.P.p8 = static_cast<const uint8_t*>(p8);
+  a.P.m8 = static_cast<const float2*>(m8);
+  a.P.p16 = static_cast<const uint16_t*>(p16);
+  a.P.cap4 = cap4;
+  a.P.cap8 = cap8;
+  a.P.cap16 = cap16;
+  a.P.heads = heads;
+  a.rows = rows;
+  a.codes = codes;
+  a.out = static_cast<uint16_t*>(out);
+  a.qh = qh; a.qt = qt; a.kh = kh; a.kt = kt; a.vh = vh; a.vt = vt;
+  a.layer = layer;
+  a.past = past;
+  a.nq = nq;
+  a.G = group;
+  a.HQ = heads * group;
+  a.mrows = p.mrows;
+  a.cta_rows = p.cta_rows;
+  a.mblocks = p.mblocks;
+  a.splits = p.splits;
+  a.chunk = p.chunk;
+  a.ws_o = static_cast<float*>(workspace);
+  a.ws_ml = need > 0 ? reinterpret_cast<float2*>(static_cast<uint8_t*>(workspace) + p.ws_o_bytes) : nullptr;
+  a.status = status;
+  return cuda_status(dkv::launch_attention_split(a, heads, static_cast<cudaStream_t>(stream)),
+                     "packed_attention launch");
+}
+
+int dkv_reconstruct(const void* p4, const void* m4, const void* p8, const void* m8, const void* p16,
+                    const int32_t* rows, const uint8_t* codes, void* out, int32_t layer, int32_t n,
+                    int64_t cap4, int64_t cap8, int64_t cap16, int32_t heads, int32_t dim, int32_t layers,
+                    int32_t* status, void* stream) {
+  int rc = check_geometry(heads, dim, layers, layer);
+  if (rc) return rc;
+  if ((rc = check_pools(p4, m4, p8, m8, p16, cap4, cap8, cap16))) return rc;
+  if (n < 0) return fail(DKV_EINVAL, "negative token count");
+  if (n == 0) return ok();
+  if (rows == nullptr || codes == nullptr) return fail(DKV_EINVAL, "null token map");
+  if (out == nullptr || !aligned16(out)) return fail(DKV_EINVAL, "out must be 16-byte aligned");
+  if (2LL * heads * n * 8 > INT32_MAX) return fail(DKV_EINVAL, "history too large");
+  dkv::Pools P{static_cast<const uint8_t*>(p4), static_cast<const float2*>(m4),
+               static_cast<const uint8_t*>(p8), static_cast<const float2*>(m8),
+               static_cast<const uint16_t*>(p16), cap4, cap8, cap16, heads};
+  return cuda_status(dkv::launch_reconstruct(P, rows, codes, out, layer, n, status,
+                                             static_cast<cudaStream_t>(stream)),
+                     "reconstruct launch");
+}
+
+int dkv_map_fill(int32_t* rows, uint8_t* codes, int64_t start, int32_t n, int64_t row, int32_t bits,
+                 int64_t capacity, void* stream) {
+  if (rows == nullptr || codes == nullptr) return fail(DKV_EINVAL, "null token map");
+  if (bits != 4 && bits != 8 && bits != 16) return fail(DKV_EINVAL, "Supported bit widths: 4, 8, 16");
+  if (n < 0 || start < 0 || row < 0) return fail(DKV_EINVAL, "negative map range");
+  if (start + n > capacity) return fail(DKV_ECAPACITY, "GPU context limit exceeded");
+  if (row + n > INT32_MAX) return fail(DKV_ECAPACITY, "pool row exceeds int32");
+  if (n == 0) return ok();
+  return cuda_status(dkv::launch_map_fill(rows, codes, start, n, row, bits, static_cast<cudaStream_t>(stream)),
+                     "map_fill launch");
+}
+
+}  // extern "C"

@@ -1,0 +1,243 @@
+"""Packed mixed-precision KV cache on the B200 kernels.
+
+Drop-in for the reference's src/gpu_cache.py: same class name, constructor
+keywords, methods, attributes and error messages (GPUCache, src/gpu_cache.py:
+10-149; install_packed_attention, :151-183). The pools keep the reference's
+physical layout and growth policy, so `caps`, `host_counts`, `plan`, the token
+maps `rows`/`codes` and `accounting()` read exactly as the reference's do. The
+Triton launches are replaced by the sm_100a kernels of libdkv.so (gpu_kernels),
+and the per-token map update is one device launch (map_fill).
+"""
+import types
+
+import torch
+import torch.nn.functional as F
+from transformers.cache_utils import DynamicCache
+
+from . import gpu_kernels as K
+
+BITS = (4, 8, 16)
+
+
+class GPUCache(DynamicCache):
+    def __init__(self, plan=None, layers=30, heads=3, dim=64, device='cuda', dtype=torch.bfloat16,
+                 backend='fused', block_m=16, block_n=64, max_tokens=8192):
+        super().__init__()
+        if dim != 64:
+            raise ValueError('GPU kernel currently supports head_dim=64')
+        if dtype != torch.bfloat16:
+            raise ValueError('GPU kernel stores 16-bit rows as bfloat16')
+        self.layers, self.heads, self.dim = layers, heads, dim
+        self.dtype, self.device = dtype, torch.device(device)
+        self.backend, self.block_m, self.block_n = backend, block_m, block_n
+        self.seen = [0] * layers
+        self.cursors = [0] * layers
+        self.pending_bits = 16
+        self.frame_id = -1
+        self.online = plan is None
+        rows, codes, counts = [], [], {4: 0, 8: 0, 16: 0}
+        self.plan = []
+        # Offline plan: segments (start, end, bits, first pool row), src/gpu_cache.py:23-29.
+        for bits, n in (plan or []):
+            if bits not in counts or n < 0:
+                raise ValueError('Invalid GPU cache plan')
+            self.plan.append((len(rows), len(rows) + n, bits, counts[bits]))
+            rows.extend(range(counts[bits], counts[bits] + n))
+            codes.extend([bits] * n)
+            counts[bits] += n
+        self.capacity = max_tokens if self.online else len(rows)
+        self.caps = {b: 64 if self.online else max(1, n) for b, n in counts.items()}
+        if self.online:
+            self.rows = torch.zeros(self.capacity, dtype=torch.int32, device=self.device)
+            self.codes = torch.zeros(self.capacity, dtype=torch.uint8, device=self.device)
+        else:
+            self.rows = torch.tensor(rows, dtype=torch.int32, device=self.device)
+            self.codes = torch.tensor(codes, dtype=torch.uint8, device=self.device)
+        common = (layers, 2, heads)
+        self.p4 = torch.empty((*common, self.caps[4], dim // 2), dtype=torch.uint8, device=self.device)
+        self.p8 = torch.empty((*common, self.caps[8], dim), dtype=torch.uint8, device=self.device)
+        self.p16 = torch.empty((*common, self.caps[16], dim), dtype=dtype, device=self.device)
+        self.m4 = torch.empty((*common, self.caps[4], 2), dtype=torch.float32, device=self.device)
+        self.m8 = torch.empty((*common, self.caps[8], 2), dtype=torch.float32, device=self.device)
+        self.host_counts = counts
+        # Device status word written by the kernels (first error code, detail index).
+        self.status = torch.zeros(4, dtype=torch.int32, device=self.device)
+
+    # -- capacity ---------------------------------------------------------------
+    def reserve(self, bits, needed):
+        """Grows pool `bits` to at least `needed` rows: max(needed, 1.5x rounded up
+        to 64), as src/gpu_cache.py:44-59, copying the old rows on the device."""
+        old = self.caps[bits]
+        if needed <= old:
+            return
+        cap = max(needed, ((int(old * 1.5) + 63) // 64) * 64)
+        common = (self.layers, 2, self.heads)
+        attr = {4: 'p4', 8: 'p8', 16: 'p16'}[bits]
+        source = getattr(self, attr)
+        target = torch.empty((*common, cap, self.dim // 2 if bits == 4 else self.dim),
+                             dtype=source.dtype, device=self.device)
+        target[:, :, :, :old].copy_(source)
+        setattr(self, attr, target)
+        if bits != 16:
+            attr = 'm4' if bits == 4 else 'm8'
+            source = getattr(self, attr)
+            target = torch.empty((*common, cap, 2), dtype=source.dtype, device=self.device)
+            target[:, :, :, :old].copy_(source)
+            setattr(self, attr, target)
+        self.caps[bits] = cap
+
+    def select(self, bits, frame_id=-1):
+        self.pending_bits, self.frame_id = bits, frame_id
+
+    def get_seq_length(self, layer_idx=0):
+        return self.seen[layer_idx]
+
+    def get_max_cache_shape(self, layer_idx=0):
+        return None
+
+    def __len__(self):
+        return self.layers
+
+    # -- hot path -----------------------------------------------------------------
+    def _pools(self):
+        return (self.p4, self.m4, self.p8, self.m8, self.p16)
+
+    def append(self, k, v, layer):
+        """Packs one frame's K/V for `layer`; returns the history length before it
+        (src/gpu_cache.py:68-94)."""
+        if k.shape[0] != 1 or k.shape[-1] != self.dim or k.device.type != 'cuda':
+            raise ValueError('GPU cache requires CUDA, batch one and the configured head dimension')
+        past, n = self.seen[layer], k.shape[-2]
+        if past + n > self.capacity:
+            raise ValueError('GPU context limit exceeded')
+        if self.online:
+            if layer == 0:
+                row = self.host_counts[self.pending_bits]
+                self.reserve(self.pending_bits, row + n)
+                self.plan.append((past, past + n, self.pending_bits, row))
+                self.host_counts[self.pending_bits] += n
+                K.map_fill(self.rows, self.codes, past, n, row, self.pending_bits, self.capacity)
+            segment = self.plan[-1]
+        else:
+            cursor = self.cursors[layer]
+            while cursor < len(self.plan) and past >= self.plan[cursor][1]:
+                cursor += 1
+            self.cursors[layer] = cursor
+            segment = self.plan[cursor] if cursor < len(self.plan) else None
+        if segment is None or past + n > segment[1] or segment[2] != self.pending_bits:
+            raise ValueError(f'Cache append does not match plan at token {past}, length {n}, '
+                             f'bits {self.pending_bits}')
+        row = segment[3] + past - segment[0]
+        K.pack_rows(k, v, *self._pools(), layer, row, n, self.caps[4], self.caps[8], self.caps[16],
+                    self.heads, self.dim, self.pending_bits, self.layers, self.status)
+        self.seen[layer] = past + n
+        return past
+
+    def attend(self, q, k, v, layer, past):
+        """Causal GQA attention of the n new queries over the packed history plus
+        the native new K/V; returns [1, n, query_heads, dim] (src/gpu_cache.py:96-104)."""
+        n = q.shape[-2]
+        out = torch.empty((1, n, q.shape[1], self.dim), dtype=q.dtype, device=q.device)
+        K.packed_attention(q, k, v, *self._pools(), self.rows, self.codes, out, layer, past, n,
+                           self.caps[4], self.caps[8], self.caps[16], self.heads, q.shape[1] // self.heads,
+                           self.dim, self.block_m, self.block_n, self.layers, self.status)
+        return out
+
+    def materialize(self, layer):
+        """Dequantised bf16 history (k, v), each [1, heads, seen, dim] (src/gpu_cache.py:106-112)."""
+        n = self.seen[layer]
+        out = torch.empty((2, self.heads, n, self.dim), dtype=self.dtype, device=self.device)
+        K.reconstruct(*self._pools(), self.rows, self.codes, out, layer, n, self.caps[4], self.caps[8],
+                      self.caps[16], self.heads, self.dim, self.layers, self.status)
+        return out[0:1], out[1:2]
+
+    def update(self, key_states, value_states, layer_idx, cache_kwargs=None):
+        """HF Cache.update contract used by the sdpa backend (src/gpu_cache.py:114-119)."""
+        self.append(key_states, value_states, layer_idx)
+        k, v = self.materialize(layer_idx)
+        k[:, :, -key_states.shape[-2]:].copy_(key_states)
+        v[:, :, -value_states.shape[-2]:].copy_(value_states)
+        return k, v
+
+    def fork(self):
+        """QA branch sharing the pools and maps; host bookkeeping is copied, so a
+        branch's appends and growth never move the base (src/gpu_cache.py:121-132).
+        Branches overwrite the same reserved rows and must run one after another
+        on one stream."""
+        other = object.__new__(GPUCache)
+        other.__dict__ = self.__dict__.copy()
+        other.seen = self.seen.copy()
+        other.cursors = self.cursors.copy()
+        other.plan = self.plan.copy()
+        other.host_counts = self.host_counts.copy()
+        other.caps = self.caps.copy()
+        other.pending_bits = 16
+        return other
+
+    def check(self):
+        """Synchronises and raises ValueError if a kernel flagged an error (a
+        non-finite pack input or a corrupt token map). Not in the reference,
+        whose kernels have no device-side checks."""
+        K.raise_for_status(self.status)
+
+    def accounting(self):
+        """Used/allocated bytes with the reference's formulas (src/gpu_cache.py:134-149)."""
+        tensors = [self.p4, self.p8, self.p16, self.m4, self.m8, self.rows, self.codes]
+        allocated = sum(t.numel() * t.element_size() for t in tensors)
+        used = {4: 0, 8: 0, 16: 0}
+        n = self.seen[0]
+        for start, end, bits, row in self.plan:
+            used[bits] += max(0, min(n, end) - start)
+        payload = self.layers * 2 * self.heads * self.dim * sum(used[b] * b / 8 for b in used)
+        scales = self.layers * 2 * self.heads * 8 * (used[4] + used[8])
+        mapping = n * 5
+        return dict(gpu_cache_used_bytes=int(payload + scales + mapping),
+                    gpu_cache_allocated_bytes=allocated, cpu_cache_payload_bytes=0,
+                    payload_bytes=int(payload), quantization_metadata_bytes=int(scales),
+                    token_mapping_bytes=mapping, logical_index_capacity=self.capacity,
+                    precision_pool_capacities=self.caps,
+                    used_tokens=n, precision_token_counts=used)
+
+
+def install_packed_attention(model):
+    """Routes GPUCache through the fused kernels in every LlamaAttention of `model`;
+    other caches keep the upstream forward (src/gpu_cache.py:151-183)."""
+    def forward(module, hidden_states, position_embeddings, attention_mask=None,
+                past_key_value=None, cache_position=None, **kwargs):
+        cache = past_key_value if past_key_value is not None else kwargs.get('past_key_values')
+        fused = isinstance(cache, GPUCache) and cache.backend == 'fused'
+        fast_gqa = getattr(cache, 'fast_gqa', False)
+        if not fused and not fast_gqa:
+            if past_key_value is not None:
+                kwargs['past_key_value'] = past_key_value
+            return module._original_forward(hidden_states=hidden_states,
+                                            position_embeddings=position_embeddings,
+                                            attention_mask=attention_mask,
+                                            cache_position=cache_position, **kwargs)
+        if kwargs.get('output_attentions', False):
+            raise ValueError('Fused packed attention does not expose attention matrices')
+        from transformers.models.llama.modeling_llama import apply_rotary_pos_emb
+        shape = hidden_states.shape[:-1]
+        if fused and hasattr(module, '_qkv_weight'):
+            q, k, v = F.linear(hidden_states, module._qkv_weight).split(module._qkv_sizes, dim=-1)
+        else:
+            q, k, v = module.q_proj(hidden_states), module.k_proj(hidden_states), module.v_proj(hidden_states)
+        q = q.view(*shape, -1, module.head_dim).transpose(1, 2)
+        k = k.view(*shape, -1, module.head_dim).transpose(1, 2)
+        v = v.view(*shape, -1, module.head_dim).transpose(1, 2)
+        q, k = apply_rotary_pos_emb(q, k, *position_embeddings)
+        if fused:
+            past = cache.append(k, v, module.layer_idx)
+            output = cache.attend(q, k, v, module.layer_idx, past)
+        else:
+            k, v = cache.update(k, v, module.layer_idx, {'cache_position': cache_position})
+            mask = None if attention_mask is None else attention_mask[:, :, :, :k.shape[-2]]
+            output = F.scaled_dot_product_attention(
+                q, k, v, attn_mask=mask, dropout_p=0, is_causal=mask is None and q.shape[-2] > 1,
+                scale=module.scaling, enable_gqa=True).transpose(1, 2)
+        return module.o_proj(output.reshape(*shape, -1).contiguous()), None
+
+    for module in model.modules():
+        if module.__class__.__name__ == 'LlamaAttention' and not hasattr(module, '_original_forward'):
+            module._original_forward = module.forward
+            module.forward = types.MethodType(forward, module)

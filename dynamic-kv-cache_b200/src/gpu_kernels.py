@@ -1,0 +1,130 @@
+"""Host bindings of the sm_100a kernels (libdkv.so, C ABI in include/dkv.h).
+
+Replaces the reference's Triton module src/gpu_kernels.py. The four launch
+functions keep the Triton kernels' names and argument meaning:
+
+  pack_rows         <- src/gpu_kernels.py:11-46
+  packed_attention  <- src/gpu_kernels.py:71-105 (load_history :48-69 is fused in)
+  reconstruct       <- src/gpu_kernels.py:107-119
+  map_fill          <- the two map writes at src/gpu_cache.py:79-80
+
+Each takes torch tensors, passes raw device pointers, element strides and the
+current CUDA stream through ctypes, and raises ValueError (argument errors, the
+reference's exception type) or RuntimeError (CUDA errors) on a non-zero status.
+There is no fallback: importing this module without the built library raises.
+"""
+import ctypes
+from pathlib import Path
+
+import torch
+
+_LIB_PATH = Path(__file__).resolve().parent.parent / 'libdkv.so'
+
+DKV_OK, DKV_EINVAL, DKV_ECAPACITY, DKV_EPLAN, DKV_ECUDA, DKV_ENONFINITE, DKV_EWORKSPACE = range(7)
+STATUS_NAMES = {DKV_EINVAL: 'invalid argument', DKV_ECAPACITY: 'capacity exceeded',
+                DKV_EPLAN: 'bad precision code in token map', DKV_ECUDA: 'CUDA error',
+                DKV_ENONFINITE: 'Nonfinite KV tensor', DKV_EWORKSPACE: 'workspace too small'}
+
+
+def _load():
+    if not _LIB_PATH.exists():
+        raise ImportError(f'{_LIB_PATH} is not built; run `python __graft_entry__.py build` '
+                          '(or dynamic-kv-cache_b200/build.py) first. There is no CPU fallback.')
+    lib = ctypes.CDLL(str(_LIB_PATH))
+    P, I32, I64, SZ = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_size_t
+    sigs = {
+        'dkv_version': ([], I32),
+        'dkv_last_error': ([], ctypes.c_char_p),
+        'dkv_pack_rows': ([P, P, P, P, P, P, P, I64, I64, I64, I64, I32, I64, I32, I64, I64, I64,
+                           I32, I32, I32, I32, P, P], ctypes.c_int),
+        'dkv_packed_attention': ([P, P, P, P, P, P, P, P, P, P, P, I64, I64, I64, I64, I64, I64,
+                                  I32, I32, I32, I64, I64, I64, I32, I32, I32, I32, I32, I32,
+                                  P, SZ, P, P], ctypes.c_int),
+        'dkv_packed_attention_workspace': ([I32, I32, I32, I32, I32], SZ),
+        'dkv_reconstruct': ([P, P, P, P, P, P, P, P, I32, I32, I64, I64, I64, I32, I32, I32, P, P],
+                            ctypes.c_int),
+        'dkv_map_fill': ([P, P, I64, I32, I64, I32, I64, P], ctypes.c_int),
+    }
+    for name, (args, res) in sigs.items():
+        fn = getattr(lib, name)
+        fn.argtypes, fn.restype = args, res
+    return lib
+
+
+LIB = _load()
+EXPORTS = ('dkv_version', 'dkv_last_error', 'dkv_pack_rows', 'dkv_packed_attention',
+           'dkv_packed_attention_workspace', 'dkv_reconstruct', 'dkv_map_fill')
+
+
+def _check(rc):
+    if rc == DKV_OK:
+        return
+    message = LIB.dkv_last_error().decode() or STATUS_NAMES.get(rc, f'status {rc}')
+    if rc == DKV_ECUDA:
+        raise RuntimeError(message)
+    raise ValueError(message)
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _stream(t):
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _rows_ready(x):
+    """bf16 [1, heads, n, 64] view whose rows the kernels can load 16 bytes at a time."""
+    if x.dtype != torch.bfloat16:
+        raise ValueError('GPU kernels take bfloat16 queries, keys and values')
+    ok = (x.stride(-1) == 1 and x.stride(1) % 8 == 0 and x.stride(2) % 8 == 0
+          and x.data_ptr() % 16 == 0)
+    return x if ok else x.contiguous()
+
+
+def pack_rows(k, v, p4, m4, p8, m8, p16, layer, row_start, n, cap4, cap8, cap16, heads, dim, bits,
+              layers, status=None):
+    k, v = _rows_ready(k), _rows_ready(v)
+    _check(LIB.dkv_pack_rows(_ptr(k), _ptr(v), _ptr(p4), _ptr(m4), _ptr(p8), _ptr(m8), _ptr(p16),
+                             k.stride(1), k.stride(2), v.stride(1), v.stride(2), layer, row_start, n,
+                             cap4, cap8, cap16, heads, dim, bits, layers, _ptr(status), _stream(k)))
+
+
+def attention_workspace_bytes(past, nq, heads, group, dim=64):
+    return LIB.dkv_packed_attention_workspace(past, nq, heads, group, dim)
+
+
+def packed_attention(q, knew, vnew, p4, m4, p8, m8, p16, rows, codes, out, layer, past, nq, cap4, cap8,
+                     cap16, heads, group, dim, block_m, block_n, layers, status=None):
+    q, knew, vnew = _rows_ready(q), _rows_ready(knew), _rows_ready(vnew)
+    size = attention_workspace_bytes(past, nq, heads, group, dim)
+    workspace = torch.empty(size, dtype=torch.uint8, device=q.device) if size else None
+    _check(LIB.dkv_packed_attention(
+        _ptr(q), _ptr(knew), _ptr(vnew), _ptr(p4), _ptr(m4), _ptr(p8), _ptr(m8), _ptr(p16), _ptr(rows),
+        _ptr(codes), _ptr(out), q.stride(1), q.stride(2), knew.stride(1), knew.stride(2),
+        vnew.stride(1), vnew.stride(2), layer, past, nq, cap4, cap8, cap16, heads, group, dim,
+        block_m, block_n, layers, _ptr(workspace), size, _ptr(status), _stream(q)))
+    return out
+
+
+def reconstruct(p4, m4, p8, m8, p16, rows, codes, out, layer, n, cap4, cap8, cap16, heads, dim, layers,
+                status=None):
+    _check(LIB.dkv_reconstruct(_ptr(p4), _ptr(m4), _ptr(p8), _ptr(m8), _ptr(p16), _ptr(rows), _ptr(codes),
+                               _ptr(out), layer, n, cap4, cap8, cap16, heads, dim, layers, _ptr(status),
+                               _stream(out)))
+    return out
+
+
+def map_fill(rows, codes, start, n, row, bits, capacity):
+    _check(LIB.dkv_map_fill(_ptr(rows), _ptr(codes), start, n, row, bits, capacity, _stream(rows)))
+
+
+def raise_for_status(status):
+    """Reads a device status word (synchronises) and raises if a kernel reported an error."""
+    code, detail = (int(x) for x in status[:2].tolist())
+    if code == DKV_OK:
+        return
+    status.zero_()
+    if code == DKV_ENONFINITE:
+        raise ValueError('Nonfinite KV tensor')
+    raise ValueError(f'{STATUS_NAMES.get(code, f"status {code}")} (index {detail})')

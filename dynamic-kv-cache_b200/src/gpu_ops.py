@@ -1,0 +1,66 @@
+"""Decoder-side engine ops kept from the reference's src/gpu_ops.py.
+
+The reference joins the QKV and gate/up projection weights into single GEMMs
+and runs RMSNorm / SiLU*up as prebuilt PyTorch CUDA ops (src/gpu_ops.py:9-48).
+These are library GEMMs and pointwise ops, not part of the packed-KV kernels,
+so they stay on PyTorch here too; the API and the weight-joining invariants
+(bit-identical parameter views over one joined tensor) are the same.
+"""
+import types
+
+import torch
+
+
+def cuda_rms(x, weight, eps):
+    """RMSNorm with the bf16 rounding before the weight multiply (src/gpu_ops.py:9-12)."""
+    return torch.nn.functional.rms_norm(x, (x.shape[-1],), None, eps) * weight
+
+
+def activation_product(gate, up):
+    """silu(gate) * up (src/gpu_ops.py:14-17)."""
+    return torch.nn.functional.silu(gate) * up
+
+
+def join_weights(modules):
+    """Concatenates the weights of `modules` along dim 0 and re-points each module's
+    weight at its slice of the joined tensor, so no second copy is kept and every
+    projection stays bit-identical (src/gpu_ops.py:26-37)."""
+    with torch.no_grad():
+        joined = torch.cat([m.weight for m in modules], dim=0)
+        offset = 0
+        for m in modules:
+            n = m.weight.shape[0]
+            view = joined[offset:offset + n]
+            if not torch.equal(view, m.weight):
+                raise AssertionError('Projection values changed during packing')
+            m.weight = torch.nn.Parameter(view, requires_grad=False)
+            offset += n
+    return joined
+
+
+def install_fused_ops(text, state):
+    """Patches LlamaRMSNorm / LlamaMLP forwards and joins projection weights of an
+    HF Llama text model; `state['enabled']` switches the fused forms on
+    (src/gpu_ops.py:19-48)."""
+    def rms_forward(module, x):
+        return cuda_rms(x, module.weight, module.variance_epsilon) if state['enabled'] else module._original_rms(x)
+
+    def mlp_forward(module, x):
+        if not state['enabled']:
+            return module._original_mlp(x)
+        gate, up = torch.nn.functional.linear(x, module._gate_up_weight).chunk(2, dim=-1)
+        return module.down_proj(activation_product(gate, up))
+
+    for module in text.modules():
+        name = module.__class__.__name__
+        if name == 'LlamaAttention' and all(m.bias is None for m in [module.q_proj, module.k_proj, module.v_proj]):
+            module._qkv_weight = join_weights([module.q_proj, module.k_proj, module.v_proj])
+            module._qkv_sizes = [module.q_proj.out_features, module.k_proj.out_features,
+                                 module.v_proj.out_features]
+        elif name == 'LlamaRMSNorm':
+            module._original_rms = module.forward
+            module.forward = types.MethodType(rms_forward, module)
+        elif name == 'LlamaMLP' and text.config.hidden_act == 'silu':
+            module._gate_up_weight = join_weights([module.gate_proj, module.up_proj])
+            module._original_mlp = module.forward
+            module.forward = types.MethodType(mlp_forward, module)

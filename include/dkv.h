@@ -1,0 +1,135 @@
+/*
+ * dkv.h — C-ABI of the B200 (sm_100a) packed mixed-precision KV-cache library
+ * (libdkv.so).
+ *
+ * The entry points replace the three Triton kernels of the reference's packed-KV
+ * hot path (zoaibs/Dynamic-KV-Cache, src/gpu_kernels.py) plus the two device-side
+ * bookkeeping writes of its cache object (src/gpu_cache.py:79-80). Argument lists
+ * follow the Triton launch signatures, in the same order, with three additions:
+ * the layer count (for bounds checks), a device status word and the CUDA stream.
+ *
+ * Conventions
+ *  - Every pointer is a device pointer unless stated; nothing is freed or retained.
+ *  - Strides are in ELEMENTS (bf16), exactly as torch's Tensor.stride() reports
+ *    them; the innermost (head_dim) stride must be 1.
+ *  - bf16 tensors are passed as void*; pools use the reference's physical layout:
+ *      p4  uint8 [layers, 2, heads, cap4, dim/2]   two 4-bit codes per byte, lo = even
+ *      m4  f32   [layers, 2, heads, cap4, 2]       (offset, scale) per row
+ *      p8  uint8 [layers, 2, heads, cap8, dim]
+ *      m8  f32   [layers, 2, heads, cap8, 2]
+ *      p16 bf16  [layers, 2, heads, cap16, dim]
+ *    (index 1 selects K = 0 or V = 1), and the token maps
+ *      rows  int32 [capacity]  pool row of logical token t
+ *      codes uint8 [capacity]  storage bits of logical token t (4, 8 or 16)
+ *  - `stream` is a cudaStream_t (NULL = legacy default stream). All work is
+ *    asynchronous on it; no entry point synchronises.
+ *  - Return value: DKV_OK or a DKV_E* code; dkv_last_error() gives the message
+ *    (per host thread). Host-side argument errors launch nothing.
+ *  - `status` (may be NULL) is an int32[4] device word: the first device-detected
+ *    error stores its DKV_E* code in status[0] and a detail index in status[1]
+ *    (kernels never trap; the offending access is skipped). The caller reads it
+ *    after a synchronisation and clears it.
+ *  - head_dim must be 64 (the reference raises the same restriction,
+ *    src/gpu_cache.py:14).
+ */
+#ifndef DKV_H
+#define DKV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DKV_VERSION 1
+
+enum dkv_status {
+  DKV_OK = 0,
+  DKV_EINVAL = 1,     /* bad argument (shape, stride, alignment, bits)            */
+  DKV_ECAPACITY = 2,  /* row or token outside a pool / map capacity               */
+  DKV_EPLAN = 3,      /* token map holds a code other than 4, 8 or 16             */
+  DKV_ECUDA = 4,      /* a CUDA runtime call or launch failed                     */
+  DKV_ENONFINITE = 5, /* pack input held NaN or Inf                               */
+  DKV_EWORKSPACE = 6  /* workspace smaller than dkv_packed_attention_workspace()  */
+};
+
+/* Library version (DKV_VERSION). */
+int32_t dkv_version(void);
+
+/* Message of the last error returned on this host thread ("" if none). */
+const char* dkv_last_error(void);
+
+/*
+ * Pack one frame of K and V for one layer into the pools at rows
+ * [row_start, row_start + n) of the `bits` pool (4, 8 or 16).
+ * Replaces Triton `pack_rows` (src/gpu_kernels.py:11-46), launched by
+ * GPUCache.append (src/gpu_cache.py:90-92). k, v: bf16 [1, heads, n, dim] with
+ * head/token strides (kh, kt) and (vh, vt). 4/8-bit rows use per-row min/max
+ * affine quantisation with IEEE fp32 arithmetic, bit-identical to the reference
+ * CPU quantiser src/kv_quantization.py:57-71 (group = one 64-wide row).
+ */
+int dkv_pack_rows(const void* k, const void* v,
+                  void* p4, void* m4, void* p8, void* m8, void* p16,
+                  int64_t kh, int64_t kt, int64_t vh, int64_t vt,
+                  int32_t layer, int64_t row_start, int32_t n,
+                  int64_t cap4, int64_t cap8, int64_t cap16,
+                  int32_t heads, int32_t dim, int32_t bits,
+                  int32_t layers, int32_t* status, void* stream);
+
+/*
+ * Causal GQA attention of nq new queries over `past` packed history tokens plus
+ * the nq native new K/V rows. Replaces Triton `packed_attention`
+ * (src/gpu_kernels.py:71-105), launched by GPUCache.attend
+ * (src/gpu_cache.py:96-104). q: bf16 [1, heads*group, nq, dim] with strides
+ * (qh, qt); knew/vnew: bf16 [1, heads, nq, dim]; out: bf16 [1, nq, heads*group,
+ * dim] contiguous. Query m sees keys t <= past + m. block_m / block_n are the
+ * reference's tile knobs: validated (powers of two, 16..256) but the kernel picks
+ * its own B200 tiling. `workspace` must hold dkv_packed_attention_workspace()
+ * bytes (it may be NULL when that size is 0).
+ */
+int dkv_packed_attention(const void* q, const void* knew, const void* vnew,
+                         const void* p4, const void* m4, const void* p8,
+                         const void* m8, const void* p16,
+                         const int32_t* rows, const uint8_t* codes, void* out,
+                         int64_t qh, int64_t qt, int64_t kh, int64_t kt,
+                         int64_t vh, int64_t vt,
+                         int32_t layer, int32_t past, int32_t nq,
+                         int64_t cap4, int64_t cap8, int64_t cap16,
+                         int32_t heads, int32_t group, int32_t dim,
+                         int32_t block_m, int32_t block_n,
+                         int32_t layers, void* workspace, size_t workspace_bytes,
+                         int32_t* status, void* stream);
+
+/* Workspace bytes dkv_packed_attention needs for this shape (0 = none). */
+size_t dkv_packed_attention_workspace(int32_t past, int32_t nq, int32_t heads,
+                                      int32_t group, int32_t dim);
+
+/*
+ * Dequantised bf16 history of one layer: out[2, heads, n, dim] (K then V) for
+ * logical tokens [0, n). Replaces Triton `reconstruct` (src/gpu_kernels.py:
+ * 107-119), launched by GPUCache.materialize (src/gpu_cache.py:106-112).
+ * x = bf16(fp32(code * scale) + offset), the operation order of the reference
+ * CPU unpack (src/kv_quantization.py:91).
+ */
+int dkv_reconstruct(const void* p4, const void* m4, const void* p8,
+                    const void* m8, const void* p16,
+                    const int32_t* rows, const uint8_t* codes, void* out,
+                    int32_t layer, int32_t n,
+                    int64_t cap4, int64_t cap8, int64_t cap16,
+                    int32_t heads, int32_t dim, int32_t layers,
+                    int32_t* status, void* stream);
+
+/*
+ * Device-resident token-map update for one appended segment:
+ * rows[start + i] = row + i and codes[start + i] = bits for i in [0, n).
+ * Replaces the two tensor writes at src/gpu_cache.py:79-80 with one launch.
+ */
+int dkv_map_fill(int32_t* rows, uint8_t* codes, int64_t start, int32_t n,
+                 int64_t row, int32_t bits, int64_t capacity, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DKV_H */

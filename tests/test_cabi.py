@@ -1,0 +1,69 @@
+"""CPU checks of the C ABI: the library loads, exports every symbol include/dkv.h
+declares, and rejects bad arguments on the host before any launch."""
+import ctypes
+import re
+
+import pytest
+
+from conftest import ROOT
+
+HEADER = (ROOT / 'include' / 'dkv.h').read_text()
+DECLARED = sorted(set(re.findall(r'^\s*(?:[\w\s\*]+?)\b(dkv_\w+)\s*\(', HEADER, re.M)))
+
+
+def test_header_declares_the_hot_path_entry_points():
+    for name in ('dkv_pack_rows', 'dkv_packed_attention', 'dkv_reconstruct', 'dkv_map_fill',
+                 'dkv_packed_attention_workspace', 'dkv_last_error', 'dkv_version'):
+        assert name in DECLARED
+
+
+def test_library_exports_every_declared_symbol():
+    from src import gpu_kernels as K
+    raw = ctypes.CDLL(str(K._LIB_PATH))
+    missing = [name for name in DECLARED if not hasattr(raw, name)]
+    assert not missing, missing
+    assert set(K.EXPORTS) <= set(DECLARED)
+    assert K.LIB.dkv_version() == int(re.search(r'#define DKV_VERSION (\d+)', HEADER).group(1))
+
+
+def _pack_args(**over):
+    # Fake but 16-byte aligned "device" addresses: every call below fails in host
+    # validation, before anything is dereferenced or launched.
+    a = dict(k=0x1000, v=0x2000, p4=0x3000, m4=0x4000, p8=0x5000, m8=0x6000, p16=0x7000, kh=64 * 19,
+             kt=64, vh=64 * 19, vt=64, layer=0, row_start=0, n=19, cap4=64, cap8=64, cap16=64, heads=3,
+             dim=64, bits=4, layers=1, status=None, stream=None)
+    a.update(over)
+    return list(a.values())
+
+
+@pytest.mark.parametrize('over,code,text', [
+    (dict(dim=32), 1, 'head_dim=64'),
+    (dict(bits=5), 1, 'bit widths'),
+    (dict(layer=1), 1, 'layer'),
+    (dict(row_start=50), 2, 'capacity'),
+    (dict(kt=63), 1, 'aligned'),
+    (dict(p8=None), 1, 'null pool'),
+])
+def test_pack_rejects_bad_arguments_on_host(over, code, text):
+    from src import gpu_kernels as K
+    rc = K.LIB.dkv_pack_rows(*_pack_args(**over))
+    assert rc == code
+    assert text in K.LIB.dkv_last_error().decode()
+
+
+def test_attention_argument_checks_and_workspace_size():
+    from src import gpu_kernels as K
+    base = [0x1000] * 11 + [64 * 16, 64, 64 * 16, 64, 64 * 16, 64, 0, 128, 16, 64, 64, 64, 5, 3, 64]
+    rc = K.LIB.dkv_packed_attention(*base, 16, 48, 1, None, 0, None, None)  # block_m=16, block_n=48
+    assert rc == K.DKV_EINVAL and 'power' in K.LIB.dkv_last_error().decode()
+    rc = K.LIB.dkv_packed_attention(*base, 16, 64, 1, None, 0, None, None)
+    need = K.attention_workspace_bytes(128, 16, 5, 3)
+    assert need > 0 and rc == K.DKV_EWORKSPACE
+    assert K.attention_workspace_bytes(0, 1, 5, 3) == 0  # a single split needs no workspace
+    assert K.attention_workspace_bytes(8128, 64, 5, 3) < 64 << 20
+
+
+def test_map_fill_capacity_is_the_reference_context_limit_message():
+    from src import gpu_kernels as K
+    rc = K.LIB.dkv_map_fill(0x1000, 0x2000, 8190, 64, 0, 16, 8192, None)
+    assert rc == K.DKV_ECAPACITY and K.LIB.dkv_last_error().decode() == 'GPU context limit exceeded'

@@ -1,0 +1,230 @@
+"""GPU parity of the packed attention kernel against (1) golden outputs of the
+reference's own Triton kernel, (2) the CPU oracle (dequantise + SDPA) at the
+BASELINE shapes up to 8K context, and (3) the reference's own GPU tests."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN
+from dkv_testlib import assert_attention_close, frame_mix, oracle_attention, oracle_frames, outlier_kv
+from oracle import kvq
+
+pytestmark = pytest.mark.gpu
+ATTN_CASES = sorted(p.stem[len('attn_'):] for p in GOLDEN.glob('attn_*.npz'))
+
+
+def bf16_gpu(bits16):
+    return torch.from_numpy(np.ascontiguousarray(bits16).astype(np.int16)).view(torch.bfloat16).cuda()
+
+
+def build_cache(hist_k, hist_v, plan, nq, layers=1, layer=0, heads=5, online=True, **kw):
+    from src.gpu_cache import GPUCache
+    if online:
+        c = GPUCache(None, layers=layers, heads=heads, **kw)
+    else:
+        c = GPUCache(list(plan) + [(16, nq)], layers=layers, heads=heads, **kw)
+    start = 0
+    for f, (bits, n) in enumerate(plan):
+        c.select(bits, f)
+        for lay in range(layers) if online else [layer]:
+            c.append(hist_k[:, :, start:start + n], hist_v[:, :, start:start + n], lay)
+        start += n
+    return c
+
+
+@pytest.mark.parametrize('case', ATTN_CASES)
+def test_attention_matches_reference_triton_golden(cuda, case):
+    g = np.load(GOLDEN / f'attn_{case}.npz')
+    heads, group, nq, layers, layer = (int(g[k]) for k in ('heads', 'group', 'nq', 'layers', 'layer'))
+    plan = list(zip(g['frame_bits'].tolist(), g['frame_tokens'].tolist()))
+    hist_k = bf16_gpu(g['hist_k']) if plan else None
+    hist_v = bf16_gpu(g['hist_v']) if plan else None
+    c = build_cache(hist_k, hist_v, plan, nq, layers=layers, layer=layer, heads=heads, online=False)
+    q, kn, vn = bf16_gpu(g['q']), bf16_gpu(g['knew']), bf16_gpu(g['vnew'])
+    c.select(16)
+    past = c.append(kn, vn, layer)
+    assert past == sum(n for _, n in plan)
+    out = c.attend(q, kn, vn, layer, past)
+    c.check()
+    assert out.shape == (1, nq, heads * group, 64) and out.dtype == torch.bfloat16
+    # golden is the reference kernel in fp32; ours rounds history and p to bf16
+    assert_attention_close(out, torch.from_numpy(g['out']))
+    if 'recon' in g.files:
+        mk, mv = c.materialize(layer)
+        recon = torch.from_numpy(g['recon'])
+        assert torch.allclose(torch.stack([mk[0], mv[0]]).float().cpu(), recon.bfloat16().float(),
+                              atol=0, rtol=2 ** -8)
+
+
+@pytest.mark.parametrize('past', [1024, 4096, 8128])
+def test_frame_append_attention_c3_vs_oracle(cuda, past):
+    """15Q/5KV, 64-token append after `past` packed tokens with a
+    seeded 50/30/20 int4/int8/bf16 frame mix."""
+    gen = torch.Generator().manual_seed(past)
+    outliers = torch.randperm(64, generator=gen)[:4]
+    frames = (past + 63) // 64
+    plan = [(b, 64) for b in frame_mix(past, frames)]
+    plan[-1] = (plan[-1][0], past - 64 * (frames - 1))
+    hist_k, hist_v = outlier_kv(gen, 5, past, outliers)
+    c = build_cache(hist_k.cuda(), hist_v.cuda(), plan, 64)
+    q = torch.randn(1, 15, 64, 64, generator=gen).bfloat16()
+    kn, vn = outlier_kv(gen, 5, 64, outliers)
+    c.select(16)
+    p = c.append(kn.cuda(), vn.cuda(), 0)
+    out = c.attend(q.cuda(), kn.cuda(), vn.cuda(), 0, p)
+    c.check()
+    expected = oracle_attention(oracle_frames(hist_k, hist_v, plan), q, kn, vn)
+    assert_attention_close(out, expected, atol=0.01, rtol=0.01)
+    again = c.attend(q.cuda(), kn.cuda(), vn.cuda(), 0, p)
+    assert torch.equal(out, again)  # fixed split order: bit-identical reruns
+
+
+@pytest.mark.parametrize('nq', [1, 2, 5, 7, 19, 56, 64, 65, 77, 130])
+def test_query_lengths_vs_oracle(cuda, nq):
+    gen = torch.Generator().manual_seed(1000 + nq)
+    outliers = torch.randperm(64, generator=gen)[:4]
+    plan = [(4, 100), (16, 37), (8, 64), (4, 3)]
+    past = sum(n for _, n in plan)
+    hist_k, hist_v = outlier_kv(gen, 5, past, outliers)
+    c = build_cache(hist_k.cuda(), hist_v.cuda(), plan, nq, layers=2)
+    q = torch.randn(1, 15, nq, 64, generator=gen).bfloat16()
+    kn, vn = outlier_kv(gen, 5, nq, outliers)
+    c.select(16)
+    for layer in (0, 1):
+        p = c.append(kn.cuda(), vn.cuda(), layer)
+    out = c.attend(q.cuda(), kn.cuda(), vn.cuda(), 1, p)
+    c.check()
+    expected = oracle_attention(oracle_frames(hist_k, hist_v, plan), q, kn, vn)
+    assert_attention_close(out, expected, atol=0.01, rtol=0.01)
+
+
+@pytest.mark.parametrize('query_length', [1, 77])
+def test_reference_mixed_attention_five_kv_heads_and_long_history(cuda, query_length):
+    # tests/test_gpu_backend.py:82-101 of the reference, same seed and tolerance
+    from src.gpu_cache import GPUCache
+    torch.manual_seed(97)
+    c = GPUCache(None, layers=1, heads=5, max_tokens=2048)
+    for bits, n in [(4, 501), (8, 498)]:
+        k = torch.randn(1, 5, n, 64, device='cuda', dtype=torch.bfloat16)
+        v = torch.randn(1, n, 5, 64, device='cuda', dtype=torch.bfloat16).transpose(1, 2)
+        c.select(bits)
+        c.append(k, v, 0)
+    history_k, history_v = c.materialize(0)
+    n = query_length
+    q = torch.randn(1, 15, n, 64, device='cuda', dtype=torch.bfloat16)
+    k = torch.randn(1, 5, n, 64, device='cuda', dtype=torch.bfloat16)
+    v = torch.randn(1, n, 5, 64, device='cuda', dtype=torch.bfloat16).transpose(1, 2)
+    c.select(16)
+    past = c.append(k, v, 0)
+    actual = c.attend(q, k, v, 0, past)
+    full_k = torch.cat((history_k, k), 2).repeat_interleave(3, 1)
+    full_v = torch.cat((history_v, v), 2).repeat_interleave(3, 1)
+    mask = torch.arange(past + n, device='cuda')[None, :] <= past + torch.arange(n, device='cuda')[:, None]
+    expected = torch.nn.functional.scaled_dot_product_attention(q, full_k, full_v, attn_mask=mask).transpose(1, 2)
+    assert torch.allclose(actual.float(), expected.float(), atol=.035, rtol=.015)
+
+
+@pytest.mark.parametrize('bits_list', [[16, 16, 16], [4, 8, 16], [8, 4, 8]])
+def test_reference_script_mixed_plans(cuda, bits_list):
+    # scripts/test_gpu_backend.py:12-39 of the reference: 9Q/3KV, lengths 15/67/23
+    from src.gpu_cache import GPUCache
+    torch.manual_seed(12)
+    lengths = [15, 67, 23]
+    cache = GPUCache(list(zip(bits_list, lengths)), layers=1)
+    full_k, full_v = [], []
+    for bits, n in zip(bits_list, lengths):
+        q = torch.randn((1, 9, n, 64), device='cuda', dtype=torch.bfloat16)
+        k = torch.randn((1, 3, n, 64), device='cuda', dtype=torch.bfloat16)
+        v = torch.randn_like(k)
+        cache.select(bits)
+        past = cache.append(k, v, 0)
+        output = cache.attend(q, k, v, 0, past)
+        if past:
+            rk = torch.cat([torch.cat(full_k, 2), k], 2)
+            rv = torch.cat([torch.cat(full_v, 2), v], 2)
+        else:
+            rk, rv = k, v
+        mask = torch.arange(rk.shape[-2], device='cuda')[None, :] <= past + torch.arange(n, device='cuda')[:, None]
+        expected = torch.nn.functional.scaled_dot_product_attention(
+            q, rk.repeat_interleave(3, 1), rv.repeat_interleave(3, 1), attn_mask=mask).transpose(1, 2)
+        assert (output.float() - expected.float()).abs().max().item() < .035
+        mk, mv = cache.materialize(0)
+        full_k, full_v = [mk], [mv]
+        if bits == 16:
+            assert torch.equal(mk[:, :, -n:], k)
+
+
+def test_reference_branch_does_not_advance_video_cache(cuda):
+    # tests/test_gpu_backend.py:29-37
+    from src.gpu_cache import GPUCache
+    c = GPUCache([(4, 20), (16, 10)], layers=1)
+    k = torch.randn(1, 3, 20, 64, device='cuda', dtype=torch.bfloat16)
+    c.select(4)
+    c.append(k, k, 0)
+    before = c.materialize(0)[0].clone()
+    branch = c.fork()
+    q = torch.randn(1, 3, 5, 64, device='cuda', dtype=torch.bfloat16)
+    branch.append(q, q, 0)
+    assert c.get_seq_length() == 20 and branch.get_seq_length() == 25
+    assert torch.equal(c.materialize(0)[0], before)
+
+
+def test_reference_online_growth_and_mapping(cuda):
+    # tests/test_gpu_backend.py:39-54
+    from src.gpu_cache import GPUCache
+    c = GPUCache(None, layers=1, max_tokens=512)
+    expected = []
+    for i, (bits, n) in enumerate([(4, 79), (8, 93), (4, 88), (16, 71)]):
+        x = torch.randn(1, 3, n, 64, device='cuda', dtype=torch.bfloat16)
+        c.select(bits, i)
+        c.append(x, x, 0)
+        expected.extend([bits] * n)
+    assert c.codes[:len(expected)].tolist() == expected
+    assert c.caps[4] >= 167 and c.caps[8] >= 93 and c.caps[16] >= 71
+    assert c.get_seq_length() == len(expected)
+    before = c.materialize(0)[0].clone()
+    branch = c.fork()
+    branch.select(16)
+    z = torch.randn(1, 3, 90, 64, device='cuda', dtype=torch.bfloat16)
+    old_caps = c.caps.copy()
+    branch.append(z, z, 0)
+    assert c.caps == old_caps
+    assert torch.equal(c.materialize(0)[0], before)
+
+
+def test_update_contract_for_sdpa_backend(cuda):
+    from src.gpu_cache import GPUCache
+    c = GPUCache(None, layers=1, heads=2, backend='sdpa')
+    x = torch.randn(1, 2, 10, 64, device='cuda', dtype=torch.bfloat16)
+    c.select(8)
+    k, v = c.update(x, x, 0)
+    assert k.shape == (1, 2, 10, 64) and torch.equal(k[:, :, -10:], x)
+    y = torch.randn(1, 2, 4, 64, device='cuda', dtype=torch.bfloat16)
+    c.select(16)
+    k, v = c.update(y, y, 0)
+    assert k.shape == (1, 2, 14, 64) and torch.equal(v[:, :, -4:], y)
+
+
+@pytest.mark.parametrize('dim', [576, 960])
+def test_reference_cuda_rms_matches_upstream(cuda, dim):
+    # tests/test_gpu_backend.py:103-110
+    from src.gpu_ops import cuda_rms
+    x = torch.randn(1, 19, dim, device='cuda', dtype=torch.bfloat16)
+    weight = torch.randn(dim, device='cuda', dtype=torch.bfloat16)
+    reference = weight * (x.float() * torch.rsqrt(x.float().pow(2).mean(-1, keepdim=True) + 1e-5)).bfloat16()
+    actual = cuda_rms(x, weight, 1e-5)
+    assert (reference.float() - actual.float()).abs().max() < .063
+    assert (reference.float() - actual.float()).abs().mean() < .001
+
+
+def test_reference_fused_activation_matches_upstream(cuda):
+    # tests/test_gpu_backend.py:112-122
+    from src.gpu_ops import activation_product
+    gate = torch.randn(1, 23, 2560, device='cuda', dtype=torch.bfloat16)
+    up = torch.randn_like(gate)
+    expected = torch.nn.functional.silu(gate) * up
+    actual = activation_product(gate, up)
+    assert (expected.float() - actual.float()).abs().max() < .063
+    joined = torch.randn(1, 23, 5120, device='cuda', dtype=torch.bfloat16)
+    gate, up = joined.chunk(2, -1)
+    assert torch.allclose(activation_product(gate, up), torch.nn.functional.silu(gate) * up, atol=.063, rtol=.01)

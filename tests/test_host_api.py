@@ -1,0 +1,93 @@
+"""CPU tests of the GPUCache host logic (plan, growth, fork, accounting), which
+mirrors src/gpu_cache.py of the reference. Pools live on the CPU here; every
+path that would launch a kernel is rejected before reaching the library."""
+import pytest
+import torch
+
+from src.gpu_cache import GPUCache
+
+
+def test_constructor_validation_messages():
+    with pytest.raises(ValueError, match='head_dim=64'):
+        GPUCache(dim=128, device='cpu')
+    with pytest.raises(ValueError, match='Invalid GPU cache plan'):
+        GPUCache([(5, 10)], device='cpu')
+    with pytest.raises(ValueError, match='Invalid GPU cache plan'):
+        GPUCache([(4, -1)], device='cpu')
+
+
+def test_offline_plan_rows_codes_and_caps():
+    c = GPUCache([(4, 20), (16, 10), (4, 5), (8, 3)], layers=2, device='cpu')
+    assert c.plan == [(0, 20, 4, 0), (20, 30, 16, 0), (30, 35, 4, 20), (35, 38, 8, 0)]
+    assert c.rows.tolist() == list(range(20)) + list(range(10)) + list(range(20, 25)) + list(range(3))
+    assert c.codes.tolist() == [4] * 20 + [16] * 10 + [4] * 5 + [8] * 3
+    assert c.caps == {4: 25, 8: 3, 16: 10} and c.capacity == 38
+    assert c.p4.shape == (2, 2, 3, 25, 32) and c.m8.shape == (2, 2, 3, 3, 2)
+    assert c.p16.dtype == torch.bfloat16 and len(c) == 2 and c.get_seq_length() == 0
+
+
+def test_online_growth_policy_matches_reference():
+    c = GPUCache(None, layers=1, device='cpu', max_tokens=512)
+    assert c.caps == {4: 64, 8: 64, 16: 64} and c.capacity == 512
+    sentinel = torch.arange(c.p4.numel(), dtype=torch.int64).remainder(251).to(torch.uint8).view(c.p4.shape)
+    c.p4.copy_(sentinel)
+    c.reserve(4, 79)           # max(79, ceil64(96)) = 128
+    assert c.caps[4] == 128 and c.p4.shape[3] == 128 and c.m4.shape[3] == 128
+    assert torch.equal(c.p4[:, :, :, :64], sentinel)  # old rows copied
+    c.reserve(4, 167)          # max(167, ceil64(192)) = 192
+    assert c.caps[4] == 192
+    c.reserve(4, 100)          # no shrink / no-op
+    assert c.caps[4] == 192
+    c.reserve(16, 400)         # needed beats 1.5x
+    assert c.caps[16] == 400 and c.p16.shape[3] == 400
+
+
+def test_append_requires_cuda_and_batch_one():
+    c = GPUCache(None, layers=1, device='cpu')
+    x = torch.zeros(1, 3, 4, 64, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match='requires CUDA'):
+        c.append(x, x, 0)
+    with pytest.raises(ValueError, match='requires CUDA'):
+        c.append(torch.zeros(2, 3, 4, 64), torch.zeros(2, 3, 4, 64), 0)
+
+
+def test_fork_copies_host_state_and_shares_pools():
+    c = GPUCache([(4, 20), (16, 10)], layers=1, device='cpu')
+    c.seen[0] = 20
+    c.select(4, 3)
+    b = c.fork()
+    assert b.pending_bits == 16 and c.pending_bits == 4 and c.frame_id == 3
+    b.seen[0] = 25
+    b.caps[16] = 999
+    b.plan.append((99, 100, 16, 0))
+    b.host_counts[16] += 5
+    assert c.seen[0] == 20 and c.caps[16] == 10 and len(c.plan) == 2 and c.host_counts[16] == 10
+    assert b.p4 is c.p4 and b.rows is c.rows  # pools and maps are shared, as in the reference
+
+
+def test_accounting_matches_reference_audit_formulas():
+    # scripts/gpu_validate.py:61-70 formulas, L=32, H=5
+    c = GPUCache(None, layers=32, heads=5, device='cpu')
+    plan = [(16, 11), (4, 64), (8, 64), (16, 64), (4, 64)]
+    for bits, n in plan:
+        row = c.host_counts[bits]
+        c.reserve(bits, row + n)
+        c.plan.append((c.seen[0], c.seen[0] + n, bits, row))
+        c.host_counts[bits] += n
+        c.seen = [s + n for s in c.seen]
+    a = c.accounting()
+    tokens = {4: 128, 8: 64, 16: 75}
+    used = sum(tokens.values())
+    assert a['precision_token_counts'] == tokens and a['used_tokens'] == used
+    assert a['payload_bytes'] == 32 * 2 * 5 * 64 * sum(tokens[b] * b / 8 for b in tokens)
+    assert a['quantization_metadata_bytes'] == 32 * 2 * 5 * 8 * (tokens[4] + tokens[8])
+    assert a['token_mapping_bytes'] == used * 5
+    assert a['gpu_cache_used_bytes'] == a['payload_bytes'] + a['quantization_metadata_bytes'] + used * 5
+    caps = a['precision_pool_capacities']
+    assert a['gpu_cache_allocated_bytes'] == 32 * 2 * 5 * (40 * caps[4] + 72 * caps[8] + 128 * caps[16]) + 8192 * 5
+    assert a['cpu_cache_payload_bytes'] == 0
+
+
+def test_non_bf16_pool_dtype_is_rejected():
+    with pytest.raises(ValueError, match='bfloat16'):
+        GPUCache(device='cpu', dtype=torch.float16)

@@ -154,8 +154,10 @@ int dkv_packed_attention(const void* q, const void* knew, const void* vnew, cons
   a.ws_o = static_cast<float*>(workspace);
   a.ws_ml = need > 0 ? reinterpret_cast<float2*>(static_cast<uint8_t*>(workspace) + p.ws_o_bytes) : nullptr;
   a.status = status;
-  return cuda_status(dkv::launch_attention_split(a, heads, static_cast<cudaStream_t>(stream)),
-                     "packed_attention launch");
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = p.tc ? dkv::launch_attention_tc(a, heads, st) : dkv::launch_attention_split(a, heads, st);
+  if (e == cudaSuccess && p.splits > 1) e = dkv::launch_attention_combine(a, heads, st);
+  return cuda_status(e, "packed_attention launch");
 }
 
 int dkv_reconstruct(const void* p4, const void* m4, const void* p8, const void* m8, const void* p16,

@@ -6,7 +6,9 @@
 namespace dkv {
 
 constexpr int kBN = 64;                 // keys per history tile
-constexpr int kMaxCtaRows = 192;        // flattened (query, head) rows per CTA
+constexpr int kMaxCtaRows = 192;        // flattened (query, head) rows per CTA, CUDA-core path
+constexpr int kTcCtaRows = 256;         // rows per CTA on the tensor-core path (2 x M=128)
+constexpr int kTcMinRows = 49;          // group*nq from which the tensor-core path is used
 constexpr int kTargetCtas = 148;        // one wave on a B200 (148 SMs)
 // D^-0.5 * log2(e): the reference scales scores by D^-0.5 (src/gpu_kernels.py:95)
 // and uses exp; the kernels work in the exp2 domain with the factor folded in.
@@ -15,9 +17,10 @@ constexpr float kScaleLog2 = 0.125f * 1.4426950408889634f;
 // Work decomposition of one attention call. Deterministic in (past, nq, heads,
 // group): no dependence on the device, so results are bit-identical across GPUs.
 struct AttnPlan {
+  int tc;        // 1: tcgen05 tensor-core kernel, 0: mma.sync split kernel
   int mrows;     // group * nq flattened rows per KV head (row r = query r/G, head r%G)
   int mblocks;   // row blocks per KV head
-  int cta_rows;  // rows per block, multiple of 16
+  int cta_rows;  // rows per block (multiple of 16; 256 on the tensor-core path)
   int splits;    // history splits per (head, row block)
   int chunk;     // keys per split, multiple of kBN
   size_t ws_o_bytes, ws_ml_bytes;
@@ -26,17 +29,22 @@ struct AttnPlan {
 inline AttnPlan make_plan(int past, int nq, int heads, int group) {
   AttnPlan p{};
   p.mrows = group * nq;
-  p.mblocks = (p.mrows + kMaxCtaRows - 1) / kMaxCtaRows;
-  const int per_block = (p.mrows + p.mblocks - 1) / p.mblocks;
-  p.cta_rows = ((per_block + 15) / 16) * 16;
+  p.tc = p.mrows >= kTcMinRows;
+  if (p.tc) {
+    p.cta_rows = kTcCtaRows;
+    p.mblocks = (p.mrows + kTcCtaRows - 1) / kTcCtaRows;
+  } else {
+    p.mblocks = (p.mrows + kMaxCtaRows - 1) / kMaxCtaRows;
+    const int per_block = (p.mrows + p.mblocks - 1) / p.mblocks;
+    p.cta_rows = ((per_block + 15) / 16) * 16;
+  }
   const int total = past + nq;
-  const int max_splits = (total + kBN - 1) / kBN;
-  int splits = (kTargetCtas + heads * p.mblocks - 1) / (heads * p.mblocks);
-  if (splits > max_splits) splits = max_splits;
-  if (splits < 1) splits = 1;
-  const int per_split = (total + splits - 1) / splits;
-  p.chunk = ((per_split + kBN - 1) / kBN) * kBN;
-  p.splits = (total + p.chunk - 1) / p.chunk;
+  const int tiles = (total + kBN - 1) / kBN;
+  int target = kTargetCtas / (heads * p.mblocks);
+  if (target < 1) target = 1;
+  const int per_split = (tiles + target - 1) / target;  // tiles per split
+  p.chunk = per_split * kBN;
+  p.splits = (tiles + per_split - 1) / per_split;
   if (p.splits > 1) {
     const size_t ctas = static_cast<size_t>(heads) * p.mblocks * p.splits;
     p.ws_o_bytes = ctas * p.cta_rows * kDim * sizeof(float);
@@ -62,5 +70,7 @@ struct AttnArgs {
 };
 
 cudaError_t launch_attention_split(const AttnArgs& a, int heads, cudaStream_t stream);
+cudaError_t launch_attention_tc(const AttnArgs& a, int heads, cudaStream_t stream);
+cudaError_t launch_attention_combine(const AttnArgs& a, int heads, cudaStream_t stream);
 
 }  // namespace dkv

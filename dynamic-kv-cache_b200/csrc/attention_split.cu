@@ -338,14 +338,12 @@ cudaError_t launch_nw(const AttnArgs& a, int heads, size_t smem, cudaStream_t st
 cudaError_t launch_attention_split(const AttnArgs& a, int heads, cudaStream_t stream) {
   const int cw = a.cta_rows / 16;
   const size_t smem = static_cast<size_t>(a.cta_rows) * 128 + 4 * kBN * 128;
-  cudaError_t e;
-  if (cw <= 4)
-    e = launch_nw<4>(a, heads, smem, stream);
-  else if (cw <= 8)
-    e = launch_nw<8>(a, heads, smem, stream);
-  else
-    e = launch_nw<12>(a, heads, smem, stream);
-  if (e != cudaSuccess || a.splits == 1) return e;
+  if (cw <= 4) return launch_nw<4>(a, heads, smem, stream);
+  if (cw <= 8) return launch_nw<8>(a, heads, smem, stream);
+  return launch_nw<12>(a, heads, smem, stream);
+}
+
+cudaError_t launch_attention_combine(const AttnArgs& a, int heads, cudaStream_t stream) {
   const int warps = heads * a.mrows;
   attention_combine_kernel<<<(warps + 7) / 8, 256, 0, stream>>>(a, heads);
   return cudaGetLastError();

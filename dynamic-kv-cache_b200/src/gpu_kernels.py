@@ -20,10 +20,11 @@ import torch
 
 _LIB_PATH = Path(__file__).resolve().parent.parent / 'libdkv.so'
 
-DKV_OK, DKV_EINVAL, DKV_ECAPACITY, DKV_EPLAN, DKV_ECUDA, DKV_ENONFINITE, DKV_EWORKSPACE = range(7)
+DKV_OK, DKV_EINVAL, DKV_ECAPACITY, DKV_EPLAN, DKV_ECUDA, DKV_ENONFINITE, DKV_EWORKSPACE, DKV_ETIMEOUT = range(8)
 STATUS_NAMES = {DKV_EINVAL: 'invalid argument', DKV_ECAPACITY: 'capacity exceeded',
                 DKV_EPLAN: 'bad precision code in token map', DKV_ECUDA: 'CUDA error',
-                DKV_ENONFINITE: 'Nonfinite KV tensor', DKV_EWORKSPACE: 'workspace too small'}
+                DKV_ENONFINITE: 'Nonfinite KV tensor', DKV_EWORKSPACE: 'workspace too small',
+                DKV_ETIMEOUT: 'kernel pipeline wait timed out'}
 
 
 def _load():

@@ -51,7 +51,8 @@ enum dkv_status {
   DKV_EPLAN = 3,      /* token map holds a code other than 4, 8 or 16             */
   DKV_ECUDA = 4,      /* a CUDA runtime call or launch failed                     */
   DKV_ENONFINITE = 5, /* pack input held NaN or Inf                               */
-  DKV_EWORKSPACE = 6  /* workspace smaller than dkv_packed_attention_workspace()  */
+  DKV_EWORKSPACE = 6, /* workspace smaller than dkv_packed_attention_workspace() */
+  DKV_ETIMEOUT = 7    /* a kernel pipeline wait gave up (bounded waits, no hang)  */
 };
 
 /* Library version (DKV_VERSION). */

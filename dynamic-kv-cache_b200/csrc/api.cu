@@ -117,6 +117,8 @@ int dkv_packed_attention(const void* q, const void* knew, const void* vnew, cons
   if (past < 0 || nq < 0) return fail(DKV_EINVAL, "negative past or query length");
   if (nq == 0) return ok();
   if (past > 0 && (rows == nullptr || codes == nullptr)) return fail(DKV_EINVAL, "null token map");
+  if (past > 0 && (!aligned16(rows) || !aligned16(codes)))
+    return fail(DKV_EINVAL, "token maps must be 16-byte aligned");
   if (!rows_aligned(q, qh, qt) || !rows_aligned(knew, kh, kt) || !rows_aligned(vnew, vh, vt))
     return fail(DKV_EINVAL, "q/k/v rows must be 16-byte aligned (head/token strides multiples of 8)");
   if (out == nullptr || !aligned16(out)) return fail(DKV_EINVAL, "out must be 16-byte aligned");

@@ -18,6 +18,7 @@
 //    XOR-swizzled shared memory while the next tile's packed bytes are already in
 //    flight (register double buffering), then consumed by ldmatrix + mma.sync.
 #include "attention.cuh"
+#include "tc_ptx.cuh"
 
 namespace dkv {
 namespace {
@@ -272,47 +273,87 @@ attention_split_kernel(const AttnArgs a) {
     }
     return;
   }
+  // partial layout [cta][dim][row], shared with the tensor-core kernel
   const int64_t cta = (static_cast<int64_t>(g) * a.mblocks + mb) * a.splits + split;
+  float* base = a.ws_o + cta * kDim * a.cta_rows;
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
     const int r = half ? rb : ra;
-    float* dst = a.ws_o + (cta * a.cta_rows + r) * kDim;
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      *reinterpret_cast<float2*>(dst + 8 * j + c2) = make_float2(o[j][2 * half], o[j][2 * half + 1]);
+    for (int j = 0; j < 8; ++j) {
+      base[(8 * j + c2) * a.cta_rows + r] = o[j][2 * half];
+      base[(8 * j + c2 + 1) * a.cta_rows + r] = o[j][2 * half + 1];
+    }
     if ((lane & 3) == 0)
       a.ws_ml[cta * a.cta_rows + r] = half ? make_float2(m_b, l_b) : make_float2(m_a, l_a);
   }
 }
 
-// Merges the split partials of each (KV head, row) in split order.
-// One warp per row; lane owns dims 2*lane, 2*lane+1.
-__global__ void __launch_bounds__(256) attention_combine_kernel(const AttnArgs a, int heads) {
-  const int w = blockIdx.x * 8 + (threadIdx.x >> 5);
+// Merges the split partials of each (KV head, row) in split order (fixed order:
+// deterministic). One thread per (row, dim): warps read 32 consecutive rows of one
+// dim (coalesced in the [cta][dim][row] partial layout); the block's 32 x 8 tile
+// is transposed through shared memory so the bf16 output leaves as 16-byte rows.
+__global__ void __launch_bounds__(256) attention_combine_kernel(const AttnArgs a) {
+  __shared__ float tile[8][33];
+  ptx::pdl_wait();  // partials of the attention grid
+  ptx::pdl_trigger();
+  const int g = blockIdx.z;
   const int lane = threadIdx.x & 31;
-  if (w >= heads * a.mrows) return;
-  const int g = w / a.mrows;
-  const int fr = w - g * a.mrows;
-  const int mb = fr / a.cta_rows;
-  const int r = fr - mb * a.cta_rows;
-  const int64_t first = ((static_cast<int64_t>(g) * a.mblocks + mb) * a.splits) * a.cta_rows + r;
-  float mx = -INFINITY;
-  for (int s = 0; s < a.splits; ++s) mx = fmaxf(mx, a.ws_ml[first + static_cast<int64_t>(s) * a.cta_rows].x);
-  float den = 0.f, x0 = 0.f, x1 = 0.f;
-  for (int s = 0; s < a.splits; ++s) {
-    const int64_t idx = first + static_cast<int64_t>(s) * a.cta_rows;
-    const float2 ml = a.ws_ml[idx];
-    const float wgt = ml.x == -INFINITY ? 0.f : exp2f(ml.x - mx);
-    const float2 v = *reinterpret_cast<const float2*>(a.ws_o + idx * kDim + 2 * lane);
-    den += wgt * ml.y;
-    x0 += wgt * v.x;
-    x1 += wgt * v.y;
+  const int dl = threadIdx.x >> 5;       // dim within the block's 8
+  const int d = blockIdx.y * 8 + dl;
+  const int fr = blockIdx.x * 32 + lane;
+  float val = 0.f;
+  if (fr < a.mrows) {
+    const int mb = fr / a.cta_rows;
+    const int r = fr - mb * a.cta_rows;
+    const int64_t cta0 = (static_cast<int64_t>(g) * a.mblocks + mb) * a.splits;
+    // chunks of 16 splits: all 32 loads of a chunk are in flight together, and
+    // the chunk maxima rescale the running sums (fixed order: deterministic)
+    float mx = -INFINITY, den = 0.f, acc = 0.f;
+    for (int base = 0; base < a.splits; base += 16) {
+      float2 ml[16];
+      float o[16];
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        ml[q] = make_float2(-INFINITY, 0.f);
+        o[q] = 0.f;
+        if (base + q < a.splits) {
+          ml[q] = a.ws_ml[(cta0 + base + q) * a.cta_rows + r];
+          o[q] = a.ws_o[((cta0 + base + q) * kDim + d) * a.cta_rows + r];
+        }
+      }
+      float cm = mx;
+#pragma unroll
+      for (int q = 0; q < 16; ++q) cm = fmaxf(cm, ml[q].x);
+      if (cm == -INFINITY) continue;
+      const float keep = mx == -INFINITY ? 0.f : exp2f(mx - cm);
+      den *= keep;
+      acc *= keep;
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        const float wgt = ml[q].x == -INFINITY ? 0.f : exp2f(ml[q].x - cm);
+        den += wgt * ml[q].y;
+        acc += wgt * o[q];
+      }
+      mx = cm;
+    }
+    val = acc / den;
   }
-  const float inv = 1.f / den;
-  const int m = fr / a.G;
-  const int h = g * a.G + (fr - m * a.G);
-  uint16_t* dst = a.out + (static_cast<int64_t>(m) * a.HQ + h) * kDim + 2 * lane;
-  *reinterpret_cast<uint32_t*>(dst) = pack_bf16x2(x0 * inv, x1 * inv);
+  tile[dl][lane] = val;
+  __syncthreads();
+  if (threadIdx.x < 32) {  // one thread per row: 8 dims = 16 bytes
+    const int row = blockIdx.x * 32 + threadIdx.x;
+    if (row < a.mrows) {
+      const int m = row / a.G;
+      const int h = g * a.G + (row - m * a.G);
+      uint4 w;
+      w.x = pack_bf16x2(tile[0][threadIdx.x], tile[1][threadIdx.x]);
+      w.y = pack_bf16x2(tile[2][threadIdx.x], tile[3][threadIdx.x]);
+      w.z = pack_bf16x2(tile[4][threadIdx.x], tile[5][threadIdx.x]);
+      w.w = pack_bf16x2(tile[6][threadIdx.x], tile[7][threadIdx.x]);
+      *reinterpret_cast<uint4*>(a.out + (static_cast<int64_t>(m) * a.HQ + h) * kDim + blockIdx.y * 8) = w;
+    }
+  }
 }
 
 template <int NW>
@@ -344,9 +385,16 @@ cudaError_t launch_attention_split(const AttnArgs& a, int heads, cudaStream_t st
 }
 
 cudaError_t launch_attention_combine(const AttnArgs& a, int heads, cudaStream_t stream) {
-  const int warps = heads * a.mrows;
-  attention_combine_kernel<<<(warps + 7) / 8, 256, 0, stream>>>(a, heads);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((a.mrows + 31) / 32, kDim / 8, heads);
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, attention_combine_kernel, a);
 }
 
 }  // namespace dkv

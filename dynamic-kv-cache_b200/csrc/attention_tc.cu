@@ -7,23 +7,26 @@
 // current chunk's native K/V, q.k * D^-0.5 (:95), bottom-right causal mask (:96),
 // online softmax (:98-103), p rounded to bf16 before P.V (:102), fp32 accumulation.
 //
-// One CTA per (KV head, block of up to 256 stacked rows, history split), 13 warps
-// in three roles connected by mbarriers:
-//   warps 9-12  producers: gather the split's packed history tile by tile (token
-//               maps -> pool rows), dequantise in registers and write bf16 K and V
-//               tiles (64 keys) into a 3-stage ring in the 128B-swizzled K-major
-//               layout the tensor core reads;
-//   warp 8      MMA issuer (one thread): S = Q K^T into TMEM (double-buffered), then
-//               O += P V into TMEM, both tcgen05.mma kind::f16 with M = 128;
+// One CTA per (KV head, block of up to 256 stacked rows, history split), 16 warps
+// in five roles, connected only by mbarriers:
+//   warps 10-11 loaders (even / odd tiles): token maps of tile i+6 arrive by TMA
+//               bulk copy; for tile i+4
+//               the warp splits the 64 tokens into runs of consecutive pool rows of
+//               one precision and streams each run (codes, and the offset/scale
+//               pairs) into a 4-deep raw ring with one TMA bulk copy per run;
+//   warps 12-15 converters: dequantise a raw tile in registers into bf16 K and V
+//               tiles (64 keys) of a 3-stage ring, 128B-swizzled for the tensor core;
+//   warp 8      S issuer (one thread): S = Q K^T into TMEM, double-buffered;
+//   warp 9      PV issuer (one thread): [O | l] += P [V | 1] into TMEM; the block
+//               of ones makes the tensor core accumulate the softmax denominator;
 //   warps 0-7   softmax: one TMEM lane = one stacked row each; read S, mask, online
-//               max / exp2 / sum in fp32, write P (bf16) to shared memory for the
-//               P V product, and rescale O in TMEM when the running max moves.
+//               max and exp2 in fp32, write P (bf16) to shared memory, and rescale
+//               O in TMEM when the running max moves.
 // The running max is only moved when a tile's max exceeds it by more than 2^8
-// (p <= 256, exact after the final O / l division); everything else is the
-// reference's arithmetic. Partial (max, sum, O) per split go to the workspace and
-// are merged by the deterministic combine kernel. Every mbarrier wait is bounded:
-// a stalled pipeline reports DKV_ETIMEOUT in the status word and the CTA exits
-// after its MMAs drain and TMEM is freed.
+// (p <= 256, exact after the final O / l division). Partial (max, sum, O) per
+// split go to the workspace and are merged by the deterministic combine kernel.
+// Every mbarrier wait is bounded: a stalled pipeline reports DKV_ETIMEOUT in the
+// status word and the CTA exits after its MMAs drain and TMEM is freed.
 #include "attention.cuh"
 #include "tc_ptx.cuh"
 
@@ -32,43 +35,164 @@ namespace {
 
 using namespace ptx;
 
-constexpr int kStages = 3;
+constexpr int kStages = 3;     // bf16 operand ring (K and V tiles)
+constexpr int kRawStages = 4;  // packed-bytes ring filled by TMA
+constexpr int kMapStages = 6;  // token-map ring filled by TMA
 constexpr int kSoftmaxWarps = 8;
-constexpr int kMmaWarp = 8;
-constexpr int kProdWarp0 = 9;
-constexpr int kProdWarps = 4;
-constexpr int kThreadsTc = (kSoftmaxWarps + 1 + kProdWarps) * 32;  // 416
-constexpr int kProdThreads = kProdWarps * 32;
-constexpr int kTasksPerProd = (2 * kBN * 8) / kProdThreads;  // 8 (row, 8-dim part) tasks
+constexpr int kSWarp = 8;
+constexpr int kPVWarp = 9;
+constexpr int kLoadWarp0 = 10;  // two loader warps: even / odd tiles
+constexpr int kLoadWarps = 2;
+constexpr int kConvWarp0 = kLoadWarp0 + kLoadWarps;
+constexpr int kConvWarps = 4;
+constexpr int kThreadsTc = (kConvWarp0 + kConvWarps) * 32;  // 512
+constexpr int kConvThreads = kConvWarps * 32;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0;    // S[buf][mt] at columns (buf * 2 + mt) * 64
-constexpr uint32_t kColO = 256;  // O[mt] at columns 256 + mt * 64
+constexpr uint32_t kColO = 256;  // O[mt] at columns 256 + mt * 128: 64 output dims + 16 row-sum columns
+constexpr int kNPV = kDim + 16;  // P V product width: V plus a block of ones (sum of p per row)
 
 constexpr int kTile = kBN * 128;  // one 64-key bf16 tile, 8 KB
-constexpr int kOffQ = 0;          // 2 M-tiles x 128 rows x 128 B
+// Raw stage: K rows, V rows (a run starting at token j0 is packed densely from
+// byte j0 * 128), K/V (offset, scale) pairs (a run's pairs from byte j0 * 16,
+// shifted by one pair when its first pair sits at an odd pool index), and one
+// 64-bit entry per token: {code | raw offset << 8, K meta offset | V meta offset << 16}.
+constexpr int kRawK = 0;
+constexpr int kRawV = kTile;
+constexpr int kRawMetaK = 2 * kTile;
+constexpr int kRawMetaV = kRawMetaK + kBN * 16;
+constexpr int kRawTab = kRawMetaV + kBN * 16;
+// Header word: the tile's code when all 64 tokens form one pool run (else 0),
+// bit 8 / bit 9 = K / V pairs shifted by one (odd first pair index).
+constexpr int kRawHdr = kRawTab + kBN * 8;
+constexpr int kRawStage = kRawHdr + 16;
+// Map stage: codes (64 B) then rows (256 B) of one tile.
+constexpr int kMapStage = kBN + kBN * 4;
+
+constexpr int kOffQ = 0;  // 2 M-tiles x 128 rows x 128 B
 constexpr int kOffP = kOffQ + 2 * 128 * 128;
 constexpr int kOffK = kOffP + 2 * 128 * 128;
 constexpr int kOffV = kOffK + kStages * kTile;
-constexpr int kOffBar = kOffV + kStages * kTile;
+constexpr int kOffOnes = kOffV + kStages * kTile;  // 64 x 64 bf16 ones: the second N-atom of every V tile
+constexpr int kOffRaw = kOffOnes + kTile;
+constexpr int kOffMap = kOffRaw + kRawStages * kRawStage;
+constexpr int kOffBar = ((kOffMap + kMapStages * kMapStage + 15) / 16) * 16;
 enum {
-  B_FULL = 0,
-  B_EMPTY = B_FULL + kStages,
-  B_SFULL = B_EMPTY + kStages,
+  B_FULL = 0,                           // operand stage ready    (converters, 128)
+  B_EMPTY = B_FULL + kStages,           // operand stage free     (PV commit)
+  B_RAWFULL = B_EMPTY + kStages,        // raw stage landed       (loader + TMA bytes)
+  B_RAWEMPTY = B_RAWFULL + kRawStages,  // raw stage consumed     (converters, 128)
+  B_MAPFULL = B_RAWEMPTY + kRawStages,  // map stage landed       (loader + TMA bytes)
+  B_SFULL = B_MAPFULL + kMapStages,
   B_SFREE = B_SFULL + 2,
   B_PFULL = B_SFREE + 2,
   B_ODONE = B_PFULL + 1,
-  B_FIN = B_ODONE + 1,
-  B_COUNT = B_FIN + 1
+  B_QREADY = B_ODONE + 1,
+  B_FINS = B_QREADY + 1,
+  B_FINPV = B_FINS + 1,
+  B_COUNT = B_FINPV + 1
 };
 constexpr int kOffTmem = kOffBar + B_COUNT * 8;
 constexpr int kOffAbort = kOffTmem + 4;
 constexpr int kSmemTc = kOffAbort + 4 + 1024;  // + slack to align the base to 1024 B
-constexpr long long kWaitCycles = 400000000LL; // ~0.2 s: a healthy wait is microseconds
+static_assert(kSmemTc <= 227 * 1024, "shared memory budget");
+constexpr long long kWaitCycles = 400000000LL;  // ~0.2 s: a healthy wait is microseconds
 
-constexpr uint32_t kIdescS = idesc_bf16(128, kBN, 0);   // S = Q K^T: B = K tile, K-major
-constexpr uint32_t kIdescPV = idesc_bf16(128, kDim, 1); // O = P V:  B = V tile, MN-major
+constexpr uint32_t kIdescS = idesc_bf16(128, kBN, 0);    // S = Q K^T: B = K tile, K-major
+constexpr uint32_t kIdescPV = idesc_bf16(128, kNPV, 1);  // [O | l] = P [V | 1]: B MN-major, 2 N-atoms
+
+constexpr int kCodeNew = 17;  // token of the current chunk: native row of knew / vnew
 
 __device__ __forceinline__ int swz(int row, int chunk) { return row * 128 + ((chunk ^ (row & 7)) << 4); }
+
+__device__ __forceinline__ int row_bytes(int code) { return code == 4 ? 32 : (code == 8 ? 64 : 128); }
+
+// 32-bit x -> 64-bit with bit i moved to bit 2i.
+__device__ __forceinline__ uint64_t spread_bits(uint32_t x) {
+  uint64_t v = x;
+  v = (v | (v << 16)) & 0x0000FFFF0000FFFFull;
+  v = (v | (v << 8)) & 0x00FF00FF00FF00FFull;
+  v = (v | (v << 4)) & 0x0F0F0F0F0F0F0F0Full;
+  v = (v | (v << 2)) & 0x3333333333333333ull;
+  v = (v | (v << 1)) & 0x5555555555555555ull;
+  return v;
+}
+
+// 8 codes (bytes b0 = elements 0..3 and b1 = 4..7 for 8-bit; nibbles of w for
+// 4-bit) -> 8 bf16 of code * scale + offset, one packed FMA per pair. Codes become
+// exact floats as 2^23 + code minus 2^23.
+template <int BITS>
+__device__ __forceinline__ uint4 dequant_fast(uint32_t w0, uint32_t w1, float offset, float scale) {
+  uint32_t b0, b1;
+  if (BITS == 8) {
+    b0 = w0;
+    b1 = w1;
+  } else {
+    b0 = w0 & 0x0F0F0F0Fu;         // byte j = element 2j
+    b1 = (w0 >> 4) & 0x0F0F0F0Fu;  // byte j = element 2j + 1
+  }
+  const float2 sc = make_float2(scale, scale);
+  const float2 of = make_float2(offset, offset);
+  const float2 mag = make_float2(-8388608.f, -8388608.f);
+  uint32_t out[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    uint32_t lo, hi;
+    if (BITS == 8) {
+      const uint32_t w = e < 2 ? b0 : b1;
+      lo = __byte_perm(w, 0x4B000000u, 0x7540 | (2 * (e & 1)));
+      hi = __byte_perm(w, 0x4B000000u, 0x7540 | (2 * (e & 1) + 1));
+    } else {
+      lo = __byte_perm(b0, 0x4B000000u, 0x7540 | e);
+      hi = __byte_perm(b1, 0x4B000000u, 0x7540 | e);
+    }
+    const float2 qf = add2(make_float2(__uint_as_float(lo), __uint_as_float(hi)), mag);
+    const float2 x = fma2(qf, sc, of);
+    out[e] = pack_bf16x2(x.x, x.y);
+  }
+  return make_uint4(out[0], out[1], out[2], out[3]);
+}
+
+// Whole tile of one precision, rows packed densely from token 0: every load of
+// this thread's 8 parts is issued before any conversion, no per-token branches.
+template <int BITS>
+__device__ __forceinline__ void convert_uniform(const uint8_t* st, uint8_t* dstK, uint8_t* dstV, int jb, int c,
+                                                uint32_t hdr) {
+  constexpr int rb = BITS == 4 ? 32 : (BITS == 8 ? 64 : 128);
+  const int park = (hdr >> 8) & 1, parv = (hdr >> 9) & 1;
+  uint4 raw[8];
+  float2 mt[8];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int j = jb + 16 * k;
+#pragma unroll
+    for (int kv = 0; kv < 2; ++kv) {
+      const uint8_t* rrow = st + (kv ? kRawV : kRawK) + j * rb;
+      const int q = 2 * k + kv;
+      if (BITS == 16) {
+        raw[q] = *reinterpret_cast<const uint4*>(rrow + c * 16);
+      } else {
+        if (BITS == 8) {
+          const uint2 w = *reinterpret_cast<const uint2*>(rrow + c * 8);
+          raw[q] = make_uint4(w.x, w.y, 0, 0);
+        } else {
+          raw[q] = make_uint4(*reinterpret_cast<const uint32_t*>(rrow + c * 4), 0, 0, 0);
+        }
+        mt[q] = *reinterpret_cast<const float2*>(st + (kv ? kRawMetaV : kRawMetaK) + ((kv ? parv : park) + j) * 8);
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int j = jb + 16 * k;
+#pragma unroll
+    for (int kv = 0; kv < 2; ++kv) {
+      const int q = 2 * k + kv;
+      const uint4 v = BITS == 16 ? raw[q] : dequant_fast<BITS>(raw[q].x, raw[q].y, mt[q].x, mt[q].y);
+      *reinterpret_cast<uint4*>((kv ? dstV : dstK) + swz(j, c)) = v;
+    }
+  }
+}
 
 __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnArgs a) {
   extern __shared__ uint8_t smem_raw[];
@@ -95,53 +219,48 @@ __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnA
 
   auto bar = [&](int i) { return sbase + kOffBar + 8 * i; };
 
-  // ---- set-up: barriers, TMEM, Q (zero padding rows), P zeroed ----
+  // ---- set-up: barriers and TMEM, then every role starts at once ----
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(bar(B_FULL + s), kProdThreads);
+      mbar_init(bar(B_FULL + s), kConvThreads);
       mbar_init(bar(B_EMPTY + s), 1);
     }
+    for (int s = 0; s < kRawStages; ++s) {
+      mbar_init(bar(B_RAWFULL + s), 1);
+      mbar_init(bar(B_RAWEMPTY + s), kConvThreads);
+    }
+    for (int s = 0; s < kMapStages; ++s) mbar_init(bar(B_MAPFULL + s), 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(bar(B_SFULL + b), 1);
       mbar_init(bar(B_SFREE + b), soft_threads);
     }
     mbar_init(bar(B_PFULL), soft_threads);
     mbar_init(bar(B_ODONE), 1);
-    mbar_init(bar(B_FIN), 1);
+    mbar_init(bar(B_QREADY), kSoftmaxWarps * 32);
+    mbar_init(bar(B_FINS), 1);
+    mbar_init(bar(B_FINPV), 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
-  if (warp == kMmaWarp) {
+  if (warp == kSWarp) {
     tmem_alloc(sbase + kOffTmem, kTmemCols);
     tmem_relinquish();
   }
-  for (int i = tid; i < 2 * 128 * 8; i += kThreadsTc) {
-    const int r = i >> 3, c = i & 7;
-    uint4 val = make_uint4(0, 0, 0, 0);
-    if (r < rows_here) {
-      const int fr = row0 + r;
-      const int m = fr / a.G;
-      const int h = g * a.G + (fr - m * a.G);
-      val = __ldg(reinterpret_cast<const uint4*>(a.q + h * a.qh + m * a.qt) + c);
-    }
-    *reinterpret_cast<uint4*>(smem + kOffQ + (r >> 7) * 16384 + swz(r & 127, c)) = val;
-    *reinterpret_cast<uint4*>(smem + kOffP + (r >> 7) * 16384 + swz(r & 127, c)) = make_uint4(0, 0, 0, 0);
-  }
-  fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + kOffTmem);
+  pdl_trigger();  // the combine grid may be scheduled now; it waits for our completion
 
-  if (warp == kMmaWarp) {
-    // ================= MMA issuer =================
+  if (warp == kSWarp) {
+    // ================= S = Q K^T issuer =================
     if (lane == 0 && ntiles > 0) {
-      bool ok = true;
-      auto issue_s = [&](int i) {
+      bool ok = mbar_wait(bar(B_QREADY), 0, kWaitCycles);
+      for (int i = 0; i < ntiles && ok; ++i) {
         const int s = i % kStages, b = i & 1;
-        ok = ok && mbar_wait(bar(B_FULL + s), (i / kStages) & 1, kWaitCycles);
-        if (i >= 2) ok = ok && mbar_wait(bar(B_SFREE + b), ((i >> 1) + 1) & 1, kWaitCycles);
-        if (!ok) return;
+        ok = mbar_wait(bar(B_FULL + s), (i / kStages) & 1, kWaitCycles);
+        if (ok && i >= 2) ok = mbar_wait(bar(B_SFREE + b), ((i >> 1) + 1) & 1, kWaitCycles);
+        if (!ok) break;
         tc_fence_after();
         for (int mt = 0; mt < mt_count; ++mt) {
           const uint32_t d = tmem + kColS + (b * 2 + mt) * 64;
@@ -153,21 +272,32 @@ __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnA
           }
         }
         umma_commit(bar(B_SFULL + b));
-      };
-      issue_s(0);
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        report(a.status, DKV_ETIMEOUT, 1);
+      }
+      umma_commit(bar(B_FINS));  // drain this thread's MMAs before TMEM is released
+      mbar_wait(bar(B_FINS), 0, kWaitCycles);
+    }
+    __syncwarp();
+  } else if (warp == kPVWarp) {
+    // ================= [O | l] += P [V | 1] issuer =================
+    if (lane == 0 && ntiles > 0) {
+      bool ok = true;
       for (int i = 0; i < ntiles && ok; ++i) {
-        if (i + 1 < ntiles) issue_s(i + 1);
-        if (!ok) break;
         ok = mbar_wait(bar(B_PFULL), i & 1, kWaitCycles);
         if (!ok) break;
         tc_fence_after();
         const int s = i % kStages;
+        // the ones block sits at kOffOnes: LBO = its distance from this V tile
+        const uint32_t lbo = static_cast<uint32_t>(kOffOnes - (kOffV + s * kTile));
         for (int mt = 0; mt < mt_count; ++mt) {
-          const uint32_t d = tmem + kColO + mt * 64;
+          const uint32_t d = tmem + kColO + mt * 128;
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const uint64_t ad = sw128_desc(sbase + kOffP + mt * 16384 + k * 32, 16, 1024);
-            const uint64_t bd = sw128_desc(sbase + kOffV + s * kTile + k * 2048, kTile, 1024);
+            const uint64_t bd = sw128_desc(sbase + kOffV + s * kTile + k * 2048, lbo, 1024);
             umma_f16(d, ad, bd, kIdescPV, (i > 0 || k > 0) ? 1u : 0u);
           }
         }
@@ -176,21 +306,363 @@ __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnA
       }
       if (!ok) {
         *abort_flag = 1;
-        report(a.status, DKV_ETIMEOUT, 1);
+        report(a.status, DKV_ETIMEOUT, 2);
       }
-      umma_commit(bar(B_FIN));  // drain every MMA before TMEM is released
-      mbar_wait(bar(B_FIN), 0, kWaitCycles);
+      umma_commit(bar(B_FINPV));
+      mbar_wait(bar(B_FINPV), 0, kWaitCycles);
     }
     __syncwarp();
-  } else if (warp < kSoftmaxWarps) {
+  } else if (warp >= kLoadWarp0 && warp < kConvWarp0) {
+    // ================= loader: token maps and packed runs by TMA =================
+    // Per-CTA block bases (layer, K|V, this head) of every pool, and the parity of
+    // each meta block's first pair index, so the per-tile work is 32-bit math.
+    const int64_t blk_k = (static_cast<int64_t>(a.layer) * 2) * a.P.heads + g;  // (layer, K, head)
+    const int64_t blk_v = blk_k + a.P.heads;                                    // (layer, V, head)
+    const int cap4 = static_cast<int>(a.P.cap4), cap8 = static_cast<int>(a.P.cap8);
+    const int cap16 = static_cast<int>(a.P.cap16);
+    const uint8_t* const pk4 = a.P.p4 + blk_k * cap4 * kRowBytes4;
+    const uint8_t* const pv4 = a.P.p4 + blk_v * cap4 * kRowBytes4;
+    const uint8_t* const pk8 = a.P.p8 + blk_k * cap8 * kRowBytes8;
+    const uint8_t* const pv8 = a.P.p8 + blk_v * cap8 * kRowBytes8;
+    const uint8_t* const pk16 = reinterpret_cast<const uint8_t*>(a.P.p16 + blk_k * cap16 * kDim);
+    const uint8_t* const pv16 = reinterpret_cast<const uint8_t*>(a.P.p16 + blk_v * cap16 * kDim);
+    const float2* const mk4 = a.P.m4 + blk_k * cap4;
+    const float2* const mv4 = a.P.m4 + blk_v * cap4;
+    const float2* const mk8 = a.P.m8 + blk_k * cap8;
+    const float2* const mv8 = a.P.m8 + blk_v * cap8;
+    const int pbk4 = static_cast<int>((blk_k * cap4) & 1), pbv4 = static_cast<int>((blk_v * cap4) & 1);
+    const int pbk8 = static_cast<int>((blk_k * cap8) & 1), pbv8 = static_cast<int>((blk_v * cap8) & 1);
+    // selectors (no dynamic array indexing: keeps everything in registers)
+    auto pool_of = [&](int code, int kv) -> const uint8_t* {
+      return code == 4 ? (kv ? pv4 : pk4) : (code == 8 ? (kv ? pv8 : pk8) : (kv ? pv16 : pk16));
+    };
+    auto meta_of = [&](int code, int kv) -> const float2* { return code == 4 ? (kv ? mv4 : mk4) : (kv ? mv8 : mk8); };
+    auto mpar_of = [&](int code, int kv) -> int { return code == 4 ? (kv ? pbv4 : pbk4) : (kv ? pbv8 : pbk8); };
+    const uint16_t* const knew_g = a.knew + g * a.kh;
+    const uint16_t* const vnew_g = a.vnew + g * a.vh;
+
+    auto map_tile = [&](int tile) {  // lane 0: start the map copy of a full history tile
+      const int t0 = kb + tile * kBN;
+      const int slot = tile % kMapStages;
+      if (t0 + kBN <= a.past) {
+        mbar_expect_tx(bar(B_MAPFULL + slot), kMapStage);
+        bulk_g2s(sbase + kOffMap + slot * kMapStage, a.codes + t0, kBN, bar(B_MAPFULL + slot));
+        bulk_g2s(sbase + kOffMap + slot * kMapStage + kBN, a.rows + t0, kBN * 4, bar(B_MAPFULL + slot));
+      }
+      mbar_arrive(bar(B_MAPFULL + slot));
+    };
+    // (offset, scale) pairs of a run of `cnt` rows from block-relative row r0 for
+    // K (kv = 0) or V: one aligned bulk copy when the 16-byte span stays inside the
+    // block and holds >= 2 rows; returns the pair shift (0/1), or -1 for "caller
+    // stores the pairs with plain loads".
+    auto meta_run = [&](int code, int kv, int r0, int cnt, uint32_t dst, uint32_t rbar) -> int {
+      const int cap = code == 4 ? cap4 : cap8;
+      const int pb = mpar_of(code, kv);
+      const int par = pb ^ (r0 & 1);
+      const int end = r0 + cnt;
+      const int hi = end + (pb ^ (end & 1));
+      if (cnt < 2 || hi > cap) return -1;
+      const uint32_t bytes = static_cast<uint32_t>(hi - (r0 - par)) * 8u;
+      mbar_expect_tx(rbar, bytes);
+      bulk_g2s(dst, meta_of(code, kv) + (r0 - par), bytes, rbar);
+      return par;
+    };
+
+    const int lw = warp - kLoadWarp0;  // this warp's tiles: lw, lw + 2, ...
+    if (lane == 0) {
+      for (int t = lw; t < kMapStages && t < ntiles; t += kLoadWarps) map_tile(t);
+    }
+    __syncwarp();
+    bool ok = true;
+    for (int i = lw; i < ntiles; i += kLoadWarps) {
+      const int rs = i % kRawStages;
+      const int slot = i % kMapStages;
+      if (i >= kRawStages) ok = mbar_wait(bar(B_RAWEMPTY + rs), ((i / kRawStages) + 1) & 1, kWaitCycles);
+      ok = ok && mbar_wait(bar(B_MAPFULL + slot), (i / kMapStages) & 1, kWaitCycles);
+      if (!__all_sync(0xffffffffu, ok) || __any_sync(0xffffffffu, *abort_flag != 0)) {
+        ok = false;
+        break;
+      }
+      fence_proxy_async_smem();  // converters' reads of this raw stage precede the TMA writes
+      const int t0 = kb + i * kBN;
+      if (t0 + kBN > a.past) pdl_wait();  // current-chunk K/V come from the previous kernels
+      const uint8_t* mcodes = smem + kOffMap + slot * kMapStage;
+      const int32_t* mrows = reinterpret_cast<const int32_t*>(mcodes + kBN);
+      const bool full_map = t0 + kBN <= a.past;
+      // --- classify this lane's two tokens j = 2 lane + e ---
+      int code[2], row[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int j = 2 * lane + e;
+        const int t = t0 + j;
+        if (t >= ke) {
+          code[e] = 0;
+          row[e] = 0;
+        } else if (t >= a.past) {
+          code[e] = kCodeNew;
+          row[e] = t - a.past;
+        } else {
+          if (full_map) {
+            code[e] = mcodes[j];
+            row[e] = mrows[j];
+          } else {  // the tile holding `past`: its map was not prefetched
+            code[e] = __ldg(a.codes + t);
+            row[e] = __ldg(a.rows + t);
+          }
+          const int cap = code[e] == 4 ? cap4 : (code[e] == 8 ? cap8 : cap16);
+          if (code[e] != 4 && code[e] != 8 && code[e] != 16) {
+            report(a.status, DKV_EPLAN, t);
+            code[e] = 0;
+          } else if (row[e] < 0 || row[e] >= cap) {
+            report(a.status, DKV_ECAPACITY, t);
+            code[e] = 0;
+          }
+        }
+      }
+      // --- runs: a token starts one unless it continues the previous token's pool run ---
+      const int pcode = __shfl_up_sync(0xffffffffu, code[1], 1);
+      const int prow = __shfl_up_sync(0xffffffffu, row[1], 1);
+      const bool pooled0 = code[0] == 4 || code[0] == 8 || code[0] == 16;
+      const bool pooled1 = code[1] == 4 || code[1] == 8 || code[1] == 16;
+      const bool start0 = lane == 0 || !pooled0 || pcode != code[0] || prow + 1 != row[0];
+      const bool start1 = !pooled1 || code[0] != code[1] || row[0] + 1 != row[1];
+      const uint32_t even_starts = __ballot_sync(0xffffffffu, start0);
+      const uint32_t odd_starts = __ballot_sync(0xffffffffu, start1);
+      const int code0 = __shfl_sync(0xffffffffu, code[0], 0);
+      uint8_t* st = smem + kOffRaw + rs * kRawStage;
+      const uint32_t sst = sbase + kOffRaw + rs * kRawStage;
+      const uint32_t rbar = bar(B_RAWFULL + rs);
+      if (even_starts == 1u && odd_starts == 0u && (code0 == 4 || code0 == 8 || code0 == 16)) {
+        // ---- uniform tile: one run of 64 rows, copies from lane 0, no per-token table ----
+        const int rb = row_bytes(code0);
+        const int r0 = __shfl_sync(0xffffffffu, row[0], 0);
+        int park = 0, parv = 0;
+        if (lane == 0) {
+          mbar_expect_tx(rbar, 2 * kBN * rb);
+          bulk_g2s(sst + kRawK, pool_of(code0, 0) + static_cast<int64_t>(r0) * rb, kBN * rb, rbar);
+          bulk_g2s(sst + kRawV, pool_of(code0, 1) + static_cast<int64_t>(r0) * rb, kBN * rb, rbar);
+          if (code0 != 16) {
+            park = meta_run(code0, 0, r0, kBN, sst + kRawMetaK, rbar);
+            parv = meta_run(code0, 1, r0, kBN, sst + kRawMetaV, rbar);
+          }
+        }
+        park = __shfl_sync(0xffffffffu, park, 0);
+        parv = __shfl_sync(0xffffffffu, parv, 0);
+        if (code0 != 16 && (park < 0 || parv < 0)) {  // block-final odd run: pairs by plain loads
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int j = 2 * lane + e;
+            if (park < 0) *reinterpret_cast<float2*>(st + kRawMetaK + j * 8) = __ldg(meta_of(code0, 0) + r0 + j);
+            if (parv < 0) *reinterpret_cast<float2*>(st + kRawMetaV + j * 8) = __ldg(meta_of(code0, 1) + r0 + j);
+          }
+          park = max(park, 0);
+          parv = max(parv, 0);
+        }
+        if (lane == 0) *reinterpret_cast<uint32_t*>(st + kRawHdr) = code0 | (park << 8) | (parv << 9);
+      } else {
+        // ---- general tile: per-token table, one copy per run ----
+        const uint64_t starts = spread_bits(even_starts) | (spread_bits(odd_starts) << 1);
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int j = 2 * lane + e;
+          const int cd = code[e];
+          uint32_t raw_off = 0, moff[2] = {0, 0};
+          if (cd == kCodeNew) {  // native current-chunk row: one 128-byte copy each for K and V
+            raw_off = j * 128;
+            mbar_expect_tx(rbar, 256);
+            bulk_g2s(sst + kRawK + raw_off, knew_g + static_cast<int64_t>(row[e]) * a.kt, 128, rbar);
+            bulk_g2s(sst + kRawV + raw_off, vnew_g + static_cast<int64_t>(row[e]) * a.vt, 128, rbar);
+          } else if (cd != 0) {
+            const int j0 = 63 - __clzll(starts & ((2ull << j) - 1));  // first token of j's run
+            const uint64_t after = starts & ~((2ull << j0) - 1);
+            const int cnt = (after ? __ffsll(static_cast<long long>(after)) - 1 : kBN) - j0;
+            const int rb = row_bytes(cd);
+            const int r0 = row[e] - (j - j0);  // pool row of the run's first token
+            raw_off = j0 * 128 + (j - j0) * rb;
+            if (j == j0) {
+              mbar_expect_tx(rbar, 2 * cnt * rb);
+              bulk_g2s(sst + kRawK + j0 * 128, pool_of(cd, 0) + static_cast<int64_t>(r0) * rb, cnt * rb, rbar);
+              bulk_g2s(sst + kRawV + j0 * 128, pool_of(cd, 1) + static_cast<int64_t>(r0) * rb, cnt * rb, rbar);
+            }
+            if (cd != 16) {
+#pragma unroll
+              for (int kv = 0; kv < 2; ++kv) {
+                const int cap = cd == 4 ? cap4 : cap8;
+                const int pb = mpar_of(cd, kv);
+                const int end = r0 + cnt;
+                const bool bulk = cnt >= 2 && end + (pb ^ (end & 1)) <= cap;
+                const int par = bulk ? (pb ^ (r0 & 1)) : 0;
+                moff[kv] = j0 * 16 + (par + (j - j0)) * 8;
+                if (bulk && j == j0) {
+                  meta_run(cd, kv, r0, cnt, sst + (kv ? kRawMetaV : kRawMetaK) + j0 * 16, rbar);
+                } else if (!bulk) {  // short or block-final odd run: this token's pair by a plain load
+                  *reinterpret_cast<float2*>(st + (kv ? kRawMetaV : kRawMetaK) + moff[kv]) =
+                      __ldg(meta_of(cd, kv) + row[e]);
+                }
+              }
+            }
+          }
+          reinterpret_cast<uint2*>(st + kRawTab)[j] = make_uint2(cd | (raw_off << 8), moff[0] | (moff[1] << 16));
+        }
+        if (lane == 0) *reinterpret_cast<uint32_t*>(st + kRawHdr) = 0u;
+      }
+      __threadfence_block();  // table entries / fallback pairs stored by every lane ...
+      __syncwarp();           // ... are ordered before lane 0's release-arrive
+      if (lane == 0) mbar_arrive(rbar);
+      // the map slot is free again: start the copy of tile i + kMapStages into it
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0 && i + kMapStages < ntiles) map_tile(i + kMapStages);
+    }
+    if (!ok && lane == 0) {
+      *abort_flag = 1;
+      report(a.status, DKV_ETIMEOUT, 3);
+    }
+  } else if (warp >= kConvWarp0) {
+    // ================= converters: raw runs -> swizzled bf16 K / V tiles =================
+    const int ctid = tid - kConvWarp0 * 32;
+    const int c = ctid & 7;    // 8-dim part
+    const int jb = ctid >> 3;  // tokens jb + 16 k
+    bool ok = true;
+    for (int i = 0; i < ntiles; ++i) {
+      const int rs = i % kRawStages;
+      const int s = i % kStages;
+      ok = mbar_wait(bar(B_RAWFULL + rs), (i / kRawStages) & 1, kWaitCycles);
+      if (ok && i >= kStages) ok = mbar_wait(bar(B_EMPTY + s), ((i / kStages) + 1) & 1, kWaitCycles);
+      if (!ok || *abort_flag) break;
+      const uint8_t* st = smem + kOffRaw + rs * kRawStage;
+      uint8_t* dstK = smem + kOffK + s * kTile;
+      uint8_t* dstV = smem + kOffV + s * kTile;
+      const uint32_t hdr = *reinterpret_cast<const uint32_t*>(st + kRawHdr);
+      const int ucode = hdr & 0xff;
+      if (ucode == 16) {
+        convert_uniform<16>(st, dstK, dstV, jb, c, hdr);
+      } else if (ucode == 8) {
+        convert_uniform<8>(st, dstK, dstV, jb, c, hdr);
+      } else if (ucode == 4) {
+        convert_uniform<4>(st, dstK, dstV, jb, c, hdr);
+      } else {
+      // general tile: gather every operand of this thread's 8 (token, K|V) parts first, then convert
+      uint2 ent[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) ent[k] = reinterpret_cast<const uint2*>(st + kRawTab)[jb + 16 * k];
+      uint4 raw[8];
+      float2 mt[8];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int code = ent[k].x & 0xff;
+        const int raw_off = ent[k].x >> 8;
+#pragma unroll
+        for (int kv = 0; kv < 2; ++kv) {
+          const uint8_t* rrow = st + (kv ? kRawV : kRawK) + raw_off;
+          const int q = 2 * k + kv;
+          raw[q] = make_uint4(0, 0, 0, 0);
+          mt[q] = make_float2(0.f, 0.f);
+          if (code == 16 || code == kCodeNew) {
+            raw[q] = *reinterpret_cast<const uint4*>(rrow + c * 16);
+          } else if (code == 8) {
+            const uint2 w = *reinterpret_cast<const uint2*>(rrow + c * 8);
+            raw[q].x = w.x;
+            raw[q].y = w.y;
+          } else if (code == 4) {
+            raw[q].x = *reinterpret_cast<const uint32_t*>(rrow + c * 4);
+          }
+          if (code == 4 || code == 8) {
+            const int meta_off = kv ? (ent[k].y >> 16) : (ent[k].y & 0xffff);
+            mt[q] = *reinterpret_cast<const float2*>(st + (kv ? kRawMetaV : kRawMetaK) + meta_off);
+          }
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int code = ent[k].x & 0xff;
+        const int j = jb + 16 * k;
+#pragma unroll
+        for (int kv = 0; kv < 2; ++kv) {
+          const int q = 2 * k + kv;
+          uint4 v = raw[q];
+          if (code == 8 || code == 4) {
+            // codes -> exact floats via 2^23 + code, then code * scale + offset as one
+            // packed FMA per pair (the single rounding of a fused multiply-add)
+            uint32_t b0, b1;  // byte j of b0 / b1 = element 2j / 2j+1 (int4) or j / j+4 (int8)
+            if (code == 8) {
+              b0 = raw[q].x;
+              b1 = raw[q].y;
+            } else {
+              b0 = raw[q].x & 0x0F0F0F0Fu;
+              b1 = (raw[q].x >> 4) & 0x0F0F0F0Fu;
+            }
+            const float2 sc = make_float2(mt[q].y, mt[q].y);
+            const float2 of = make_float2(mt[q].x, mt[q].x);
+            const float2 mag = make_float2(-8388608.f, -8388608.f);
+            uint32_t out[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              uint32_t lo, hi;  // elements (2e, 2e+1) in dim order
+              if (code == 8) {
+                const uint32_t w = e < 2 ? b0 : b1;
+                lo = __byte_perm(w, 0x4B000000u, 0x7540 | (2 * (e & 1)));
+                hi = __byte_perm(w, 0x4B000000u, 0x7540 | (2 * (e & 1) + 1));
+              } else {
+                lo = __byte_perm(b0, 0x4B000000u, 0x7540 | e);
+                hi = __byte_perm(b1, 0x4B000000u, 0x7540 | e);
+              }
+              const float2 qf = add2(make_float2(__uint_as_float(lo), __uint_as_float(hi)), mag);
+              const float2 x = fma2(qf, sc, of);
+              out[e] = pack_bf16x2(x.x, x.y);
+            }
+            v = make_uint4(out[0], out[1], out[2], out[3]);
+          } else if (code != 16 && code != kCodeNew) {
+            v = make_uint4(0, 0, 0, 0);
+          }
+          *reinterpret_cast<uint4*>(smem + (kv ? kOffV : kOffK) + s * kTile + swz(j, c)) = v;
+        }
+      }
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(bar(B_FULL + s));
+      mbar_arrive(bar(B_RAWEMPTY + rs));
+    }
+    if (!ok) {
+      *abort_flag = 1;
+      report(a.status, DKV_ETIMEOUT, 4);
+    }
+  } else {
+    // ---- Q rows -> shared by cp.async (zeros past the last row), P zeroed, ones tile ----
+    pdl_wait();  // Q is the previous kernels' output; our output / workspace writes follow too
+    for (int i = tid; i < 2 * 128 * 8; i += kSoftmaxWarps * 32) {
+      const int r = i >> 3, c = i & 7;
+      const int off = (r >> 7) * 16384 + swz(r & 127, c);
+      if (r < rows_here) {
+        const int fr = row0 + r;
+        const int m = fr / a.G;
+        const int h = g * a.G + (fr - m * a.G);
+        cp_async16(sbase + kOffQ + off, a.q + h * a.qh + m * a.qt + c * 8);
+      } else {
+        *reinterpret_cast<uint4*>(smem + kOffQ + off) = make_uint4(0, 0, 0, 0);
+      }
+      *reinterpret_cast<uint4*>(smem + kOffP + off) = make_uint4(0, 0, 0, 0);
+    }
+    for (int i = tid; i < kTile / 16; i += kSoftmaxWarps * 32)  // bf16 1.0 everywhere
+      *reinterpret_cast<uint4*>(smem + kOffOnes + i * 16) =
+          make_uint4(0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u);
+    cp_async_commit();
+    cp_async_wait<0>();
+    fence_proxy_async_smem();
+    mbar_arrive(bar(B_QREADY));
+
     // ================= softmax (one TMEM lane / stacked row per thread) =================
+    // Scores stay in raw units; p = 2^(s*c - m*c) with c = D^-0.5 log2(e) folded
+    // into one FMA. The row sum comes from the tensor core (ones block of V).
     const int mt = warp >> 2, quad = warp & 3;
     const int rl = mt * 128 + quad * 32 + lane;  // row inside the block
     if (mt * 128 + quad * 32 < rows_here) {
       const int fr = row0 + min(rl, rows_here - 1);
       const int lim = a.past + fr / a.G;  // last key this row may see
       const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
-      float m_ref = -INFINITY, l = 0.f;
+      const uint32_t col_o = kColO + mt * 128;
+      constexpr float kStale = 8.f / kScaleLog2;  // 2^8 headroom, in raw score units
+      float m_raw = -INFINITY;
       bool ok = true;
       uint8_t* prow = smem + kOffP + mt * 16384;
       const int pr = quad * 32 + lane;
@@ -215,48 +687,51 @@ __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnA
         tc_fence_before();
         mbar_arrive(bar(B_SFREE + b));
         const int t0 = kb + i * kBN;
-        if (t0 + kBN <= ke && t0 + kBN - 1 <= a.past) {
-#pragma unroll
-          for (int j = 0; j < 64; ++j) s[j] *= kScaleLog2;
-        } else {
+        if (!(t0 + kBN <= ke && t0 + kBN - 1 <= a.past)) {  // boundary tile: mask
 #pragma unroll
           for (int j = 0; j < 64; ++j) {
             const int t = t0 + j;
-            s[j] = (t < ke && t <= lim) ? s[j] * kScaleLog2 : -INFINITY;
+            s[j] = (t < ke && t <= lim) ? s[j] : -INFINITY;
           }
         }
-        float mx = s[0];
+        float mx;
+        {  // 3-input max tree: depth 4 instead of a 63-long chain
+          float t[22], u[8];
 #pragma unroll
-        for (int j = 1; j < 64; ++j) mx = fmaxf(mx, s[j]);
+          for (int j = 0; j < 21; ++j) t[j] = max3f(s[3 * j], s[3 * j + 1], s[3 * j + 2]);
+          t[21] = s[63];
+#pragma unroll
+          for (int j = 0; j < 7; ++j) u[j] = max3f(t[3 * j], t[3 * j + 1], t[3 * j + 2]);
+          u[7] = t[21];
+          mx = max3f(max3f(u[0], u[1], u[2]), max3f(u[3], u[4], u[5]), fmaxf(u[6], u[7]));
+        }
         float alpha = 1.f;
         bool rescale = false;
-        if (mx > m_ref + 8.f) {  // also true for the first visible tile (m_ref = -inf)
-          alpha = ex2(m_ref - mx);
-          rescale = m_ref != -INFINITY;
-          m_ref = mx;
+        if (mx > m_raw + kStale) {  // also true for the first visible tile (m_raw = -inf)
+          alpha = ex2((m_raw - mx) * kScaleLog2);
+          rescale = m_raw != -INFINITY;
+          m_raw = mx;
         }
-        const float mu = m_ref == -INFINITY ? 0.f : m_ref;
+        const float mc = m_raw == -INFINITY ? 0.f : m_raw * kScaleLog2;
         uint32_t pk[32];
-        float sum = 0.f;
+        const float2 c2 = make_float2(kScaleLog2, kScaleLog2);
+        const float2 nm2 = make_float2(-mc, -mc);
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-          const float p0 = ex2(s[2 * j] - mu);
-          const float p1 = ex2(s[2 * j + 1] - mu);
-          sum += p0 + p1;
-          pk[j] = pack_bf16x2(p0, p1);
+          const float2 x = fma2(make_float2(s[2 * j], s[2 * j + 1]), c2, nm2);
+          pk[j] = pack_bf16x2(ex2(x.x), ex2(x.y));
         }
-        l = l * alpha + sum;
         if (i > 0) {  // P(i-1) consumed and O stable
           ok = __all_sync(0xffffffffu, mbar_wait(bar(B_ODONE), (i - 1) & 1, kWaitCycles));
           if (!ok) break;
         }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, rescale)) {
+        if (__any_sync(0xffffffffu, rescale)) {  // scale O and its row-sum columns
           const float f = rescale ? alpha : 1.f;
 #pragma unroll
-          for (int half = 0; half < 2; ++half) {
+          for (int part = 0; part < 3; ++part) {
             uint32_t o[32];
-            const uint32_t ta = lane_base + kColO + mt * 64 + half * 32;
+            const uint32_t ta = lane_base + col_o + part * 32;
             tmem_ld32(ta, o);
             tmem_wait_ld();
 #pragma unroll
@@ -273,8 +748,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnA
         tc_fence_before();
         mbar_arrive(bar(B_PFULL));
       }
-      // ---- epilogue: O row from TMEM ----
+      // ---- epilogue: O row and its sum of p from TMEM ----
       float o[64];
+      float l = 0.f;
 #pragma unroll
       for (int j = 0; j < 64; ++j) o[j] = 0.f;
       if (ok && ntiles > 0) {
@@ -282,19 +758,22 @@ __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnA
         tc_fence_after();
         if (ok) {
           uint32_t r0[32], r1[32];
-          tmem_ld32(lane_base + kColO + mt * 64, r0);
-          tmem_ld32(lane_base + kColO + mt * 64 + 32, r1);
+          tmem_ld32(lane_base + col_o, r0);
+          tmem_ld32(lane_base + col_o + 32, r1);
           tmem_wait_ld();
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             o[j] = __uint_as_float(r0[j]);
             o[32 + j] = __uint_as_float(r1[j]);
           }
+          tmem_ld32(lane_base + col_o + 64, r0);
+          tmem_wait_ld();
+          l = __uint_as_float(r0[0]);
         }
       }
       if (!ok) {
         *abort_flag = 1;
-        report(a.status, DKV_ETIMEOUT, 2);
+        report(a.status, DKV_ETIMEOUT, 5);
       } else if (rl < rows_here) {
         const int frow = row0 + rl;
         if (a.splits == 1) {
@@ -312,71 +791,20 @@ __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnA
             reinterpret_cast<uint4*>(dst)[c] = w;
           }
         } else {
+          // partial layout [cta][dim][row]: a warp's 32 rows are one coalesced 128-byte store per dim
           const int64_t cta = (static_cast<int64_t>(g) * a.mblocks + mb) * a.splits + split;
-          float4* dst = reinterpret_cast<float4*>(a.ws_o + (cta * kTcCtaRows + rl) * kDim);
+          float* dst = a.ws_o + cta * kDim * kTcCtaRows + rl;
 #pragma unroll
-          for (int c = 0; c < 16; ++c) dst[c] = make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
-          a.ws_ml[cta * kTcCtaRows + rl] = make_float2(m_ref, l);
+          for (int d = 0; d < kDim; ++d) dst[d * kTcCtaRows] = o[d];
+          a.ws_ml[cta * kTcCtaRows + rl] = make_float2(m_raw == -INFINITY ? -INFINITY : m_raw * kScaleLog2, l);
         }
       }
-    }
-  } else {
-    // ================= producers: gather, dequantise, stage K/V tiles =================
-    const int ptid = tid - kProdWarp0 * 32;
-    RowPart pre[kTasksPerProd];
-    auto load = [&](int tile) {
-      const int t0 = kb + tile * kBN;
-#pragma unroll
-      for (int i = 0; i < kTasksPerProd; ++i) {
-        const int task = ptid + i * kProdThreads;
-        const int kv = task >> 9;
-        const int j = (task >> 3) & (kBN - 1);
-        const int part = task & 7;
-        const int t = t0 + j;
-        pre[i].bits = 0;
-        if (t < ke) {
-          if (t < a.past) {
-            pre[i] = load_history_part(a.P, a.rows, a.codes, a.layer, kv, g, t, part, a.status);
-          } else {
-            const int tn = t - a.past;
-            const uint16_t* src = kv == 0 ? a.knew + g * a.kh + tn * a.kt : a.vnew + g * a.vh + tn * a.vt;
-            pre[i].raw = __ldg(reinterpret_cast<const uint4*>(src) + part);
-            pre[i].bits = 16;
-          }
-        }
-      }
-    };
-    bool ok = true;
-    if (ntiles > 0) load(0);
-    for (int i = 0; i < ntiles; ++i) {
-      const int s = i % kStages;
-      if (*abort_flag) { ok = false; break; }
-      if (i >= kStages) {
-        ok = mbar_wait(bar(B_EMPTY + s), ((i / kStages) + 1) & 1, kWaitCycles);
-        if (!ok) break;
-      }
-#pragma unroll
-      for (int k = 0; k < kTasksPerProd; ++k) {
-        const int task = ptid + k * kProdThreads;
-        const int kv = task >> 9;
-        const int j = (task >> 3) & (kBN - 1);
-        const int part = task & 7;
-        uint8_t* dst = smem + (kv == 0 ? kOffK : kOffV) + s * kTile + swz(j, part);
-        *reinterpret_cast<uint4*>(dst) = dequant_part(pre[k]);
-      }
-      fence_proxy_async_smem();
-      mbar_arrive(bar(B_FULL + s));
-      if (i + 1 < ntiles) load(i + 1);
-    }
-    if (!ok) {
-      *abort_flag = 1;
-      report(a.status, DKV_ETIMEOUT, 3);
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == kMmaWarp) {
+  if (warp == kSWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
@@ -395,9 +823,17 @@ cudaError_t launch_attention_tc(const AttnArgs& a, int heads, cudaStream_t strea
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
-  dim3 grid(a.splits, a.mblocks, heads);
-  attention_tc_kernel<<<grid, kThreadsTc, kSmemTc, stream>>>(a);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.splits, a.mblocks, heads);
+  cfg.blockDim = dim3(kThreadsTc);
+  cfg.dynamicSmemBytes = kSmemTc;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // overlap our set-up and
+  attr[0].val.programmaticStreamSerializationAllowed = 1;          // history streaming with the
+  cfg.attrs = attr;                                                 // previous kernel's tail
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, attention_tc_kernel, a);
 }
 
 }  // namespace dkv

@@ -67,6 +67,10 @@ int check_pools(const void* p4, const void* m4, const void* p8, const void* m8, 
 
 }  // namespace
 
+namespace dkv {
+int set_last_error(int code, const char* message) { return fail(code, "%s", message); }
+}  // namespace dkv
+
 extern "C" {
 
 int32_t dkv_version(void) { return DKV_VERSION; }

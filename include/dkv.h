@@ -106,6 +106,39 @@ int dkv_packed_attention(const void* q, const void* knew, const void* vnew,
 size_t dkv_packed_attention_workspace(int32_t past, int32_t nq, int32_t heads,
                                       int32_t group, int32_t dim);
 
+/* Size of the fixed scratch array inside libdkv.so used by
+ * dkv_packed_attention_noalloc (10 MiB: the largest workspace the attention
+ * planner can ask for, at most 148 split blocks of 256 rows). */
+#define DKV_NOALLOC_SCRATCH_BYTES (10u * 1024u * 1024u)
+
+/*
+ * dkv_packed_attention for callers that cannot allocate device memory. It has no
+ * counterpart in the reference (whose Triton kernel needs no scratch): it exists
+ * for callers such as embedders with a device-memory budget fixed up front, host
+ * runtimes whose own allocator forbids cudaMalloc on the hot path, or bindings
+ * without a device allocator at all. Same arguments and results as
+ * dkv_packed_attention without the workspace pair; the partial results of the
+ * history splits go to a DKV_NOALLOC_SCRATCH_BYTES array that lives in the
+ * library, so the call allocates nothing. Every GPU that loads the library holds
+ * that array until exit and all calls on a GPU share it: calls whose kernels
+ * overlap on one GPU (e.g. on two streams) race and must be serialised. Nothing
+ * in it needs clearing between calls. The first call on each device looks the
+ * array's device address up (cudaGetSymbolAddress); make that first call before
+ * any stream capture. Shapes needing more scratch than the array holds return
+ * DKV_EWORKSPACE (the planner never asks for more).
+ */
+int dkv_packed_attention_noalloc(const void* q, const void* knew, const void* vnew,
+                                 const void* p4, const void* m4, const void* p8,
+                                 const void* m8, const void* p16,
+                                 const int32_t* rows, const uint8_t* codes, void* out,
+                                 int64_t qh, int64_t qt, int64_t kh, int64_t kt,
+                                 int64_t vh, int64_t vt,
+                                 int32_t layer, int32_t past, int32_t nq,
+                                 int64_t cap4, int64_t cap8, int64_t cap16,
+                                 int32_t heads, int32_t group, int32_t dim,
+                                 int32_t block_m, int32_t block_n,
+                                 int32_t layers, int32_t* status, void* stream);
+
 /*
  * Dequantised bf16 history of one layer: out[2, heads, n, dim] (K then V) for
  * logical tokens [0, n). Replaces Triton `reconstruct` (src/gpu_kernels.py:

@@ -1,0 +1,77 @@
+"""The allocation-free attention entry point, called through the C ABI.
+
+dkv_packed_attention_noalloc serves callers that cannot allocate device memory
+on the hot path — a process that was handed a fixed device-memory budget up
+front, a host runtime whose allocator must not run while serving, or a binding
+with no device allocator at all. It keeps its split-history scratch in a fixed
+array inside libdkv.so instead of a caller-provided workspace. This file checks
+that two consecutive calls (different shapes, one per attention kernel, the
+second reusing the scratch the first left behind) give the same outputs as the
+regular entry point within the tolerance the attention tests use. It is named
+to run last, and builds everything it needs, so it also passes alone in a fresh
+process (where its first call performs the one-time scratch lookup).
+"""
+import ctypes
+
+import pytest
+import torch
+
+from dkv_testlib import assert_attention_close, frame_mix, outlier_kv
+
+pytestmark = pytest.mark.gpu
+
+
+def _bind(lib):
+    fn = lib.dkv_packed_attention_noalloc
+    P, I32, I64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64
+    fn.argtypes = ([P] * 11 + [I64] * 6 + [I32, I32, I32] + [I64, I64, I64] + [I32] * 6 + [P, P])
+    fn.restype = ctypes.c_int
+    return fn
+
+
+def _case(past, nq, seed):
+    from src.gpu_cache import GPUCache
+    gen = torch.Generator().manual_seed(seed)
+    outliers = torch.randperm(64, generator=gen)[:4]
+    frames = (past + 63) // 64
+    plan = [(b, 64) for b in frame_mix(seed, frames)]
+    plan[-1] = (plan[-1][0], past - 64 * (frames - 1))
+    cache = GPUCache(None, layers=1, heads=5)
+    hist_k, hist_v = outlier_kv(gen, 5, past, outliers)
+    start = 0
+    for f, (bits, n) in enumerate(plan):
+        cache.select(bits, f)
+        cache.append(hist_k[:, :, start:start + n].cuda(), hist_v[:, :, start:start + n].cuda(), 0)
+        start += n
+    q = torch.randn(1, 15, nq, 64, generator=gen).bfloat16().cuda()
+    kn, vn = (x.cuda() for x in outlier_kv(gen, 5, nq, outliers))
+    cache.select(16)
+    assert cache.append(kn, vn, 0) == past
+    return cache, q, kn, vn
+
+
+def _noalloc(fn, lib, cache, q, kn, vn, past):
+    nq = q.shape[2]
+    out = torch.empty((1, nq, 15, 64), dtype=torch.bfloat16, device=q.device)
+    rc = fn(q.data_ptr(), kn.data_ptr(), vn.data_ptr(), cache.p4.data_ptr(), cache.m4.data_ptr(),
+            cache.p8.data_ptr(), cache.m8.data_ptr(), cache.p16.data_ptr(), cache.rows.data_ptr(),
+            cache.codes.data_ptr(), out.data_ptr(), q.stride(1), q.stride(2), kn.stride(1), kn.stride(2),
+            vn.stride(1), vn.stride(2), 0, past, nq, cache.caps[4], cache.caps[8], cache.caps[16], 5, 3, 64,
+            16, 64, 1, cache.status.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, lib.dkv_last_error().decode()
+    return out
+
+
+def test_noalloc_entry_point_matches_workspace_entry_point_on_two_calls(cuda):
+    from src import gpu_kernels as K
+    fn = _bind(K.LIB)
+    # (8128 past, 64 queries): tensor-core kernel, 26 splits; (4096, 5): mma.sync kernel
+    cases = [(8128, 64, 11), (4096, 5, 12)]
+    built = [_case(*c) for c in cases]
+    assert all(K.attention_workspace_bytes(p, n, 5, 3) > 0 for p, n, _ in cases)  # both use scratch
+    expected = [c.attend(q, kn, vn, 0, p) for (c, q, kn, vn), (p, _, _) in zip(built, cases)]
+    got = [_noalloc(fn, K.LIB, c, q, kn, vn, p) for (c, q, kn, vn), (p, _, _) in zip(built, cases)]
+    torch.cuda.synchronize()
+    for (c, _, _, _), e, g in zip(built, expected, got):
+        c.check()
+        assert_attention_close(g, e, atol=0.01, rtol=0.01)

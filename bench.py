@@ -45,6 +45,9 @@ PAST, NQ, FRAME = 8128, 64, 64
 MIX = ([4, 8, 16], [0.5, 0.3, 0.2])
 ROW_BYTES = {4: 32 + 8, 8: 64 + 8, 16: 128}  # code bytes + (offset, scale) per row
 METRIC = 'packed-KV attention HBM GB/s at 8K ctx'
+# DRAM bytes (read + write) of attention_tc_kernel for one call of this shape,
+# from the ncu capture summarised in profiles/attention_tc_kernel_c3_8k.md.
+NCU_TRAFFIC_BYTES = 5_790_464
 WORKLOAD = 'C3 frame-append attention, 8K ctx, 32-layer cache'
 
 
@@ -371,7 +374,7 @@ def main():
         'e2e': {'value': e2e_value, 'unit': 'GB/s', 'h2d_bytes_per_step': h2d, 'd2h_bytes_per_step': d2h,
                 'ms_per_step': e2e_ms, 'api': 'GPUCache.attend with pinned-host q/k/v in, output out'},
         'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': hbm, 'unit': 'GB/s', 'frac': achieved / hbm,
-                     'traffic': None, 'peak_kind': peak_kind,
+                     'traffic': NCU_TRAFFIC_BYTES, 'peak_kind': peak_kind,
                      'bytes_per_launch': bytes_call, 'note': 'attention op (split kernel + combine) per layer call'},
         'roofline_tensor': {'bound': 'tensor', 'achieved': achieved_tf, 'peak': tflops, 'unit': 'TFLOP/s',
                             'frac': achieved_tf / tflops, 'peak_kind': peak_kind,

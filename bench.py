@@ -60,6 +60,9 @@ def parse():
     ap.add_argument('--cpu-seconds', type=float, default=12.0, help='CPU-baseline sample budget')
     ap.add_argument('--e2e-steps', type=int, default=30)
     ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--configs', default='c1,c2,c4,c5',
+                    help='extra BASELINE configurations reported in the same line (comma list, or "none")')
+    ap.add_argument('--c5-requests', type=int, default=64, help='C5 requests in total, split across ranks')
     ap.add_argument('--layers', type=int, default=LAYERS,
                     help='cache layers (the per-call workload is unchanged; fewer layers only shrink '
                          'the set-up for profiler captures)')
@@ -215,23 +218,125 @@ def run_reference(args, rank):
     print(json.dumps(line), flush=True)
 
 
+def bench_c1(seconds=2.0):
+    """C1: the reference CPU path, one layer, P = 1024 (16 frames of the 50/30/20 mix), fp32."""
+    import numpy as np
+    from oracle import cpu_path, pools
+    torch.set_num_threads(os.cpu_count())
+    gen = torch.Generator().manual_seed(1)
+    outliers = torch.randperm(DIM, generator=gen)[:4]
+    bits = random.Random(1).choices(MIX[0], weights=MIX[1], k=16)
+    frames = []
+    for b in bits:
+        k = torch.randn(1, HEADS, FRAME, DIM, generator=gen)
+        k[..., outliers] *= 8
+        v = torch.randn(1, HEADS, FRAME, DIM, generator=gen)
+        to_bits = lambda t: t.bfloat16().contiguous().view(torch.int16).numpy().view(np.uint16)
+        frames.append(pools.pack_frame(to_bits(k), to_bits(v), b))
+    q = torch.randn(1, HEADS * GROUP, NQ, DIM, generator=gen)
+    kn, vn = torch.randn(1, HEADS, NQ, DIM, generator=gen), torch.randn(1, HEADS, NQ, DIM, generator=gen)
+    cpu_path.cpu_cache_attention(frames, q, kn, vn)
+    calls, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        cpu_path.cpu_cache_attention(frames, q, kn, vn)
+        calls += 1
+    return {'ms_per_call': 1e3 * (time.perf_counter() - t0) / calls, 'cores': os.cpu_count(), 'past': 1024,
+            'what': 'reference CPU path (unpack + cat + SDPA), one layer, 64-token append'}
+
+
+def bench_c2(device):
+    """C2: pack sweep, 32 layers x 5 KV heads, 64-token frames appended one at a time from 0
+    to 8192 tokens at fixed 4 / 8 / 16 bits, pool growth included (as in the reference)."""
+    from src.gpu_cache import GPUCache
+    gen = torch.Generator(device=device).manual_seed(2)
+    k = torch.randn(LAYERS, 1, HEADS, FRAME, DIM, generator=gen, device=device).bfloat16()
+    v = torch.randn(LAYERS, 1, HEADS, FRAME, DIM, generator=gen, device=device).bfloat16()
+    out = {}
+    for bits in (4, 8, 16):
+        cache = GPUCache(None, layers=LAYERS, heads=HEADS, device=device)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(device)
+        start.record()
+        for f in range(8192 // FRAME):
+            cache.select(bits, f)
+            for layer in range(LAYERS):
+                cache.append(k[layer], v[layer], layer)
+        end.record()
+        torch.cuda.synchronize(device)
+        ms = start.elapsed_time(end)
+        launches = (8192 // FRAME) * LAYERS
+        out[str(bits)] = {'GB_per_s': launches * pack_bytes(bits) / (ms * 1e-3) / 1e9,
+                          'us_per_layer_append': 1e3 * ms / launches, 'final_cap': cache.caps[bits]}
+        cache.check()
+    return out
+
+
+def bench_c4(device):
+    """C4: candidate scoring over a 96-frame (6144-token) mixed 4/8/16 packed prefix with the
+    random-init SmolLM2-360M-shape decoder: 32-token question, 4 x 24-token candidates."""
+    from src.decoder import SMOLLM2_360M
+    from src.streaming import StreamingModel, bits_for, synthetic_request
+    model = StreamingModel(SMOLLM2_360M, device=device, seed=0)
+    embeds, question, cands = synthetic_request(SMOLLM2_360M, seed=4, frames=96, device=device)
+    cache = model.ingest(embeds, bits_for('dynamic', 96, seed=4), 'dynamic', qa_reserve=64)
+    model.answer(question, cands, cache)
+    torch.cuda.synchronize(device)
+    reps, t0 = 5, time.perf_counter()
+    for _ in range(reps):
+        ans = model.answer(question, cands, cache)
+    torch.cuda.synchronize(device)
+    return {'ms_per_4_candidates': 1e3 * (time.perf_counter() - t0) / reps, 'prefix_tokens': cache.seen[0],
+            'scores_mean_ll': ans['scores'], 'summed_ll': ans['summed'],
+            'note': 'wall time of StreamingModel.answer (4 forks x 32 layers, eager)'}, model
+
+
+def bench_c5(model, device, rank, world, total, dist):
+    """C5: `total` independent requests (64 frames x 64 tokens, dynamic 4/8/16, seed = request
+    id, then 4-candidate scoring) split across ranks; scores gathered with NCCL."""
+    import hashlib
+    from src.streaming import bits_for, synthetic_request
+    per = total // world
+    mine = range(rank * per, (rank + 1) * per)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    t0 = time.perf_counter()
+    scores = []
+    for r in mine:
+        embeds, question, cands = synthetic_request(model.cfg, seed=r, frames=64, device=device)
+        cache = model.ingest(embeds, bits_for('dynamic', 64, seed=r), 'dynamic', qa_reserve=64)
+        scores.append(model.answer(question, cands, cache)['scores'])
+    torch.cuda.synchronize(device)
+    secs = torch.tensor([time.perf_counter() - t0], device=device)
+    local = torch.tensor(scores, dtype=torch.float32, device=device)
+    if dist is not None:
+        dist.all_reduce(secs, op=dist.ReduceOp.MAX)
+        gathered = [torch.empty_like(local) for _ in range(world)]
+        dist.all_gather(gathered, local)
+        local = torch.cat(gathered)
+    all_scores = local.cpu().numpy()
+    return {'frame_append_tokens_per_s': per * world * 64 * 64 / float(secs.item()),
+            'requests': per * world, 'seconds': float(secs.item()), 'scaling': 'strong (fixed request set)',
+            'scores_sha256': hashlib.sha256(all_scores.tobytes()).hexdigest(),
+            'note': 'wall time incl. frame appends and scoring, eager; scores gathered with NCCL all_gather'}
+
+
 def main():
+    os.environ.setdefault('CUBLAS_WORKSPACE_CONFIG', ':4096:8')  # deterministic GEMMs for C5
     args = parse()
     world = int(os.environ.get('WORLD_SIZE', '1'))
     rank = int(os.environ.get('RANK', '0'))
     local = int(os.environ.get('LOCAL_RANK', '0'))
+    if args.impl == 'reference':  # CPU path on rank 0 only; other ranks leave at once
+        run_reference(args, rank)
+        return
     dist = None
     if world > 1:
         import torch.distributed as dist
+        os.environ['NCCL_DEBUG'] = 'WARN'  # keep stdout to the one JSON line
         torch.cuda.set_device(local)
         dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device('cuda', local))
-    if args.impl == 'reference':
-        run_reference(args, rank)
-        if dist is not None:
-            dist.barrier()
-            dist.destroy_process_group()
-        return
 
     device = torch.device('cuda', local)
     torch.cuda.set_device(device)
@@ -382,6 +487,18 @@ def main():
         'gpu_launches': args.steps * LAYERS * launches_per_call,
         'clocks': clock,
     }
+    configs = set() if args.configs == 'none' else set(args.configs.split(','))
+    if 'c2' in configs:
+        line['c2_pack_sweep'] = bench_c2(device)
+    model = None
+    if 'c4' in configs or 'c5' in configs:
+        c4, model = bench_c4(device)
+        if 'c4' in configs:
+            line['c4_candidate_scoring'] = c4
+    if 'c5' in configs:
+        line['c5_request_throughput'] = bench_c5(model, device, rank, world, args.c5_requests, dist)
+    if rank == 0 and 'c1' in configs:
+        line['c1_cpu_reference_path'] = bench_c1()
     if rank == 0 and not args.no_cpu_baseline:
         line['cpu_baseline'] = cpu_baseline(args.cpu_seconds)
     if rank == 0:

@@ -1,0 +1,134 @@
+"""Random-init Llama-style text decoder of the SmolLM2-360M shape.
+
+The reference runs the pretrained SmolVLM2 text model (HF LlamaModel) and routes
+its attention through GPUCache (src/gpu_cache.py:151-183); the checkpoint is not
+part of this build, so this module restates the decoder itself with random
+weights: 32 layers, hidden 960, 15 query / 5 KV heads of dim 64, SiLU MLP of
+width 2560, RMSNorm eps 1e-5, rotary embeddings (theta 100000), tied embeddings,
+bf16. Projections use the joined QKV and gate/up weights of the reference's fused
+mode (src/gpu_ops.py:26-47). With a GPUCache the attention is the packed-KV path
+(append + attend on the sm_100a kernels); with a NativeCache it is plain bf16
+history + SDPA (the reference's "native" mode).
+"""
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+
+from .gpu_cache import GPUCache
+from .gpu_ops import activation_product, cuda_rms
+
+
+@dataclass(frozen=True)
+class DecoderConfig:
+    layers: int = 32
+    hidden: int = 960
+    q_heads: int = 15
+    kv_heads: int = 5
+    head_dim: int = 64
+    intermediate: int = 2560
+    vocab: int = 49280
+    rms_eps: float = 1e-5
+    rope_theta: float = 100000.0
+    init_std: float = 0.02
+
+
+SMOLLM2_360M = DecoderConfig()
+
+
+class NativeCache:
+    """Unquantised bf16 history per layer (the reference's native DynamicCache mode)."""
+
+    def __init__(self, layers):
+        self.k = [None] * layers
+        self.v = [None] * layers
+
+    def get_seq_length(self, layer_idx=0):
+        return 0 if self.k[layer_idx] is None else self.k[layer_idx].shape[2]
+
+    def update(self, k, v, layer):
+        self.k[layer] = k if self.k[layer] is None else torch.cat((self.k[layer], k), 2)
+        self.v[layer] = v if self.v[layer] is None else torch.cat((self.v[layer], v), 2)
+        return self.k[layer], self.v[layer]
+
+    def fork(self):
+        other = NativeCache(len(self.k))
+        other.k, other.v = list(self.k), list(self.v)  # torch.cat never mutates: sharing is safe
+        return other
+
+
+def rope_tables(cfg, positions, device):
+    inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, cfg.head_dim, 2, device=device, dtype=torch.float32) / cfg.head_dim))
+    freqs = positions.float()[:, None] * inv[None, :]
+    emb = torch.cat((freqs, freqs), dim=-1)
+    return emb.cos(), emb.sin()
+
+
+def apply_rope(x, cos, sin):
+    """HF Llama rotate-half rotary embedding on [1, heads, n, d] (computed in fp32)."""
+    half = x.shape[-1] // 2
+    xf = x.float()
+    rot = torch.cat((-xf[..., half:], xf[..., :half]), dim=-1)
+    return (xf * cos + rot * sin).to(x.dtype)
+
+
+class Decoder(torch.nn.Module):
+    def __init__(self, cfg=SMOLLM2_360M, device='cuda', dtype=torch.bfloat16, seed=0):
+        super().__init__()
+        self.cfg = cfg
+        gen = torch.Generator(device='cpu').manual_seed(seed)
+
+        def w(*shape):
+            return torch.nn.Parameter((torch.randn(*shape, generator=gen) * cfg.init_std).to(dtype).to(device),
+                                      requires_grad=False)
+
+        qkv_out = (cfg.q_heads + 2 * cfg.kv_heads) * cfg.head_dim
+        self.embed = w(cfg.vocab, cfg.hidden)
+        self.qkv = torch.nn.ParameterList([w(qkv_out, cfg.hidden) for _ in range(cfg.layers)])
+        self.o = torch.nn.ParameterList([w(cfg.hidden, cfg.q_heads * cfg.head_dim) for _ in range(cfg.layers)])
+        self.gate_up = torch.nn.ParameterList([w(2 * cfg.intermediate, cfg.hidden) for _ in range(cfg.layers)])
+        self.down = torch.nn.ParameterList([w(cfg.hidden, cfg.intermediate) for _ in range(cfg.layers)])
+        ones = lambda: torch.nn.Parameter(torch.ones(cfg.hidden, dtype=dtype, device=device), requires_grad=False)
+        self.norm_attn = torch.nn.ParameterList([ones() for _ in range(cfg.layers)])
+        self.norm_mlp = torch.nn.ParameterList([ones() for _ in range(cfg.layers)])
+        self.norm_out = ones()
+
+    def rms(self, x, weight):
+        return cuda_rms(x, weight, self.cfg.rms_eps)
+
+    def attention(self, x, layer, cache, cos, sin):
+        c = self.cfg
+        n = x.shape[1]
+        q, k, v = F.linear(x, self.qkv[layer]).split(
+            [c.q_heads * c.head_dim, c.kv_heads * c.head_dim, c.kv_heads * c.head_dim], dim=-1)
+        q = q.view(1, n, c.q_heads, c.head_dim).transpose(1, 2)
+        k = k.view(1, n, c.kv_heads, c.head_dim).transpose(1, 2)
+        v = v.view(1, n, c.kv_heads, c.head_dim).transpose(1, 2)
+        q, k = apply_rope(q, cos, sin), apply_rope(k, cos, sin)
+        if isinstance(cache, GPUCache):
+            past = cache.append(k, v, layer)
+            out = cache.attend(q, k, v, layer, past)  # [1, n, q_heads, d]
+        else:
+            past = cache.get_seq_length(layer)
+            kk, vv = cache.update(k, v, layer)
+            mask = torch.arange(past + n, device=x.device)[None, :] <= past + torch.arange(n, device=x.device)[:, None]
+            out = F.scaled_dot_product_attention(q, kk, vv, attn_mask=mask, enable_gqa=True).transpose(1, 2)
+        return F.linear(out.reshape(1, n, -1), self.o[layer])
+
+    def forward(self, cache, ids=None, embeds=None, logits=0):
+        """Runs n new tokens (ids [1, n] or embeds [1, n, hidden]) through every layer,
+        appending their K/V to `cache`; returns fp32 logits of the last `logits`
+        positions (or None)."""
+        x = self.embed[ids] if embeds is None else embeds
+        n = x.shape[1]
+        past = cache.get_seq_length(0)
+        cos, sin = rope_tables(self.cfg, torch.arange(past, past + n, device=x.device), x.device)
+        for layer in range(self.cfg.layers):
+            x = x + self.attention(self.rms(x, self.norm_attn[layer]), layer, cache, cos, sin)
+            h = self.rms(x, self.norm_mlp[layer])
+            gate, up = F.linear(h, self.gate_up[layer]).chunk(2, dim=-1)
+            x = x + F.linear(activation_product(gate, up), self.down[layer])
+        if not logits:
+            return None
+        h = self.rms(x[:, -logits:], self.norm_out)
+        return F.linear(h, self.embed).float()

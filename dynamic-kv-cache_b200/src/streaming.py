@@ -1,0 +1,106 @@
+"""Streaming engine over the packed-KV cache: frame appends and candidate scoring.
+
+Mirrors the cache-facing part of the reference engine (src/streaming.py):
+create_cache (:155-165) builds a GPUCache (online plan, bf16) or a native cache;
+ingest (:168-187) appends a prefix and then one frame at a time with the frame's
+precision selected on the cache, and reserves the QA rows; answer with the
+"candidate" protocol (:209-225) scores every candidate on a fork of the video
+cache by its mean token log-likelihood (the reference's score) — the summed
+log-likelihood is returned as well. Video decoding and the vision tower are not
+part of this path: a frame arrives as its 64 visual-token embeddings.
+
+bits_for restates the --mode switch of benchmarks/gpu_evaluate.py:23-31. The
+reference's "dynamic"/"original" modes run an OpenCV feature policy on real video;
+here they draw each frame's precision from a seeded categorical over {4, 8, 16}
+(default weights 0.5 / 0.3 / 0.2), as the benchmark configurations specify.
+"""
+import random
+
+import torch
+
+from .decoder import SMOLLM2_360M, Decoder, NativeCache
+from .gpu_cache import GPUCache
+
+MODES = ['native', 'fused16', '8', '4', 'dynamic', 'original', 'random']
+# configs/gpu_selected.json:181-185 of the reference ("random" mode weights)
+RANDOM_PROBABILITIES = [0.6834782608695652, 0.2991304347826087, 0.017391304347826087]
+DYNAMIC_PROBABILITIES = [0.5, 0.3, 0.2]
+
+
+def bits_for(mode, frames, seed=0):
+    """Per-frame storage precision for --mode (benchmarks/gpu_evaluate.py:23-31)."""
+    if mode not in MODES:
+        raise ValueError(f'mode must be one of {MODES}')
+    if mode in ('native', 'fused16'):
+        return [16] * frames
+    if mode in ('4', '8'):
+        return [int(mode)] * frames
+    weights = RANDOM_PROBABILITIES if mode == 'random' else DYNAMIC_PROBABILITIES
+    return random.Random(seed).choices([4, 8, 16], weights=weights, k=frames)
+
+
+class StreamingModel:
+    def __init__(self, cfg=SMOLLM2_360M, device='cuda', seed=0, prefix_tokens=11):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.model = Decoder(cfg, device=device, seed=seed)
+        gen = torch.Generator().manual_seed(seed + 1)
+        self.prefix_ids = torch.randint(0, cfg.vocab, (1, prefix_tokens), generator=gen).to(self.device)
+
+    def create_cache(self, frame_lengths, mode, qa_reserve=192, max_tokens=8192):
+        """GPUCache with an online plan (or a native cache for mode 'native'),
+        checking the context limit like src/streaming.py:159-163."""
+        if mode == 'native':
+            return NativeCache(self.cfg.layers)
+        total = self.prefix_ids.shape[1] + sum(frame_lengths) + qa_reserve
+        if total > max_tokens:
+            raise ValueError('Context exceeds the checkpoint limit')
+        return GPUCache(None, layers=self.cfg.layers, heads=self.cfg.kv_heads, dim=self.cfg.head_dim,
+                        device=self.device, max_tokens=max_tokens)
+
+    @torch.inference_mode()
+    def ingest(self, frames, bits, mode, qa_reserve=192):
+        """Appends the prefix, then each frame ([1, n, hidden] embeddings) at its
+        precision; returns the cache (src/streaming.py:168-187)."""
+        cache = self.create_cache([f.shape[1] for f in frames], mode, qa_reserve)
+        self.model(cache, ids=self.prefix_ids)
+        for i, (emb, bit) in enumerate(zip(frames, bits)):
+            if isinstance(cache, GPUCache):
+                cache.select(bit, i)
+            self.model(cache, embeds=emb)
+        if isinstance(cache, GPUCache):
+            cache.select(16, -1)
+            cache.reserve(16, cache.host_counts[16] + qa_reserve)
+            if len(set(cache.seen)) != 1:
+                raise RuntimeError('Decoder layers disagree about the cache length')
+        return cache
+
+    @torch.inference_mode()
+    def answer(self, question_ids, candidate_ids, cache):
+        """Candidate protocol (src/streaming.py:209-225): per candidate, a fork of
+        the cache sees question + candidate; the score is the mean log-likelihood
+        of the candidate tokens. Returns scores (mean), summed log-likelihoods and
+        the argmax."""
+        means, sums = [], []
+        for answer_ids in candidate_ids:
+            ids = torch.cat((question_ids, answer_ids), dim=1)
+            fork = cache.fork()
+            logits = self.model(fork, ids=ids, logits=answer_ids.shape[1] + 1)
+            ll = logits[0, :-1].log_softmax(-1).gather(1, answer_ids[0][:, None])[:, 0]
+            means.append(ll.mean())
+            sums.append(ll.sum())
+        means, sums = torch.stack(means), torch.stack(sums)
+        values = means.tolist()
+        return dict(scores=values, summed=sums.tolist(), prediction=max(range(len(values)), key=values.__getitem__))
+
+
+def synthetic_request(cfg, seed, frames=64, frame_tokens=64, question_tokens=32, candidates=4,
+                      candidate_tokens=24, device='cuda'):
+    """Seeded stand-in for one video QA request: frame embeddings scaled like the
+    decoder's token embeddings, question and candidate token ids."""
+    gen = torch.Generator().manual_seed(10_000 + seed)
+    embeds = [(torch.randn(1, frame_tokens, cfg.hidden, generator=gen) * cfg.init_std).to(torch.bfloat16).to(device)
+              for _ in range(frames)]
+    question = torch.randint(0, cfg.vocab, (1, question_tokens), generator=gen).to(device)
+    cands = [torch.randint(0, cfg.vocab, (1, candidate_tokens), generator=gen).to(device) for _ in range(candidates)]
+    return embeds, question, cands

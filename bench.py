@@ -459,7 +459,7 @@ def main():
     cache.check()
 
     from src import gpu_kernels as K
-    launches_per_call = 2 if K.attention_workspace_bytes(PAST, NQ, HEADS, GROUP) else 1
+    launches_per_call = K.attention_launches(PAST, NQ, HEADS, GROUP)
     hbm, tflops, peak_kind = measured_peaks()
     achieved = bytes_call / (us_call * 1e-6) / 1e9
     achieved_tf = attention_flops() / (us_call * 1e-6) / 1e12
@@ -480,7 +480,7 @@ def main():
                 'ms_per_step': e2e_ms, 'api': 'GPUCache.attend with pinned-host q/k/v in, output out'},
         'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': hbm, 'unit': 'GB/s', 'frac': achieved / hbm,
                      'traffic': NCU_TRAFFIC_BYTES, 'peak_kind': peak_kind,
-                     'bytes_per_launch': bytes_call, 'note': 'attention op (split kernel + combine) per layer call'},
+                     'bytes_per_launch': bytes_call, 'note': 'attention op per layer call (tensor-core kernel with in-kernel split merge)'},
         'roofline_tensor': {'bound': 'tensor', 'achieved': achieved_tf, 'peak': tflops, 'unit': 'TFLOP/s',
                             'frac': achieved_tf / tflops, 'peak_kind': peak_kind,
                             'flops_per_launch': attention_flops()},

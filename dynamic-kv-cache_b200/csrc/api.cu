@@ -101,8 +101,16 @@ int dkv_pack_rows(const void* k, const void* v, void* p4, void* m4, void* p8, vo
 
 size_t dkv_packed_attention_workspace(int32_t past, int32_t nq, int32_t heads, int32_t group, int32_t dim) {
   if (past < 0 || nq <= 0 || heads <= 0 || group <= 0 || dim != dkv::kDim) return 0;
+  return dkv::make_plan(past, nq, heads, group).workspace_bytes();
+}
+
+int32_t dkv_packed_attention_launches(int32_t past, int32_t nq, int32_t heads, int32_t group, int32_t dim) {
+  if (past < 0 || nq <= 0 || heads <= 0 || group <= 0 || dim != dkv::kDim) return 0;
   const dkv::AttnPlan p = dkv::make_plan(past, nq, heads, group);
-  return p.ws_o_bytes + p.ws_ml_bytes;
+  if (p.splits == 1) return 1;
+  bool fused = false;
+  if (p.tc && dkv::attention_tc_merges_in_kernel(p, heads, &fused) != cudaSuccess) return -1;
+  return fused ? 1 : 2;
 }
 
 int dkv_packed_attention(const void* q, const void* knew, const void* vnew, const void* p4, const void* m4,
@@ -127,9 +135,11 @@ int dkv_packed_attention(const void* q, const void* knew, const void* vnew, cons
     return fail(DKV_EINVAL, "q/k/v rows must be 16-byte aligned (head/token strides multiples of 8)");
   if (out == nullptr || !aligned16(out)) return fail(DKV_EINVAL, "out must be 16-byte aligned");
   const dkv::AttnPlan p = dkv::make_plan(past, nq, heads, group);
-  const size_t need = p.ws_o_bytes + p.ws_ml_bytes;
-  if (need > 0 && (workspace == nullptr || workspace_bytes < need || !aligned16(workspace)))
+  const size_t need = p.workspace_bytes();
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need))
     return fail(DKV_EWORKSPACE, "attention workspace needs %zu bytes, got %zu", need, workspace_bytes);
+  if (need > 0 && (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return fail(DKV_EWORKSPACE, "attention workspace must be 256-byte aligned");
   dkv::AttnArgs a{};
   a.q = static_cast<const uint16_t*>(q);
   a.knew = static_cast<const uint16_t*>(knew);
@@ -157,12 +167,16 @@ int dkv_packed_attention(const void* q, const void* knew, const void* vnew, cons
   a.mblocks = p.mblocks;
   a.splits = p.splits;
   a.chunk = p.chunk;
-  a.ws_o = static_cast<float*>(workspace);
-  a.ws_ml = need > 0 ? reinterpret_cast<float2*>(static_cast<uint8_t*>(workspace) + p.ws_o_bytes) : nullptr;
+  if (need > 0) {  // [merge counters][partial outputs][partial (max, sum)]
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    a.sync = reinterpret_cast<uint32_t*>(ws);
+    a.ws_o = reinterpret_cast<float*>(ws + dkv::kSyncBytes);
+    a.ws_ml = reinterpret_cast<float2*>(ws + dkv::kSyncBytes + p.ws_o_bytes);
+  }
   a.status = status;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e = p.tc ? dkv::launch_attention_tc(a, heads, st) : dkv::launch_attention_split(a, heads, st);
-  if (e == cudaSuccess && p.splits > 1) e = dkv::launch_attention_combine(a, heads, st);
+  if (e == cudaSuccess && p.splits > 1 && !a.fused) e = dkv::launch_attention_combine(a, heads, st);
   return cuda_status(e, "packed_attention launch");
 }
 

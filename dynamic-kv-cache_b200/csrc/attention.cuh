@@ -13,6 +13,12 @@ constexpr int kTargetCtas = 148;        // one wave on a B200 (148 SMs)
 // D^-0.5 * log2(e): the reference scales scores by D^-0.5 (src/gpu_kernels.py:95)
 // and uses exp; the kernels work in the exp2 domain with the factor folded in.
 constexpr float kScaleLog2 = 0.125f * 1.4426950408889634f;
+// Head of the workspace: per (KV head, row block) group an arrival and a departure
+// counter for the in-kernel split merge. Zero before a workspace's first use; every
+// call returns them to zero. A split plan never has more than 74 groups (>= 2 splits
+// per group out of 148 CTAs), so 128 slots of each suffice.
+constexpr int kSyncGroups = 128;
+constexpr size_t kSyncBytes = 2 * kSyncGroups * sizeof(uint32_t);
 
 // Work decomposition of one attention call. Deterministic in (past, nq, heads,
 // group): no dependence on the device, so results are bit-identical across GPUs.
@@ -24,6 +30,7 @@ struct AttnPlan {
   int splits;    // history splits per (head, row block)
   int chunk;     // keys per split, multiple of kBN
   size_t ws_o_bytes, ws_ml_bytes;
+  size_t workspace_bytes() const { return splits > 1 ? kSyncBytes + ws_o_bytes + ws_ml_bytes : 0; }
 };
 
 inline AttnPlan make_plan(int past, int nq, int heads, int group) {
@@ -48,7 +55,7 @@ inline AttnPlan make_plan(int past, int nq, int heads, int group) {
   if (p.splits > 1) {
     const size_t ctas = static_cast<size_t>(heads) * p.mblocks * p.splits;
     p.ws_o_bytes = ctas * p.cta_rows * kDim * sizeof(float);
-    p.ws_ml_bytes = ctas * p.cta_rows * sizeof(float2);
+    p.ws_ml_bytes = ctas * p.cta_rows * sizeof(float2) + sizeof(float2) * p.cta_rows * heads * p.mblocks;  // even split count
   }
   return p;
 }
@@ -64,13 +71,72 @@ struct AttnArgs {
   int64_t qh, qt, kh, kt, vh, vt;
   int layer, past, nq, G, HQ;
   int mrows, cta_rows, mblocks, splits, chunk;
-  float* ws_o;    // [heads][mblocks][splits][cta_rows][64] unnormalised partial outputs
-  float2* ws_ml;  // [heads][mblocks][splits][cta_rows] (running max in log2 units, sum)
+  float* ws_o;    // [heads * mblocks][cta_rows][splits][64] unnormalised partial outputs
+  float2* ws_ml;  // [heads * mblocks][cta_rows][even(splits)] (running max in log2 units, sum)
+  uint32_t* sync;  // [2][kSyncGroups] arrival / departure counters of the in-kernel merge
+  int fused;       // 1: the attention kernel merges the splits itself (no combine launch)
   int32_t* status;
 };
 
+// Partials of group grp (= KV head * mblocks + row block): for each row, every
+// split's 64 outputs side by side, so the splits of a run of rows are one
+// contiguous block; the (max, sum) pairs likewise, with the split count rounded
+// up to even so that a run of rows starts on a 16-byte boundary.
+__host__ __device__ __forceinline__ int even_splits(int splits) { return splits + (splits & 1); }
+__host__ __device__ __forceinline__ int64_t part_o(int grp, int row, int cta_rows, int splits, int sp) {
+  return ((static_cast<int64_t>(grp) * cta_rows + row) * splits + sp) * kDim;
+}
+__host__ __device__ __forceinline__ int64_t part_ml(int grp, int row, int cta_rows, int splits, int sp) {
+  return (static_cast<int64_t>(grp) * cta_rows + row) * even_splits(splits) + sp;
+}
+
+// Split merge of one (row, dim), shared by the in-kernel merge and the combine
+// kernel so both give bit-identical results: M = max of the split maxima, weights
+// w_s = 2^(m_s - M) (0 for an empty split), out = (sum_s w_s o_s) / (sum_s w_s l_s),
+// both sums as fused multiply-adds in split order.
+__device__ __forceinline__ float merge_weight(float m, float M) { return m == -INFINITY ? 0.f : exp2f(m - M); }
+
+// One warp: the merge weights of one row. load(sp) returns split sp's (max, sum)
+// of the row (called by lane sp % 32, at most twice per split). Writes w_s to
+// w[s] and l_s to l[s] (shared memory); returns, in lane 0, the denominator
+// sum_s w_s l_s as fused multiply-adds in split order.
+template <class Load>
+__device__ __forceinline__ float merge_row_weights(Load load, int splits, float* w, float* l, int lane) {
+  const float2 first = lane < splits ? load(lane) : make_float2(-INFINITY, 0.f);
+  float M = first.x;
+  for (int sp = lane + 32; sp < splits; sp += 32) M = fmaxf(M, load(sp).x);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+  for (int sp = lane; sp < splits; sp += 32) {
+    const float2 v = sp == lane ? first : load(sp);
+    w[sp] = merge_weight(v.x, M);
+    l[sp] = v.y;
+  }
+  __syncwarp();
+  float den = 0.f;
+  if (lane == 0) {
+    for (int s0 = 0; s0 < splits; s0 += 8) {
+      float wv[8], lv[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        wv[u] = s0 + u < splits ? w[s0 + u] : 0.f;
+        lv[u] = s0 + u < splits ? l[s0 + u] : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (s0 + u < splits) den = __fmaf_rn(wv[u], lv[u], den);
+    }
+  }
+  return den;
+}
+
 cudaError_t launch_attention_split(const AttnArgs& a, int heads, cudaStream_t stream);
-cudaError_t launch_attention_tc(const AttnArgs& a, int heads, cudaStream_t stream);
+// Sets a.fused when every CTA of the grid can be resident at once (one CTA per SM):
+// the split merge then runs inside the kernel and no combine launch follows.
+cudaError_t launch_attention_tc(AttnArgs& a, int heads, cudaStream_t stream);
+// Whether a call with this plan merges its splits inside the tensor-core kernel
+// on the current device (one launch) or needs the combine kernel (two).
+cudaError_t attention_tc_merges_in_kernel(const AttnPlan& p, int heads, bool* fused);
 cudaError_t launch_attention_combine(const AttnArgs& a, int heads, cudaStream_t stream);
 
 }  // namespace dkv

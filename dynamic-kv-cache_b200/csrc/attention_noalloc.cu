@@ -12,8 +12,10 @@
 //
 // The array is a file-scope __device__ object: every GPU that loads the library
 // holds these bytes until the process exits, and every call on that GPU shares
-// them. Nothing in the array needs to start at zero: each call writes every
-// partial it later reads. Two calls whose kernels overlap on the same GPU (for
+// them. Its head holds the split-merge counters, which must be zero when a call
+// starts: static storage starts zeroed and every call leaves them zero again.
+// The partials behind them need no clearing: each call writes every partial it
+// later reads. Two calls whose kernels overlap on the same GPU (for
 // example on two streams) would race on the array; issue them one after the
 // other, as the regular entry point's one-stream rule already asks.
 #include <atomic>
@@ -27,11 +29,14 @@ int set_last_error(int code, const char* message);  // api.cu: the dkv_last_erro
 
 namespace {
 
-// Upper bound of dkv_packed_attention_workspace() over all shapes: the planner
-// never launches more than 148 split CTAs (fewer splits -> no workspace), each
-// with at most 256 rows x (64 fp32 outputs + (max, sum)) = 67,584 bytes.
+// Upper bound of dkv_packed_attention_workspace() over all shapes: the merge
+// counters plus at most 148 split CTAs (fewer splits -> no workspace), each with
+// at most 256 rows x (64 fp32 outputs + (max, sum)) = 67,584 bytes, plus one
+// padding (max, sum) column per row of each of at most 74 groups.
 constexpr size_t kScratchBytes = DKV_NOALLOC_SCRATCH_BYTES;
-static_assert(static_cast<size_t>(dkv::kTargetCtas) * dkv::kTcCtaRows * (dkv::kDim * 4 + 8) <= kScratchBytes,
+static_assert(dkv::kSyncBytes + static_cast<size_t>(dkv::kTargetCtas) * dkv::kTcCtaRows * (dkv::kDim * 4 + 8) +
+                      static_cast<size_t>(dkv::kTargetCtas / 2) * dkv::kTcCtaRows * 8 <=
+                  kScratchBytes,
               "static scratch smaller than the planner's largest workspace");
 
 static __device__ __align__(256) unsigned char g_scratch[kScratchBytes];

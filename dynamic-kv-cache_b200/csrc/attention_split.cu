@@ -273,87 +273,61 @@ attention_split_kernel(const AttnArgs a) {
     }
     return;
   }
-  // partial layout [cta][dim][row], shared with the tensor-core kernel
-  const int64_t cta = (static_cast<int64_t>(g) * a.mblocks + mb) * a.splits + split;
-  float* base = a.ws_o + cta * kDim * a.cta_rows;
+  // partial layout of part_o / part_ml, shared with the tensor-core kernel
+  const int grp = g * a.mblocks + mb;
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
     const int r = half ? rb : ra;
+    float* base = a.ws_o + part_o(grp, r, a.cta_rows, a.splits, split);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      base[(8 * j + c2) * a.cta_rows + r] = o[j][2 * half];
-      base[(8 * j + c2 + 1) * a.cta_rows + r] = o[j][2 * half + 1];
-    }
+    for (int j = 0; j < 8; ++j)
+      *reinterpret_cast<float2*>(base + 8 * j + c2) = make_float2(o[j][2 * half], o[j][2 * half + 1]);
     if ((lane & 3) == 0)
-      a.ws_ml[cta * a.cta_rows + r] = half ? make_float2(m_b, l_b) : make_float2(m_a, l_a);
+      a.ws_ml[part_ml(grp, r, a.cta_rows, a.splits, split)] = half ? make_float2(m_b, l_b) : make_float2(m_a, l_a);
   }
 }
 
-// Merges the split partials of each (KV head, row) in split order (fixed order:
-// deterministic). One thread per (row, dim): warps read 32 consecutive rows of one
-// dim (coalesced in the [cta][dim][row] partial layout); the block's 32 x 8 tile
-// is transposed through shared memory so the bf16 output leaves as 16-byte rows.
+// Merges the split partials of 4 (KV head, row) pairs per block when the
+// attention kernel did not merge them itself, with the in-kernel merge's
+// arithmetic (merge_row_weights, then the fused multiply-add chain in split
+// order): the same bits either way. A warp per row finds the weights; then one
+// thread per (row, dim) sums its column, 16 partial loads in flight at a time,
+// and stores its bf16 output (a warp writes 64 contiguous bytes).
 __global__ void __launch_bounds__(256) attention_combine_kernel(const AttnArgs a) {
-  __shared__ float tile[8][33];
+  __shared__ float s_w[4 * kTargetCtas], s_l[4 * kTargetCtas], s_den[4];
   ptx::pdl_wait();  // partials of the attention grid
   ptx::pdl_trigger();
   const int g = blockIdx.z;
-  const int lane = threadIdx.x & 31;
-  const int dl = threadIdx.x >> 5;       // dim within the block's 8
-  const int d = blockIdx.y * 8 + dl;
-  const int fr = blockIdx.x * 32 + lane;
-  float val = 0.f;
-  if (fr < a.mrows) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int fr0 = blockIdx.x * 4;
+  if (warp < 4 && fr0 + warp < a.mrows) {
+    const int fr = fr0 + warp;
     const int mb = fr / a.cta_rows;
-    const int r = fr - mb * a.cta_rows;
-    const int64_t cta0 = (static_cast<int64_t>(g) * a.mblocks + mb) * a.splits;
-    // chunks of 16 splits: all 32 loads of a chunk are in flight together, and
-    // the chunk maxima rescale the running sums (fixed order: deterministic)
-    float mx = -INFINITY, den = 0.f, acc = 0.f;
-    for (int base = 0; base < a.splits; base += 16) {
-      float2 ml[16];
-      float o[16];
-#pragma unroll
-      for (int q = 0; q < 16; ++q) {
-        ml[q] = make_float2(-INFINITY, 0.f);
-        o[q] = 0.f;
-        if (base + q < a.splits) {
-          ml[q] = a.ws_ml[(cta0 + base + q) * a.cta_rows + r];
-          o[q] = a.ws_o[((cta0 + base + q) * kDim + d) * a.cta_rows + r];
-        }
-      }
-      float cm = mx;
-#pragma unroll
-      for (int q = 0; q < 16; ++q) cm = fmaxf(cm, ml[q].x);
-      if (cm == -INFINITY) continue;
-      const float keep = mx == -INFINITY ? 0.f : exp2f(mx - cm);
-      den *= keep;
-      acc *= keep;
-#pragma unroll
-      for (int q = 0; q < 16; ++q) {
-        const float wgt = ml[q].x == -INFINITY ? 0.f : exp2f(ml[q].x - cm);
-        den += wgt * ml[q].y;
-        acc += wgt * o[q];
-      }
-      mx = cm;
-    }
-    val = acc / den;
+    const float2* ml = a.ws_ml + part_ml(g * a.mblocks + mb, fr - mb * a.cta_rows, a.cta_rows, a.splits, 0);
+    const float den = merge_row_weights([&](int sp) { return ml[sp]; }, a.splits, s_w + warp * kTargetCtas,
+                                        s_l + warp * kTargetCtas, lane);
+    if (lane == 0) s_den[warp] = den;
   }
-  tile[dl][lane] = val;
   __syncthreads();
-  if (threadIdx.x < 32) {  // one thread per row: 8 dims = 16 bytes
-    const int row = blockIdx.x * 32 + threadIdx.x;
-    if (row < a.mrows) {
-      const int m = row / a.G;
-      const int h = g * a.G + (row - m * a.G);
-      uint4 w;
-      w.x = pack_bf16x2(tile[0][threadIdx.x], tile[1][threadIdx.x]);
-      w.y = pack_bf16x2(tile[2][threadIdx.x], tile[3][threadIdx.x]);
-      w.z = pack_bf16x2(tile[4][threadIdx.x], tile[5][threadIdx.x]);
-      w.w = pack_bf16x2(tile[6][threadIdx.x], tile[7][threadIdx.x]);
-      *reinterpret_cast<uint4*>(a.out + (static_cast<int64_t>(m) * a.HQ + h) * kDim + blockIdx.y * 8) = w;
-    }
+  const int rl = threadIdx.x >> 6, d = threadIdx.x & 63;
+  const int fr = fr0 + rl;
+  if (fr >= a.mrows) return;
+  const int mb = fr / a.cta_rows;
+  const float* src = a.ws_o + part_o(g * a.mblocks + mb, fr - mb * a.cta_rows, a.cta_rows, a.splits, 0) + d;
+  const int64_t sstride = kDim;
+  float acc = 0.f;
+  for (int s0 = 0; s0 < a.splits; s0 += 16) {
+    float x[16];
+#pragma unroll
+    for (int u = 0; u < 16; ++u) x[u] = s0 + u < a.splits ? __ldcg(src + (s0 + u) * sstride) : 0.f;
+#pragma unroll
+    for (int u = 0; u < 16; ++u)
+      if (s0 + u < a.splits) acc = __fmaf_rn(s_w[rl * kTargetCtas + s0 + u], x[u], acc);
   }
+  const float val = __fdiv_rn(acc, s_den[rl]);
+  const int m = fr / a.G;
+  const int h = g * a.G + (fr - m * a.G);
+  a.out[(static_cast<int64_t>(m) * a.HQ + h) * kDim + d] = static_cast<uint16_t>(pack_bf16x2(val, 0.f) & 0xffffu);
 }
 
 template <int NW>
@@ -386,7 +360,7 @@ cudaError_t launch_attention_split(const AttnArgs& a, int heads, cudaStream_t st
 
 cudaError_t launch_attention_combine(const AttnArgs& a, int heads, cudaStream_t stream) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((a.mrows + 31) / 32, kDim / 8, heads);
+  cfg.gridDim = dim3((a.mrows + 3) / 4, 1, heads);
   cfg.blockDim = dim3(256);
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];

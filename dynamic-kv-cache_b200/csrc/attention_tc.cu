@@ -27,6 +27,15 @@
 // split go to the workspace and are merged by the deterministic combine kernel.
 // Every mbarrier wait is bounded: a stalled pipeline reports DKV_ETIMEOUT in the
 // status word and the CTA exits after its MMAs drain and TMEM is freed.
+//
+// When the whole grid is resident at once (one CTA per SM, at most 148 CTAs), the
+// splits are merged in the same launch: each CTA publishes its partial, counts
+// itself in on its group's arrival counter and, once all splits of the group are
+// in, merges an equal slice of the group's rows from every split's partial. The
+// wait is bounded; the last CTA to leave resets the counters for the next call.
+#include <cstdlib>
+#include <cstring>
+
 #include "attention.cuh"
 #include "tc_ptx.cuh"
 
@@ -90,13 +99,20 @@ enum {
   B_QREADY = B_ODONE + 1,
   B_FINS = B_QREADY + 1,
   B_FINPV = B_FINS + 1,
-  B_COUNT = B_FINPV + 1
+  B_MERGE = B_FINPV + 1,                // split partials landed   (merge, TMA bytes)
+  B_COUNT = B_MERGE + 1
 };
 constexpr int kOffTmem = kOffBar + B_COUNT * 8;
 constexpr int kOffAbort = kOffTmem + 4;
 constexpr int kSmemTc = kOffAbort + 4 + 1024;  // + slack to align the base to 1024 B
 static_assert(kSmemTc <= 227 * 1024, "shared memory budget");
 constexpr long long kWaitCycles = 400000000LL;  // ~0.2 s: a healthy wait is microseconds
+
+constexpr int kMergePairs = kTcCtaRows + kTargetCtas;  // (split, row) pairs one CTA merges, at most
+static_assert(kMergePairs * kDim * 4 <= kOffBar - kOffK, "merge staging fits the operand and raw rings");
+// (row, split) pairs staged: at most kMergePairs + kTcCtaRows with the split count rounded up to even
+static_assert((kMergePairs + kTcCtaRows) * 8 + 2 * kMergePairs * 4 + kTcCtaRows * 4 <= 2 * 128 * 128,
+              "merge (max, sum) pairs, weights and denominators fit the Q region");
 
 constexpr uint32_t kIdescS = idesc_bf16(128, kBN, 0);    // S = Q K^T: B = K tile, K-major
 constexpr uint32_t kIdescPV = idesc_bf16(128, kNPV, 1);  // [O | l] = P [V | 1]: B MN-major, 2 N-atoms
@@ -194,6 +210,72 @@ __device__ __forceinline__ void convert_uniform(const uint8_t* st, uint8_t* dstK
   }
 }
 
+// Rows [r_begin, r_end) of group grp (rows counted from row0), merged from all
+// splits' partials and written to `out` (merge_row_weights, then the fused
+// multiply-add chain in split order: bit-identical to the combine kernel). The
+// rows' partials of every split and their (max, sum) pairs are two contiguous
+// blocks (part_o / part_ml layout): two TMA bulk copies bring them into the idle
+// operand rings; then a warp per row finds the weights and one thread per
+// (row, dim) sums its column from shared memory.
+__device__ __forceinline__ void merge_rows(const AttnArgs& a, int g, int grp, int row0, int r_begin, int r_end,
+                                           uint8_t* smem, int tid) {
+  const int nr = r_end - r_begin;
+  if (nr <= 0) return;
+  const uint32_t sbase = smem_addr(smem);
+  const uint32_t mbar = sbase + kOffBar + 8 * B_MERGE;
+  const int S = a.splits, Se = even_splits(S);
+  const uint32_t o_bytes = static_cast<uint32_t>(nr * S) * kDim * 4;
+  const uint32_t ml_bytes = static_cast<uint32_t>(nr * Se) * 8;
+  const float* s_o = reinterpret_cast<const float*>(smem + kOffK);                // [nr][S][64]
+  const float2* s_ml = reinterpret_cast<const float2*>(smem + kOffQ);             // [nr][Se]
+  float* s_w = reinterpret_cast<float*>(smem + kOffQ) + 2 * (kMergePairs + kTcCtaRows);  // [nr][S]
+  float* s_l = s_w + kMergePairs;                                                         // [nr][S]
+  float* s_den = s_l + kMergePairs;                                                       // [nr]
+  const int warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    fence_proxy_async_global();  // partials stored through the generic proxy, read by TMA
+    fence_proxy_async_smem();    // the rings were last read by generic loads
+    mbar_expect_tx(mbar, o_bytes + ml_bytes);
+    bulk_g2s(sbase + kOffK, a.ws_o + part_o(grp, r_begin, kTcCtaRows, S, 0), o_bytes, mbar);
+    bulk_g2s(sbase + kOffQ, a.ws_ml + part_ml(grp, r_begin, kTcCtaRows, S, 0), ml_bytes, mbar);
+    mbar_arrive(mbar);
+  }
+  if (!mbar_wait(mbar, 0, kWaitCycles)) {
+    report(a.status, DKV_ETIMEOUT, 7);
+    mbar_wait(mbar, 0, kWaitCycles);  // the copies still target this CTA's shared memory
+    return;
+  }
+  for (int r = warp; r < nr; r += kThreadsTc / 32) {
+    const float2* ml = s_ml + r * Se;
+    const float den = merge_row_weights([&](int sp) { return ml[sp]; }, S, s_w + r * S, s_l + r * S, lane);
+    if (lane == 0) s_den[r] = den;
+  }
+  __syncthreads();
+  for (int i = tid; i < nr * kDim; i += kThreadsTc) {
+    const int r = i >> 6, d = i & (kDim - 1);
+    const float* col = s_o + r * S * kDim + d;
+    const float* w = s_w + r * S;
+    float acc = 0.f;
+    for (int s0 = 0; s0 < S; s0 += 8) {
+      float wv[8], ov[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const bool in = s0 + u < S;
+        wv[u] = in ? w[s0 + u] : 0.f;
+        ov[u] = in ? col[(s0 + u) * kDim] : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (s0 + u < S) acc = __fmaf_rn(wv[u], ov[u], acc);
+    }
+    const float val = __fdiv_rn(acc, s_den[r]);
+    const int frow = row0 + r_begin + r;
+    const int m = frow / a.G;
+    const int h = g * a.G + (frow - m * a.G);
+    a.out[(static_cast<int64_t>(m) * a.HQ + h) * kDim + d] = static_cast<uint16_t>(pack_bf16x2(val, 0.f) & 0xffffu);
+  }
+}
+
 __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -239,6 +321,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnA
     mbar_init(bar(B_QREADY), kSoftmaxWarps * 32);
     mbar_init(bar(B_FINS), 1);
     mbar_init(bar(B_FINPV), 1);
+    mbar_init(bar(B_MERGE), 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
@@ -791,12 +874,14 @@ __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnA
             reinterpret_cast<uint4*>(dst)[c] = w;
           }
         } else {
-          // partial layout [cta][dim][row]: a warp's 32 rows are one coalesced 128-byte store per dim
-          const int64_t cta = (static_cast<int64_t>(g) * a.mblocks + mb) * a.splits + split;
-          float* dst = a.ws_o + cta * kDim * kTcCtaRows + rl;
+          // partial layout of part_o / part_ml: this split's 64 outputs of the row are 256
+          // contiguous bytes, stored as eight whole 32-byte sectors
+          const int grp = g * a.mblocks + mb;
+          float* dst = a.ws_o + part_o(grp, rl, kTcCtaRows, a.splits, split);
 #pragma unroll
-          for (int d = 0; d < kDim; ++d) dst[d * kTcCtaRows] = o[d];
-          a.ws_ml[cta * kTcCtaRows + rl] = make_float2(m_raw == -INFINITY ? -INFINITY : m_raw * kScaleLog2, l);
+          for (int c = 0; c < kDim / 8; ++c) st_global_v8(dst + 8 * c, o + 8 * c);
+          a.ws_ml[part_ml(grp, rl, kTcCtaRows, a.splits, split)] =
+              make_float2(m_raw == -INFINITY ? -INFINITY : m_raw * kScaleLog2, l);
         }
       }
     }
@@ -808,21 +893,108 @@ __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnA
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
+
+  // ================= in-kernel split merge =================
+  if (a.fused) {
+    // block coordinates re-read here so nothing stays live across the roles above
+    const int msplit = blockIdx.x, mrow0 = blockIdx.y * kTcCtaRows, mg = blockIdx.z;
+    const int mrows_here = min(kTcCtaRows, a.mrows - mrow0);
+    const int grp = mg * a.mblocks + blockIdx.y;
+    uint32_t* arrive = a.sync + grp;
+    uint32_t* depart = a.sync + kSyncGroups + grp;
+    // shared-memory base recomputed here: nothing from the roles above stays live
+    uint8_t* msmem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    volatile int* go = reinterpret_cast<volatile int*>(msmem + kOffP);  // P region: idle now
+    if (tid == 0) {
+      __threadfence();             // the partials this CTA stored before the barrier above ...
+      fence_proxy_async_global();  // (read back by TMA) ...
+      red_add_release(arrive, 1u);  // ... are visible to whoever sees this arrival
+      const long long start = clock64();
+      int ready = 1;
+      while (ld_acquire(arrive) < static_cast<uint32_t>(a.splits)) {
+        if (clock64() - start > kWaitCycles) {
+          ready = 0;
+          break;
+        }
+        __nanosleep(64);
+      }
+      if (!ready) report(a.status, DKV_ETIMEOUT, 6);
+      *go = ready;
+    }
+    __syncthreads();
+    if (*go) {
+      const int r_begin = msplit * mrows_here / a.splits;
+      const int r_end = (msplit + 1) * mrows_here / a.splits;
+      merge_rows(a, mg, grp, mrow0, r_begin, r_end, msmem, threadIdx.x);
+    }
+    __syncthreads();
+    // every CTA departs exactly once (also after a timeout): the last one out
+    // returns both counters to zero for the next call on this workspace
+    if (tid == 0 && atomicAdd(depart, 1u) == static_cast<uint32_t>(a.splits - 1)) {
+      atomicExch(arrive, 0u);
+      atomicExch(depart, 0u);
+    }
+  }
 }
 
 }  // namespace
 
-cudaError_t launch_attention_tc(const AttnArgs& a, int heads, cudaStream_t stream) {
-  static bool configured[64] = {};
-  int dev = 0;
+namespace {
+bool g_configured[64] = {};
+int g_resident[64] = {};  // CTAs of this kernel the device holds at once
+
+cudaError_t configure(int& dev) {
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (!configured[dev]) {
+  if (!g_configured[dev]) {
     e = cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemTc);
     if (e != cudaSuccess) return e;
-    configured[dev] = true;
+    int per_sm = 0, sms = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attention_tc_kernel, kThreadsTc, kSmemTc);
+    if (e != cudaSuccess) return e;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    g_resident[dev] = per_sm * sms;
+    g_configured[dev] = true;
   }
+  return cudaSuccess;
+}
+
+// DKV_ATTENTION_MERGE=combine keeps the split merge in the separate combine
+// kernel (for GPUs shared under MPS, where a grid may not be resident at once).
+bool merge_in_kernel_allowed() {
+  static const bool allowed = [] {
+    const char* v = getenv("DKV_ATTENTION_MERGE");
+    return !(v && strcmp(v, "combine") == 0);
+  }();
+  return allowed;
+}
+}  // namespace
+
+bool attention_tc_fused(const AttnPlan& p, int heads, int dev) {
+  // in-kernel merge only when no CTA of a group can wait for one that is not yet resident
+  const long long grid = static_cast<long long>(p.splits) * p.mblocks * heads;
+  return p.tc && p.splits > 1 && heads * p.mblocks <= kSyncGroups && grid <= g_resident[dev] &&
+         merge_in_kernel_allowed();
+}
+
+cudaError_t attention_tc_merges_in_kernel(const AttnPlan& p, int heads, bool* fused) {
+  int dev = 0;
+  const cudaError_t e = configure(dev);
+  *fused = e == cudaSuccess && attention_tc_fused(p, heads, dev);
+  return e;
+}
+
+cudaError_t launch_attention_tc(AttnArgs& a, int heads, cudaStream_t stream) {
+  int dev = 0;
+  cudaError_t e = configure(dev);
+  if (e != cudaSuccess) return e;
+  AttnPlan p{};
+  p.tc = 1;
+  p.splits = a.splits;
+  p.mblocks = a.mblocks;
+  a.fused = a.sync != nullptr && attention_tc_fused(p, heads, dev);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.splits, a.mblocks, heads);
   cfg.blockDim = dim3(kThreadsTc);

@@ -5,7 +5,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include "../../include/dkv.h"
+#include "dkv.h"
 
 namespace dkv {
 

@@ -223,6 +223,26 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
 // Blocks until the grids this grid depends on have completed and their memory is
 // visible; must precede every read of their output and every write that they
 // might still read (workspace reuse).
+// 32-byte global store (one whole L2 sector: no partial-sector fill); p 32-byte aligned.
+__device__ __forceinline__ void st_global_v8(float* p, const float* v) {
+  asm volatile("st.global.v8.f32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};\n" ::"l"(p), "f"(v[0]), "f"(v[1]), "f"(v[2]),
+               "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7])
+               : "memory");
+}
+
+// Orders this thread's generic-proxy global accesses with later async-proxy (TMA)
+// accesses of the same memory.
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;\n" ::: "memory"); }
+
+// Global-memory counter with release / acquire semantics at GPU scope.
+__device__ __forceinline__ void red_add_release(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
 // Lets the dependent grid be scheduled (its own pdl_wait still orders memory).
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }

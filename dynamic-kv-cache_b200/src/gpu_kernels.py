@@ -42,6 +42,7 @@ def _load():
                                   I32, I32, I32, I64, I64, I64, I32, I32, I32, I32, I32, I32,
                                   P, SZ, P, P], ctypes.c_int),
         'dkv_packed_attention_workspace': ([I32, I32, I32, I32, I32], SZ),
+        'dkv_packed_attention_launches': ([I32, I32, I32, I32, I32], I32),
         'dkv_reconstruct': ([P, P, P, P, P, P, P, P, I32, I32, I64, I64, I64, I32, I32, I32, P, P],
                             ctypes.c_int),
         'dkv_map_fill': ([P, P, I64, I32, I64, I32, I64, P], ctypes.c_int),
@@ -54,7 +55,7 @@ def _load():
 
 LIB = _load()
 EXPORTS = ('dkv_version', 'dkv_last_error', 'dkv_pack_rows', 'dkv_packed_attention',
-           'dkv_packed_attention_workspace', 'dkv_reconstruct', 'dkv_map_fill')
+           'dkv_packed_attention_workspace', 'dkv_packed_attention_launches', 'dkv_reconstruct', 'dkv_map_fill')
 
 
 def _check(rc):
@@ -95,11 +96,39 @@ def attention_workspace_bytes(past, nq, heads, group, dim=64):
     return LIB.dkv_packed_attention_workspace(past, nq, heads, group, dim)
 
 
+def attention_launches(past, nq, heads, group, dim=64):
+    """Kernel launches of one packed_attention call of this shape on the current device."""
+    n = LIB.dkv_packed_attention_launches(past, nq, heads, group, dim)
+    if n < 0:
+        raise RuntimeError(LIB.dkv_last_error().decode() or 'CUDA error')
+    return n
+
+
+# Attention workspaces, one per (device, stream): the library keeps the merge
+# counters at the head of a workspace zero between calls, so a workspace is
+# zero-filled once and reused; calls on one stream never overlap, calls on
+# different streams get different workspaces. Outgrown workspaces stay referenced
+# so that CUDA graphs captured with them keep valid addresses.
+_WORKSPACES = {}
+_RETIRED = []
+
+
+def _workspace(device, stream, size):
+    key = (device.index, stream)
+    ws = _WORKSPACES.get(key)
+    if ws is None or ws.numel() < size:
+        if ws is not None:
+            _RETIRED.append(ws)
+        ws = torch.zeros(size, dtype=torch.uint8, device=device)
+        _WORKSPACES[key] = ws
+    return ws
+
+
 def packed_attention(q, knew, vnew, p4, m4, p8, m8, p16, rows, codes, out, layer, past, nq, cap4, cap8,
                      cap16, heads, group, dim, block_m, block_n, layers, status=None):
     q, knew, vnew = _rows_ready(q), _rows_ready(knew), _rows_ready(vnew)
     size = attention_workspace_bytes(past, nq, heads, group, dim)
-    workspace = torch.empty(size, dtype=torch.uint8, device=q.device) if size else None
+    workspace = _workspace(q.device, _stream(q), size) if size else None
     _check(LIB.dkv_packed_attention(
         _ptr(q), _ptr(knew), _ptr(vnew), _ptr(p4), _ptr(m4), _ptr(p8), _ptr(m8), _ptr(p16), _ptr(rows),
         _ptr(codes), _ptr(out), q.stride(1), q.stride(2), knew.stride(1), knew.stride(2),

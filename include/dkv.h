@@ -87,7 +87,19 @@ int dkv_pack_rows(const void* k, const void* v,
  * dim] contiguous. Query m sees keys t <= past + m. block_m / block_n are the
  * reference's tile knobs: validated (powers of two, 16..256) but the kernel picks
  * its own B200 tiling. `workspace` must hold dkv_packed_attention_workspace()
- * bytes (it may be NULL when that size is 0).
+ * bytes, 256-byte aligned (it may be NULL when that size is 0). Its first 1024 bytes are the
+ * split-merge arrival counters: they must be zero before the first call that
+ * uses the workspace, and every call leaves them zero again (also when a
+ * pipeline wait times out), so a workspace is zero-filled once and then reused.
+ * A workspace belongs to one call at a time: calls that may overlap (different
+ * streams) need different workspaces.
+ *
+ * When every block of the launch fits on the GPU at once (one block per SM, at
+ * most 148 blocks) the history splits are merged inside the attention kernel:
+ * one launch per call. Otherwise, or with the environment variable
+ * DKV_ATTENTION_MERGE=combine (e.g. under MPS, where a grid may not be resident
+ * at once), a second kernel merges them. Both merges do the same arithmetic in
+ * the same order: the output is bit-identical either way.
  */
 int dkv_packed_attention(const void* q, const void* knew, const void* vnew,
                          const void* p4, const void* m4, const void* p8,
@@ -104,6 +116,12 @@ int dkv_packed_attention(const void* q, const void* knew, const void* vnew,
 
 /* Workspace bytes dkv_packed_attention needs for this shape (0 = none). */
 size_t dkv_packed_attention_workspace(int32_t past, int32_t nq, int32_t heads,
+                                      int32_t group, int32_t dim);
+
+/* Kernel launches one dkv_packed_attention call of this shape makes on the
+ * current device (1 or 2; 0 for invalid shapes, -1 on a CUDA error). No
+ * reference counterpart: it lets callers and benchmarks count launches. */
+int32_t dkv_packed_attention_launches(int32_t past, int32_t nq, int32_t heads,
                                       int32_t group, int32_t dim);
 
 /* Size of the fixed scratch array inside libdkv.so used by

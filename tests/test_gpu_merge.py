@@ -1,0 +1,38 @@
+"""The split merge: inside the tensor-core kernel when the grid is resident at
+once, otherwise (or with DKV_ATTENTION_MERGE=combine) in the combine kernel. Both
+must give the same bits, and the workspace's arrival counters must be back at
+zero after every call."""
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+from dkv_merge_cases import CASES, run_case
+
+pytestmark = pytest.mark.gpu
+
+
+def test_in_kernel_merge_is_bit_identical_to_combine_kernel(cuda, tmp_path):
+    path = tmp_path / 'combine.npz'
+    env = dict(os.environ, DKV_ATTENTION_MERGE='combine')
+    script = os.path.join(os.path.dirname(__file__), 'dkv_merge_cases.py')
+    subprocess.run([sys.executable, script, str(path)], env=env, check=True, timeout=600)
+    ref = np.load(path)
+    for i, case in enumerate(CASES):
+        out, launches = run_case(*case)
+        assert launches == 1, case  # 148-SM B200: every planned grid is resident at once
+        assert int(ref[f'launches{i}']) == 2, case
+        assert np.array_equal(out.view(torch.int16).cpu().numpy(), ref[f'out{i}']), case
+
+
+def test_merge_counters_return_to_zero(cuda):
+    from src import gpu_kernels as K
+    for case in CASES[:3]:
+        run_case(*case)
+        run_case(*case, seed=1)
+    torch.cuda.synchronize()
+    ws = K._WORKSPACES[(torch.cuda.current_device(), torch.cuda.current_stream().cuda_stream)]
+    assert int(ws[:1024].count_nonzero()) == 0

@@ -16,12 +16,16 @@
 //               pairs) into a 4-deep raw ring with one TMA bulk copy per run;
 //   warps 12-15 converters: dequantise a raw tile in registers into bf16 K and V
 //               tiles (64 keys) of a 3-stage ring, 128B-swizzled for the tensor core;
-//   warp 8      S issuer (one thread): S = Q K^T into TMEM, double-buffered;
-//   warp 9      PV issuer (one thread): [O | l] += P [V | 1] into TMEM; the block
-//               of ones makes the tensor core accumulate the softmax denominator;
+//   warp 8      S issuer (one thread): S = Q K^T into TMEM, double-buffered, with Q
+//               held in TMEM; an S buffer is reused as soon as the softmax has read it;
+//   warp 9      PV issuer (one thread): O += P V into TMEM with P read from TMEM;
 //   warps 0-7   softmax: one TMEM lane = one stacked row each; read S, mask, online
-//               max and exp2 in fp32, write P (bf16) to shared memory, and rescale
-//               O in TMEM when the running max moves.
+//               max and exp2 in fp32, the row sum of p in fp32 registers, write P
+//               (bf16 pairs) into TMEM once the previous P V product has landed, and
+//               rescale O in TMEM when the running max moves.
+// Both products read their A operand from tensor memory: shared memory carries
+// only the K and V tiles (2 KB per MMA), so the tensor core is not held up by the
+// converters' and TMA's shared-memory traffic.
 // The running max is only moved when a tile's max exceeds it by more than 2^8
 // (p <= 256, exact after the final O / l division). Partial (max, sum, O) per
 // split go to the workspace and are merged by the deterministic combine kernel.
@@ -58,8 +62,9 @@ constexpr int kThreadsTc = (kConvWarp0 + kConvWarps) * 32;  // 512
 constexpr int kConvThreads = kConvWarps * 32;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0;    // S[buf][mt] at columns (buf * 2 + mt) * 64
-constexpr uint32_t kColO = 256;  // O[mt] at columns 256 + mt * 128: 64 output dims + 16 row-sum columns
-constexpr int kNPV = kDim + 16;  // P V product width: V plus a block of ones (sum of p per row)
+constexpr uint32_t kColO = 256;  // O[mt] (64 fp32) at columns 256 + mt * 64
+constexpr uint32_t kColP = 384;  // P[mt] (64 bf16 = 32 columns) at 384 + mt * 32
+constexpr uint32_t kColQ = 448;  // Q[mt] (64 bf16 = 32 columns) at 448 + mt * 32
 
 constexpr int kTile = kBN * 128;  // one 64-key bf16 tile, 8 KB
 // Raw stage: K rows, V rows (a run starting at token j0 is packed densely from
@@ -82,8 +87,7 @@ constexpr int kOffQ = 0;  // 2 M-tiles x 128 rows x 128 B
 constexpr int kOffP = kOffQ + 2 * 128 * 128;
 constexpr int kOffK = kOffP + 2 * 128 * 128;
 constexpr int kOffV = kOffK + kStages * kTile;
-constexpr int kOffOnes = kOffV + kStages * kTile;  // 64 x 64 bf16 ones: the second N-atom of every V tile
-constexpr int kOffRaw = kOffOnes + kTile;
+constexpr int kOffRaw = kOffV + kStages * kTile;
 constexpr int kOffMap = kOffRaw + kRawStages * kRawStage;
 constexpr int kOffBar = ((kOffMap + kMapStages * kMapStage + 15) / 16) * 16;
 enum {
@@ -92,10 +96,10 @@ enum {
   B_RAWFULL = B_EMPTY + kStages,        // raw stage landed       (loader + TMA bytes)
   B_RAWEMPTY = B_RAWFULL + kRawStages,  // raw stage consumed     (converters, 128)
   B_MAPFULL = B_RAWEMPTY + kRawStages,  // map stage landed       (loader + TMA bytes)
-  B_SFULL = B_MAPFULL + kMapStages,
-  B_SFREE = B_SFULL + 2,
-  B_PFULL = B_SFREE + 2,
-  B_ODONE = B_PFULL + 1,
+  B_SFULL = B_MAPFULL + kMapStages,    // S[b] computed            (S commit)
+  B_SFREE = B_SFULL + 2,                // S[b] read                (softmax threads)
+  B_PFULL = B_SFREE + 2,                // P written                (softmax threads)
+  B_ODONE = B_PFULL + 1,                // O updated, P consumed    (PV commit)
   B_QREADY = B_ODONE + 1,
   B_FINS = B_QREADY + 1,
   B_FINPV = B_FINS + 1,
@@ -115,7 +119,7 @@ static_assert((kMergePairs + kTcCtaRows) * 8 + 2 * kMergePairs * 4 + kTcCtaRows 
               "merge (max, sum) pairs, weights and denominators fit the Q region");
 
 constexpr uint32_t kIdescS = idesc_bf16(128, kBN, 0);    // S = Q K^T: B = K tile, K-major
-constexpr uint32_t kIdescPV = idesc_bf16(128, kNPV, 1);  // [O | l] = P [V | 1]: B MN-major, 2 N-atoms
+constexpr uint32_t kIdescPV = idesc_bf16(128, kDim, 1);  // O += P V: B (the V tile) MN-major
 
 constexpr int kCodeNew = 17;  // token of the current chunk: native row of knew / vnew
 
@@ -348,10 +352,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnA
         for (int mt = 0; mt < mt_count; ++mt) {
           const uint32_t d = tmem + kColS + (b * 2 + mt) * 64;
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const uint64_t ad = sw128_desc(sbase + kOffQ + mt * 16384 + k * 32, 16, 1024);
+          for (int k = 0; k < 4; ++k) {  // 16 dims per step = 8 TMEM columns of Q
             const uint64_t bd = sw128_desc(sbase + kOffK + s * kTile + k * 32, 16, 1024);
-            umma_f16(d, ad, bd, kIdescS, k > 0);
+            umma_f16_ts(d, tmem + kColQ + mt * 32 + k * 8, bd, kIdescS, k > 0);
           }
         }
         umma_commit(bar(B_SFULL + b));
@@ -373,15 +376,12 @@ __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnA
         if (!ok) break;
         tc_fence_after();
         const int s = i % kStages;
-        // the ones block sits at kOffOnes: LBO = its distance from this V tile
-        const uint32_t lbo = static_cast<uint32_t>(kOffOnes - (kOffV + s * kTile));
         for (int mt = 0; mt < mt_count; ++mt) {
-          const uint32_t d = tmem + kColO + mt * 128;
+          const uint32_t d = tmem + kColO + mt * 64;
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const uint64_t ad = sw128_desc(sbase + kOffP + mt * 16384 + k * 32, 16, 1024);
-            const uint64_t bd = sw128_desc(sbase + kOffV + s * kTile + k * 2048, lbo, 1024);
-            umma_f16(d, ad, bd, kIdescPV, (i > 0 || k > 0) ? 1u : 0u);
+          for (int k = 0; k < 4; ++k) {  // 16 keys per step = 8 TMEM columns of P
+            const uint64_t bd = sw128_desc(sbase + kOffV + s * kTile + k * 2048, kTile, 1024);
+            umma_f16_ts(d, tmem + kColP + mt * 32 + k * 8, bd, kIdescPV, (i > 0 || k > 0) ? 1u : 0u);
           }
         }
         umma_commit(bar(B_ODONE));
@@ -711,44 +711,52 @@ __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnA
       report(a.status, DKV_ETIMEOUT, 4);
     }
   } else {
-    // ---- Q rows -> shared by cp.async (zeros past the last row), P zeroed, ones tile ----
+    // ---- Q rows -> this thread's TMEM lane (zeros past the last row) ----
     pdl_wait();  // Q is the previous kernels' output; our output / workspace writes follow too
-    for (int i = tid; i < 2 * 128 * 8; i += kSoftmaxWarps * 32) {
-      const int r = i >> 3, c = i & 7;
-      const int off = (r >> 7) * 16384 + swz(r & 127, c);
-      if (r < rows_here) {
-        const int fr = row0 + r;
-        const int m = fr / a.G;
-        const int h = g * a.G + (fr - m * a.G);
-        cp_async16(sbase + kOffQ + off, a.q + h * a.qh + m * a.qt + c * 8);
-      } else {
-        *reinterpret_cast<uint4*>(smem + kOffQ + off) = make_uint4(0, 0, 0, 0);
+    {
+      const int qmt = warp >> 2, qquad = warp & 3;
+      const int qrl = qmt * 128 + qquad * 32 + lane;
+      if (qmt < mt_count) {
+        uint32_t qr[32];
+        if (qrl < rows_here) {
+          const int fr = row0 + qrl;
+          const int m = fr / a.G;
+          const int h = g * a.G + (fr - m * a.G);
+          const uint4* src = reinterpret_cast<const uint4*>(a.q + h * a.qh + m * a.qt);
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const uint4 v = src[c];
+            qr[4 * c] = v.x;
+            qr[4 * c + 1] = v.y;
+            qr[4 * c + 2] = v.z;
+            qr[4 * c + 3] = v.w;
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) qr[c] = 0u;
+        }
+        tmem_st32(tmem + (static_cast<uint32_t>(qquad * 32) << 16) + kColQ + qmt * 32, qr);
+        tmem_wait_st();
       }
-      *reinterpret_cast<uint4*>(smem + kOffP + off) = make_uint4(0, 0, 0, 0);
     }
-    for (int i = tid; i < kTile / 16; i += kSoftmaxWarps * 32)  // bf16 1.0 everywhere
-      *reinterpret_cast<uint4*>(smem + kOffOnes + i * 16) =
-          make_uint4(0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u);
-    cp_async_commit();
-    cp_async_wait<0>();
-    fence_proxy_async_smem();
+    tc_fence_before();
     mbar_arrive(bar(B_QREADY));
 
     // ================= softmax (one TMEM lane / stacked row per thread) =================
     // Scores stay in raw units; p = 2^(s*c - m*c) with c = D^-0.5 log2(e) folded
-    // into one FMA. The row sum comes from the tensor core (ones block of V).
+    // into one FMA. The row sum of p is accumulated in fp32 (before p is rounded to
+    // bf16 for the product), as the reference kernel does.
     const int mt = warp >> 2, quad = warp & 3;
     const int rl = mt * 128 + quad * 32 + lane;  // row inside the block
     if (mt * 128 + quad * 32 < rows_here) {
       const int fr = row0 + min(rl, rows_here - 1);
       const int lim = a.past + fr / a.G;  // last key this row may see
       const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
-      const uint32_t col_o = kColO + mt * 128;
+      const uint32_t col_o = kColO + mt * 64;
+      float l_run = 0.f;  // sum of p of this row, scaled like O
       constexpr float kStale = 8.f / kScaleLog2;  // 2^8 headroom, in raw score units
       float m_raw = -INFINITY;
       bool ok = true;
-      uint8_t* prow = smem + kOffP + mt * 16384;
-      const int pr = quad * 32 + lane;
       for (int i = 0; i < ntiles; ++i) {
         const int b = i & 1;
         if (__any_sync(0xffffffffu, *abort_flag != 0)) { ok = false; break; }
@@ -768,7 +776,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnA
           }
         }
         tc_fence_before();
-        mbar_arrive(bar(B_SFREE + b));
+        mbar_arrive(bar(B_SFREE + b));  // S[b] may be overwritten by S(i + 2)
         const int t0 = kb + i * kBN;
         if (!(t0 + kBN <= ke && t0 + kBN - 1 <= a.past)) {  // boundary tile: mask
 #pragma unroll
@@ -799,20 +807,30 @@ __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnA
         uint32_t pk[32];
         const float2 c2 = make_float2(kScaleLog2, kScaleLog2);
         const float2 nm2 = make_float2(-mc, -mc);
+        float2 ls[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           const float2 x = fma2(make_float2(s[2 * j], s[2 * j + 1]), c2, nm2);
-          pk[j] = pack_bf16x2(ex2(x.x), ex2(x.y));
+          const float2 e = make_float2(ex2(x.x), ex2(x.y));
+          ls[j & 3] = add2(ls[j & 3], e);
+          pk[j] = pack_bf16x2(e.x, e.y);
         }
-        if (i > 0) {  // P(i-1) consumed and O stable
+        {
+          const float2 t = add2(add2(ls[0], ls[1]), add2(ls[2], ls[3]));
+          l_run = fmaf(l_run, alpha, t.x + t.y);
+        }
+        // P(i-1) V has landed before this warp touches TMEM again: O is stable for a
+        // rescale and P(i-1) is consumed (a P store overlapping an in-flight P V
+        // product corrupted the rows of warps that ran ahead, even into other columns)
+        if (i > 0) {
           ok = __all_sync(0xffffffffu, mbar_wait(bar(B_ODONE), (i - 1) & 1, kWaitCycles));
           if (!ok) break;
+          tc_fence_after();
         }
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, rescale)) {  // scale O and its row-sum columns
+        if (__any_sync(0xffffffffu, rescale)) {  // scale O
           const float f = rescale ? alpha : 1.f;
 #pragma unroll
-          for (int part = 0; part < 3; ++part) {
+          for (int part = 0; part < 2; ++part) {
             uint32_t o[32];
             const uint32_t ta = lane_base + col_o + part * 32;
             tmem_ld32(ta, o);
@@ -823,15 +841,13 @@ __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnA
           }
           tmem_wait_st();
         }
-#pragma unroll
-        for (int c = 0; c < 8; ++c)
-          *reinterpret_cast<uint4*>(prow + swz(pr, c)) =
-              make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-        fence_proxy_async_smem();
+        // P (bf16 pairs, 32 columns): the A operand of P V
+        tmem_st32(lane_base + kColP + mt * 32, pk);
+        tmem_wait_st();
         tc_fence_before();
         mbar_arrive(bar(B_PFULL));
       }
-      // ---- epilogue: O row and its sum of p from TMEM ----
+      // ---- epilogue: O row from TMEM, its sum of p from registers ----
       float o[64];
       float l = 0.f;
 #pragma unroll
@@ -849,9 +865,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnA
             o[j] = __uint_as_float(r0[j]);
             o[32 + j] = __uint_as_float(r1[j]);
           }
-          tmem_ld32(lane_base + col_o + 64, r0);
-          tmem_wait_ld();
-          l = __uint_as_float(r0[0]);
+          l = l_run;
         }
       }
       if (!ok) {

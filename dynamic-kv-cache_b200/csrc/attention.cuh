@@ -97,36 +97,27 @@ __host__ __device__ __forceinline__ int64_t part_ml(int grp, int row, int cta_ro
 __device__ __forceinline__ float merge_weight(float m, float M) { return m == -INFINITY ? 0.f : exp2f(m - M); }
 
 // One warp: the merge weights of one row. load(sp) returns split sp's (max, sum)
-// of the row (called by lane sp % 32, at most twice per split). Writes w_s to
-// w[s] and l_s to l[s] (shared memory); returns, in lane 0, the denominator
-// sum_s w_s l_s as fused multiply-adds in split order.
+// of the row (called by lane sp % 32). Writes w_s to w[s] (shared memory) and
+// returns, in every lane, the denominator sum_s w_s l_s: each lane sums its splits
+// (lane, lane + 32, ...) with fused multiply-adds in split order, then the lanes'
+// sums are added in a fixed butterfly (xor 16, 8, 4, 2, 1) -- the same order in
+// every kernel that merges, so the results are bit-identical.
 template <class Load>
-__device__ __forceinline__ float merge_row_weights(Load load, int splits, float* w, float* l, int lane) {
+__device__ __forceinline__ float merge_row_weights(Load load, int splits, float* w, int lane) {
   const float2 first = lane < splits ? load(lane) : make_float2(-INFINITY, 0.f);
   float M = first.x;
   for (int sp = lane + 32; sp < splits; sp += 32) M = fmaxf(M, load(sp).x);
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+  float den = 0.f;
   for (int sp = lane; sp < splits; sp += 32) {
     const float2 v = sp == lane ? first : load(sp);
-    w[sp] = merge_weight(v.x, M);
-    l[sp] = v.y;
+    const float wv = merge_weight(v.x, M);
+    w[sp] = wv;
+    den = __fmaf_rn(wv, v.y, den);
   }
-  __syncwarp();
-  float den = 0.f;
-  if (lane == 0) {
-    for (int s0 = 0; s0 < splits; s0 += 8) {
-      float wv[8], lv[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        wv[u] = s0 + u < splits ? w[s0 + u] : 0.f;
-        lv[u] = s0 + u < splits ? l[s0 + u] : 0.f;
-      }
-#pragma unroll
-      for (int u = 0; u < 8; ++u)
-        if (s0 + u < splits) den = __fmaf_rn(wv[u], lv[u], den);
-    }
-  }
+  for (int off = 16; off > 0; off >>= 1) den = __fadd_rn(den, __shfl_xor_sync(0xffffffffu, den, off));
   return den;
 }
 

@@ -294,7 +294,7 @@ attention_split_kernel(const AttnArgs a) {
 // thread per (row, dim) sums its column, 16 partial loads in flight at a time,
 // and stores its bf16 output (a warp writes 64 contiguous bytes).
 __global__ void __launch_bounds__(256) attention_combine_kernel(const AttnArgs a) {
-  __shared__ float s_w[4 * kTargetCtas], s_l[4 * kTargetCtas], s_den[4];
+  __shared__ float s_w[4 * kTargetCtas], s_den[4];
   ptx::pdl_wait();  // partials of the attention grid
   ptx::pdl_trigger();
   const int g = blockIdx.z;
@@ -304,8 +304,7 @@ __global__ void __launch_bounds__(256) attention_combine_kernel(const AttnArgs a
     const int fr = fr0 + warp;
     const int mb = fr / a.cta_rows;
     const float2* ml = a.ws_ml + part_ml(g * a.mblocks + mb, fr - mb * a.cta_rows, a.cta_rows, a.splits, 0);
-    const float den = merge_row_weights([&](int sp) { return ml[sp]; }, a.splits, s_w + warp * kTargetCtas,
-                                        s_l + warp * kTargetCtas, lane);
+    const float den = merge_row_weights([&](int sp) { return ml[sp]; }, a.splits, s_w + warp * kTargetCtas, lane);
     if (lane == 0) s_den[warp] = den;
   }
   __syncthreads();
@@ -316,13 +315,22 @@ __global__ void __launch_bounds__(256) attention_combine_kernel(const AttnArgs a
   const float* src = a.ws_o + part_o(g * a.mblocks + mb, fr - mb * a.cta_rows, a.cta_rows, a.splits, 0) + d;
   const int64_t sstride = kDim;
   float acc = 0.f;
-  for (int s0 = 0; s0 < a.splits; s0 += 16) {
+  int sp = 0;
+  for (; sp + 16 <= a.splits; sp += 16) {  // whole batches: 16 loads in flight
     float x[16];
 #pragma unroll
-    for (int u = 0; u < 16; ++u) x[u] = s0 + u < a.splits ? __ldcg(src + (s0 + u) * sstride) : 0.f;
+    for (int u = 0; u < 16; ++u) x[u] = __ldcg(src + (sp + u) * sstride);
+#pragma unroll
+    for (int u = 0; u < 16; ++u) acc = __fmaf_rn(s_w[rl * kTargetCtas + sp + u], x[u], acc);
+  }
+  {
+    float x[16];
+    const int rem = a.splits - sp;
+#pragma unroll
+    for (int u = 0; u < 16; ++u) x[u] = u < rem ? __ldcg(src + (sp + u) * sstride) : 0.f;
 #pragma unroll
     for (int u = 0; u < 16; ++u)
-      if (s0 + u < a.splits) acc = __fmaf_rn(s_w[rl * kTargetCtas + s0 + u], x[u], acc);
+      if (u < rem) acc = __fmaf_rn(s_w[rl * kTargetCtas + sp + u], x[u], acc);
   }
   const float val = __fdiv_rn(acc, s_den[rl]);
   const int m = fr / a.G;

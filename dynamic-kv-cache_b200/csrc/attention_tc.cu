@@ -233,8 +233,7 @@ __device__ __forceinline__ void merge_rows(const AttnArgs& a, int g, int grp, in
   const float* s_o = reinterpret_cast<const float*>(smem + kOffK);                // [nr][S][64]
   const float2* s_ml = reinterpret_cast<const float2*>(smem + kOffQ);             // [nr][Se]
   float* s_w = reinterpret_cast<float*>(smem + kOffQ) + 2 * (kMergePairs + kTcCtaRows);  // [nr][S]
-  float* s_l = s_w + kMergePairs;                                                         // [nr][S]
-  float* s_den = s_l + kMergePairs;                                                       // [nr]
+  float* s_den = s_w + kMergePairs;                                                       // [nr]
   const int warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
     fence_proxy_async_global();  // partials stored through the generic proxy, read by TMA
@@ -251,7 +250,7 @@ __device__ __forceinline__ void merge_rows(const AttnArgs& a, int g, int grp, in
   }
   for (int r = warp; r < nr; r += kThreadsTc / 32) {
     const float2* ml = s_ml + r * Se;
-    const float den = merge_row_weights([&](int sp) { return ml[sp]; }, S, s_w + r * S, s_l + r * S, lane);
+    const float den = merge_row_weights([&](int sp) { return ml[sp]; }, S, s_w + r * S, lane);
     if (lane == 0) s_den[r] = den;
   }
   __syncthreads();
@@ -260,18 +259,18 @@ __device__ __forceinline__ void merge_rows(const AttnArgs& a, int g, int grp, in
     const float* col = s_o + r * S * kDim + d;
     const float* w = s_w + r * S;
     float acc = 0.f;
-    for (int s0 = 0; s0 < S; s0 += 8) {
+    int sp = 0;
+    for (; sp + 8 <= S; sp += 8) {  // whole batches: every load issued before the chain
       float wv[8], ov[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        const bool in = s0 + u < S;
-        wv[u] = in ? w[s0 + u] : 0.f;
-        ov[u] = in ? col[(s0 + u) * kDim] : 0.f;
+        wv[u] = w[sp + u];
+        ov[u] = col[(sp + u) * kDim];
       }
 #pragma unroll
-      for (int u = 0; u < 8; ++u)
-        if (s0 + u < S) acc = __fmaf_rn(wv[u], ov[u], acc);
+      for (int u = 0; u < 8; ++u) acc = __fmaf_rn(wv[u], ov[u], acc);
     }
+    for (; sp < S; ++sp) acc = __fmaf_rn(w[sp], col[sp * kDim], acc);
     const float val = __fdiv_rn(acc, s_den[r]);
     const int frow = row0 + r_begin + r;
     const int m = frow / a.G;
@@ -811,7 +810,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnA
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           const float2 x = fma2(make_float2(s[2 * j], s[2 * j + 1]), c2, nm2);
-          const float2 e = make_float2(ex2(x.x), ex2(x.y));
+          // one pair in four on the FMA / integer pipes: MUFU ex2 is the softmax's bottleneck
+          const float2 e = (j & 3) == 3 ? ex2_poly2(x) : make_float2(ex2(x.x), ex2(x.y));
           ls[j & 3] = add2(ls[j & 3], e);
           pk[j] = pack_bf16x2(e.x, e.y);
         }
@@ -920,9 +920,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnA
     uint8_t* msmem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     volatile int* go = reinterpret_cast<volatile int*>(msmem + kOffP);  // P region: idle now
     if (tid == 0) {
-      __threadfence();             // the partials this CTA stored before the barrier above ...
-      fence_proxy_async_global();  // (read back by TMA) ...
-      red_add_release(arrive, 1u);  // ... are visible to whoever sees this arrival
+      // release at GPU scope, cumulative over the partials every thread of this CTA
+      // stored before the barrier above: whoever acquires this arrival sees them
+      red_add_release(arrive, 1u);
       const long long start = clock64();
       int ready = 1;
       while (ld_acquire(arrive) < static_cast<uint32_t>(a.splits)) {

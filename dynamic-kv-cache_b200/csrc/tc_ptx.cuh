@@ -259,6 +259,24 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\
 // Lets the dependent grid be scheduled (its own pdl_wait still orders memory).
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
 
+// 2^x for a pair on the FMA and integer pipes (no MUFU): j = round(x) by the
+// 1.5 * 2^23 shift (round to nearest even), f = x - j (exact) in [-1/2, 1/2],
+// 2^f by a cubic fitted here to relative-minimax on [-1/2, 1/2] (max relative
+// error 7.5e-5, well under a bf16 half-ulp of 2^-9), then j added to the exponent
+// field. x is clamped at -126.5, so inputs below it (and -inf) give ~4.9e-39, not 0.
+__device__ __forceinline__ float2 ex2_poly2(float2 x) {
+  x.x = fmaxf(x.x, -126.5f);
+  x.y = fmaxf(x.y, -126.5f);
+  const float2 t = add2(x, make_float2(12582912.f, 12582912.f));
+  const float2 j = add2(t, make_float2(-12582912.f, -12582912.f));
+  const float2 f = fma2(j, make_float2(-1.f, -1.f), x);
+  float2 p = fma2(make_float2(0x1.c3f760p-5f, 0x1.c3f760p-5f), f, make_float2(0x1.f0de1cp-3f, 0x1.f0de1cp-3f));
+  p = fma2(p, f, make_float2(0x1.62f31ap-1f, 0x1.62f31ap-1f));
+  p = fma2(p, f, make_float2(0x1.fff692p-1f, 0x1.fff692p-1f));
+  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
+}
+
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));

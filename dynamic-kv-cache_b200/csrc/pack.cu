@@ -21,6 +21,11 @@ pack_rows_kernel(const uint16_t* __restrict__ k, const uint16_t* __restrict__ v,
                  float2* __restrict__ m8, uint16_t* __restrict__ p16, int64_t kh, int64_t kt,
                  int64_t vh, int64_t vt, int layer, int64_t row_start, int n, int64_t cap,
                  int heads, int32_t* status) {
+  // Launched as a programmatic dependent: the next kernel (the frame's attention,
+  // which reads the new K/V natively and only history rows of the pools) may start
+  // streaming history at once; k / v are the previous kernels' output.
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
   const int gtid = blockIdx.x * blockDim.x + threadIdx.x;
   const int row = gtid >> 3;
   const int part = gtid & 7;
@@ -130,16 +135,18 @@ cudaError_t launch_pack(const void* k, const void* v, void* p4, void* m4, void* 
   float2* s4 = static_cast<float2*>(m4);
   float2* s8 = static_cast<float2*>(m8);
   uint16_t* h = static_cast<uint16_t*>(p16);
-  if (bits == 4)
-    pack_rows_kernel<4><<<blocks, kPackThreads, 0, stream>>>(kk, vv, q4, s4, q8, s8, h, kh, kt, vh, vt,
-                                                            layer, row_start, n, cap, heads, status);
-  else if (bits == 8)
-    pack_rows_kernel<8><<<blocks, kPackThreads, 0, stream>>>(kk, vv, q4, s4, q8, s8, h, kh, kt, vh, vt,
-                                                            layer, row_start, n, cap, heads, status);
-  else
-    pack_rows_kernel<16><<<blocks, kPackThreads, 0, stream>>>(kk, vv, q4, s4, q8, s8, h, kh, kt, vh, vt,
-                                                             layer, row_start, n, cap, heads, status);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(blocks);
+  cfg.blockDim = dim3(kPackThreads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  auto kernel = bits == 4 ? pack_rows_kernel<4> : (bits == 8 ? pack_rows_kernel<8> : pack_rows_kernel<16>);
+  return cudaLaunchKernelEx(&cfg, kernel, kk, vv, q4, s4, q8, s8, h, kh, kt, vh, vt, layer, row_start, n, cap,
+                            heads, status);
 }
 
 cudaError_t launch_reconstruct(const Pools& P, const int32_t* rows, const uint8_t* codes, void* out,

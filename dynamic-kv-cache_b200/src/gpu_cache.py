@@ -107,7 +107,17 @@ class GPUCache(DynamicCache):
         (src/gpu_cache.py:68-94)."""
         if k.shape[0] != 1 or k.shape[-1] != self.dim or k.device.type != 'cuda':
             raise ValueError('GPU cache requires CUDA, batch one and the configured head dimension')
-        past, n = self.seen[layer], k.shape[-2]
+        past, n, row = self._claim(layer, k.shape[-2])
+        K.pack_rows(k, v, *self._pools(), layer, row, n, self.caps[4], self.caps[8], self.caps[16],
+                    self.heads, self.dim, self.pending_bits, self.layers, self.status)
+        self.seen[layer] = past + n
+        return past
+
+    def _claim(self, layer, n):
+        """Plan bookkeeping of an n-token append to `layer` at the selected precision
+        (src/gpu_cache.py:72-90): returns (past, n, first pool row); the caller
+        writes the rows and advances seen[layer]."""
+        past = self.seen[layer]
         if past + n > self.capacity:
             raise ValueError('GPU context limit exceeded')
         if self.online:
@@ -127,11 +137,7 @@ class GPUCache(DynamicCache):
         if segment is None or past + n > segment[1] or segment[2] != self.pending_bits:
             raise ValueError(f'Cache append does not match plan at token {past}, length {n}, '
                              f'bits {self.pending_bits}')
-        row = segment[3] + past - segment[0]
-        K.pack_rows(k, v, *self._pools(), layer, row, n, self.caps[4], self.caps[8], self.caps[16],
-                    self.heads, self.dim, self.pending_bits, self.layers, self.status)
-        self.seen[layer] = past + n
-        return past
+        return past, n, segment[3] + past - segment[0]
 
     def attend(self, q, k, v, layer, past):
         """Causal GQA attention of the n new queries over the packed history plus

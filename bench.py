@@ -280,14 +280,23 @@ def bench_c4(device):
     embeds, question, cands = synthetic_request(SMOLLM2_360M, seed=4, frames=96, device=device)
     cache = model.ingest(embeds, bits_for('dynamic', 96, seed=4), 'dynamic', qa_reserve=64)
     model.answer(question, cands, cache)
+    model.answer(question, cands, cache, batched=True)
     torch.cuda.synchronize(device)
     reps, t0 = 5, time.perf_counter()
     for _ in range(reps):
         ans = model.answer(question, cands, cache)
     torch.cuda.synchronize(device)
-    return {'ms_per_4_candidates': 1e3 * (time.perf_counter() - t0) / reps, 'prefix_tokens': cache.seen[0],
+    ms = 1e3 * (time.perf_counter() - t0) / reps
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        batched = model.answer(question, cands, cache, batched=True)
+    torch.cuda.synchronize(device)
+    ms_batched = 1e3 * (time.perf_counter() - t0) / reps
+    return {'ms_per_4_candidates': ms, 'prefix_tokens': cache.seen[0],
             'scores_mean_ll': ans['scores'], 'summed_ll': ans['summed'],
-            'note': 'wall time of StreamingModel.answer (4 forks x 32 layers, eager)'}, model
+            'ms_per_4_candidates_batched': ms_batched, 'batched_scores_mean_ll': batched['scores'],
+            'note': 'wall time of StreamingModel.answer, eager: the reference protocol (4 forks x question + '
+                    'candidate) and batched (question once, 4 candidates in one forward)'}, model
 
 
 def bench_c5(model, device, rank, world, total, dist):

@@ -100,8 +100,13 @@ int dkv_pack_rows(const void* k, const void* v, void* p4, void* m4, void* p8, vo
 }
 
 size_t dkv_packed_attention_workspace(int32_t past, int32_t nq, int32_t heads, int32_t group, int32_t dim) {
-  if (past < 0 || nq <= 0 || heads <= 0 || group <= 0 || dim != dkv::kDim) return 0;
-  return dkv::make_plan(past, nq, heads, group).workspace_bytes();
+  return dkv_packed_attention_batched_workspace(past, nq, heads, group, dim, 1);
+}
+
+size_t dkv_packed_attention_batched_workspace(int32_t past, int32_t nq, int32_t heads, int32_t group, int32_t dim,
+                                              int32_t chunks) {
+  if (past < 0 || nq <= 0 || heads <= 0 || group <= 0 || dim != dkv::kDim || chunks <= 0) return 0;
+  return dkv::make_plan(past, nq, heads, group, chunks).workspace_bytes();
 }
 
 int32_t dkv_packed_attention_launches(int32_t past, int32_t nq, int32_t heads, int32_t group, int32_t dim) {
@@ -113,13 +118,17 @@ int32_t dkv_packed_attention_launches(int32_t past, int32_t nq, int32_t heads, i
   return fused ? 1 : 2;
 }
 
-int dkv_packed_attention(const void* q, const void* knew, const void* vnew, const void* p4, const void* m4,
-                         const void* p8, const void* m8, const void* p16, const int32_t* rows,
-                         const uint8_t* codes, void* out, int64_t qh, int64_t qt, int64_t kh, int64_t kt,
-                         int64_t vh, int64_t vt, int32_t layer, int32_t past, int32_t nq, int64_t cap4,
-                         int64_t cap8, int64_t cap16, int32_t heads, int32_t group, int32_t dim,
-                         int32_t block_m, int32_t block_n, int32_t layers, void* workspace,
-                         size_t workspace_bytes, int32_t* status, void* stream) {
+}  // extern "C"
+
+namespace {
+
+int attention_impl(const void* q, const void* knew, const void* vnew, const void* p4, const void* m4,
+                   const void* p8, const void* m8, const void* p16, const int32_t* rows, const uint8_t* codes,
+                   void* out, int64_t qh, int64_t qt, int64_t kh, int64_t kt, int64_t vh, int64_t vt, int32_t chunks,
+                   int64_t qc, int64_t kc, int64_t vc, int64_t oc, int32_t layer, int32_t past, int32_t nq,
+                   int64_t cap4, int64_t cap8, int64_t cap16, int32_t heads, int32_t group, int32_t dim,
+                   int32_t block_m, int32_t block_n, int32_t layers, void* workspace, size_t workspace_bytes,
+                   int32_t* status, void* stream) {
   int rc = check_geometry(heads, dim, layers, layer);
   if (rc) return rc;
   if ((rc = check_pools(p4, m4, p8, m8, p16, cap4, cap8, cap16))) return rc;
@@ -127,6 +136,9 @@ int dkv_packed_attention(const void* q, const void* knew, const void* vnew, cons
   auto pow2 = [](int x) { return x >= 16 && x <= 256 && (x & (x - 1)) == 0; };
   if (!pow2(block_m) || !pow2(block_n)) return fail(DKV_EINVAL, "block_m/block_n must be powers of two in [16, 256]");
   if (past < 0 || nq < 0) return fail(DKV_EINVAL, "negative past or query length");
+  if (chunks <= 0 || static_cast<int64_t>(chunks) * heads > 65535) return fail(DKV_EINVAL, "chunk count out of range");
+  if (chunks > 1 && ((qc % 8) || (kc % 8) || (vc % 8) || (oc % 8)))
+    return fail(DKV_EINVAL, "chunk strides must keep rows 16-byte aligned (multiples of 8 elements)");
   if (nq == 0) return ok();
   if (past > 0 && (rows == nullptr || codes == nullptr)) return fail(DKV_EINVAL, "null token map");
   if (past > 0 && (!aligned16(rows) || !aligned16(codes)))
@@ -134,7 +146,7 @@ int dkv_packed_attention(const void* q, const void* knew, const void* vnew, cons
   if (!rows_aligned(q, qh, qt) || !rows_aligned(knew, kh, kt) || !rows_aligned(vnew, vh, vt))
     return fail(DKV_EINVAL, "q/k/v rows must be 16-byte aligned (head/token strides multiples of 8)");
   if (out == nullptr || !aligned16(out)) return fail(DKV_EINVAL, "out must be 16-byte aligned");
-  const dkv::AttnPlan p = dkv::make_plan(past, nq, heads, group);
+  const dkv::AttnPlan p = dkv::make_plan(past, nq, heads, group, chunks);
   const size_t need = p.workspace_bytes();
   if (need > 0 && (workspace == nullptr || workspace_bytes < need))
     return fail(DKV_EWORKSPACE, "attention workspace needs %zu bytes, got %zu", need, workspace_bytes);
@@ -157,6 +169,7 @@ int dkv_packed_attention(const void* q, const void* knew, const void* vnew, cons
   a.codes = codes;
   a.out = static_cast<uint16_t*>(out);
   a.qh = qh; a.qt = qt; a.kh = kh; a.kt = kt; a.vh = vh; a.vt = vt;
+  a.qc = qc; a.kc = kc; a.vc = vc; a.oc = oc;
   a.layer = layer;
   a.past = past;
   a.nq = nq;
@@ -175,9 +188,39 @@ int dkv_packed_attention(const void* q, const void* knew, const void* vnew, cons
   }
   a.status = status;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  cudaError_t e = p.tc ? dkv::launch_attention_tc(a, heads, st) : dkv::launch_attention_split(a, heads, st);
-  if (e == cudaSuccess && p.splits > 1 && !a.fused) e = dkv::launch_attention_combine(a, heads, st);
+  const int zdim = heads * chunks;  // grid z: chunk * heads + KV head
+  cudaError_t e = p.tc ? dkv::launch_attention_tc(a, zdim, st) : dkv::launch_attention_split(a, zdim, st);
+  if (e == cudaSuccess && p.splits > 1 && !a.fused) e = dkv::launch_attention_combine(a, zdim, st);
   return cuda_status(e, "packed_attention launch");
+}
+
+}  // namespace
+
+extern "C" {
+
+int dkv_packed_attention(const void* q, const void* knew, const void* vnew, const void* p4, const void* m4,
+                         const void* p8, const void* m8, const void* p16, const int32_t* rows,
+                         const uint8_t* codes, void* out, int64_t qh, int64_t qt, int64_t kh, int64_t kt,
+                         int64_t vh, int64_t vt, int32_t layer, int32_t past, int32_t nq, int64_t cap4,
+                         int64_t cap8, int64_t cap16, int32_t heads, int32_t group, int32_t dim,
+                         int32_t block_m, int32_t block_n, int32_t layers, void* workspace,
+                         size_t workspace_bytes, int32_t* status, void* stream) {
+  return attention_impl(q, knew, vnew, p4, m4, p8, m8, p16, rows, codes, out, qh, qt, kh, kt, vh, vt, 1, 0, 0, 0, 0,
+                        layer, past, nq, cap4, cap8, cap16, heads, group, dim, block_m, block_n, layers, workspace,
+                        workspace_bytes, status, stream);
+}
+
+int dkv_packed_attention_batched(const void* q, const void* knew, const void* vnew, const void* p4, const void* m4,
+                                 const void* p8, const void* m8, const void* p16, const int32_t* rows,
+                                 const uint8_t* codes, void* out, int64_t qh, int64_t qt, int64_t kh, int64_t kt,
+                                 int64_t vh, int64_t vt, int32_t chunks, int64_t qc, int64_t kc, int64_t vc,
+                                 int64_t oc, int32_t layer, int32_t past, int32_t nq, int64_t cap4, int64_t cap8,
+                                 int64_t cap16, int32_t heads, int32_t group, int32_t dim, int32_t block_m,
+                                 int32_t block_n, int32_t layers, void* workspace, size_t workspace_bytes,
+                                 int32_t* status, void* stream) {
+  return attention_impl(q, knew, vnew, p4, m4, p8, m8, p16, rows, codes, out, qh, qt, kh, kt, vh, vt, chunks, qc, kc,
+                        vc, oc, layer, past, nq, cap4, cap8, cap16, heads, group, dim, block_m, block_n, layers,
+                        workspace, workspace_bytes, status, stream);
 }
 
 int dkv_reconstruct(const void* p4, const void* m4, const void* p8, const void* m8, const void* p16,

@@ -33,7 +33,10 @@ struct AttnPlan {
   size_t workspace_bytes() const { return splits > 1 ? kSyncBytes + ws_o_bytes + ws_ml_bytes : 0; }
 };
 
-inline AttnPlan make_plan(int past, int nq, int heads, int group) {
+// `chunks` independent query chunks share the history (batched calls): they act as
+// chunks x heads groups of the same shape.
+inline AttnPlan make_plan(int past, int nq, int heads, int group, int chunks = 1) {
+  heads *= chunks;
   AttnPlan p{};
   p.mrows = group * nq;
   p.tc = p.mrows >= kTcMinRows;
@@ -71,6 +74,9 @@ struct AttnArgs {
   int64_t qh, qt, kh, kt, vh, vt;
   int layer, past, nq, G, HQ;
   int mrows, cta_rows, mblocks, splits, chunk;
+  // Batched calls: blockIdx.z = chunk * heads + KV head; chunk c's q / knew / vnew /
+  // out start qc / kc / vc / oc elements after chunk 0's (0 for a single chunk).
+  int64_t qc, kc, vc, oc;
   float* ws_o;    // [heads * mblocks][cta_rows][splits][64] unnormalised partial outputs
   float2* ws_ml;  // [heads * mblocks][cta_rows][even(splits)] (running max in log2 units, sum)
   uint32_t* sync;  // [2][kSyncGroups] arrival / departure counters of the in-kernel merge

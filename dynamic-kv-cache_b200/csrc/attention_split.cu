@@ -67,7 +67,9 @@ attention_split_kernel(const AttnArgs a) {
 
   const int split = blockIdx.x;
   const int mb = blockIdx.y;
-  const int g = blockIdx.z;
+  const int zc = blockIdx.z;  // chunk * heads + KV head
+  const int chunk = zc / a.P.heads;
+  const int g = zc - chunk * a.P.heads;
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
@@ -88,7 +90,7 @@ attention_split_kernel(const AttnArgs a) {
       const int fr = row0 + r;
       const int m = fr / a.G;
       const int h = g * a.G + (fr - m * a.G);
-      val = __ldg(reinterpret_cast<const uint4*>(a.q + h * a.qh + m * a.qt) + c);
+      val = __ldg(reinterpret_cast<const uint4*>(a.q + chunk * a.qc + h * a.qh + m * a.qt) + c);
     }
     *reinterpret_cast<uint4*>(sQ + swz(r, c)) = val;
   }
@@ -111,7 +113,8 @@ attention_split_kernel(const AttnArgs a) {
             pre[i] = load_history_part(a.P, a.rows, a.codes, a.layer, kv, g, t, part, a.status);
           } else {
             const int tn = t - a.past;
-            const uint16_t* src = kv == 0 ? a.knew + g * a.kh + tn * a.kt : a.vnew + g * a.vh + tn * a.vt;
+            const uint16_t* src = kv == 0 ? a.knew + chunk * a.kc + g * a.kh + tn * a.kt
+                                          : a.vnew + chunk * a.vc + g * a.vh + tn * a.vt;
             pre[i].raw = __ldg(reinterpret_cast<const uint4*>(src) + part);
             pre[i].bits = 16;
           }
@@ -264,7 +267,7 @@ attention_split_kernel(const AttnArgs a) {
       const float inv = 1.f / (half ? l_b : l_a);
       const int m = fr / a.G;
       const int h = g * a.G + (fr - m * a.G);
-      uint16_t* dst = a.out + (static_cast<int64_t>(m) * a.HQ + h) * kDim;
+      uint16_t* dst = a.out + chunk * a.oc + (static_cast<int64_t>(m) * a.HQ + h) * kDim;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const float x0 = o[j][2 * half] * inv, x1 = o[j][2 * half + 1] * inv;
@@ -274,7 +277,7 @@ attention_split_kernel(const AttnArgs a) {
     return;
   }
   // partial layout of part_o / part_ml, shared with the tensor-core kernel
-  const int grp = g * a.mblocks + mb;
+  const int grp = zc * a.mblocks + mb;
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
     const int r = half ? rb : ra;
@@ -297,13 +300,15 @@ __global__ void __launch_bounds__(256) attention_combine_kernel(const AttnArgs a
   __shared__ float s_w[4 * kTargetCtas], s_den[4];
   ptx::pdl_wait();  // partials of the attention grid
   ptx::pdl_trigger();
-  const int g = blockIdx.z;
+  const int zc = blockIdx.z;  // chunk * heads + KV head
+  const int chunk = zc / a.P.heads;
+  const int g = zc - chunk * a.P.heads;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int fr0 = blockIdx.x * 4;
   if (warp < 4 && fr0 + warp < a.mrows) {
     const int fr = fr0 + warp;
     const int mb = fr / a.cta_rows;
-    const float2* ml = a.ws_ml + part_ml(g * a.mblocks + mb, fr - mb * a.cta_rows, a.cta_rows, a.splits, 0);
+    const float2* ml = a.ws_ml + part_ml(zc * a.mblocks + mb, fr - mb * a.cta_rows, a.cta_rows, a.splits, 0);
     const float den = merge_row_weights([&](int sp) { return ml[sp]; }, a.splits, s_w + warp * kTargetCtas, lane);
     if (lane == 0) s_den[warp] = den;
   }
@@ -312,7 +317,7 @@ __global__ void __launch_bounds__(256) attention_combine_kernel(const AttnArgs a
   const int fr = fr0 + rl;
   if (fr >= a.mrows) return;
   const int mb = fr / a.cta_rows;
-  const float* src = a.ws_o + part_o(g * a.mblocks + mb, fr - mb * a.cta_rows, a.cta_rows, a.splits, 0) + d;
+  const float* src = a.ws_o + part_o(zc * a.mblocks + mb, fr - mb * a.cta_rows, a.cta_rows, a.splits, 0) + d;
   const int64_t sstride = kDim;
   float acc = 0.f;
   int sp = 0;
@@ -335,7 +340,8 @@ __global__ void __launch_bounds__(256) attention_combine_kernel(const AttnArgs a
   const float val = __fdiv_rn(acc, s_den[rl]);
   const int m = fr / a.G;
   const int h = g * a.G + (fr - m * a.G);
-  a.out[(static_cast<int64_t>(m) * a.HQ + h) * kDim + d] = static_cast<uint16_t>(pack_bf16x2(val, 0.f) & 0xffffu);
+  a.out[chunk * a.oc + (static_cast<int64_t>(m) * a.HQ + h) * kDim + d] =
+      static_cast<uint16_t>(pack_bf16x2(val, 0.f) & 0xffffu);
 }
 
 template <int NW>

@@ -222,7 +222,7 @@ __device__ __forceinline__ void convert_uniform(const uint8_t* st, uint8_t* dstK
 // operand rings; then a warp per row finds the weights and one thread per
 // (row, dim) sums its column from shared memory.
 __device__ __forceinline__ void merge_rows(const AttnArgs& a, int g, int grp, int row0, int r_begin, int r_end,
-                                           uint8_t* smem, int tid) {
+                                           uint16_t* out, uint8_t* smem, int tid) {
   const int nr = r_end - r_begin;
   if (nr <= 0) return;
   const uint32_t sbase = smem_addr(smem);
@@ -275,7 +275,7 @@ __device__ __forceinline__ void merge_rows(const AttnArgs& a, int g, int grp, in
     const int frow = row0 + r_begin + r;
     const int m = frow / a.G;
     const int h = g * a.G + (frow - m * a.G);
-    a.out[(static_cast<int64_t>(m) * a.HQ + h) * kDim + d] = static_cast<uint16_t>(pack_bf16x2(val, 0.f) & 0xffffu);
+    out[(static_cast<int64_t>(m) * a.HQ + h) * kDim + d] = static_cast<uint16_t>(pack_bf16x2(val, 0.f) & 0xffffu);
   }
 }
 
@@ -287,7 +287,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnA
 
   const int split = blockIdx.x;
   const int mb = blockIdx.y;
-  const int g = blockIdx.z;
+  const int zc = blockIdx.z;                  // chunk * heads + KV head
+  const int chunk = zc / a.P.heads;
+  const int g = zc - chunk * a.P.heads;
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
@@ -420,8 +422,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnA
     };
     auto meta_of = [&](int code, int kv) -> const float2* { return code == 4 ? (kv ? mv4 : mk4) : (kv ? mv8 : mk8); };
     auto mpar_of = [&](int code, int kv) -> int { return code == 4 ? (kv ? pbv4 : pbk4) : (kv ? pbv8 : pbk8); };
-    const uint16_t* const knew_g = a.knew + g * a.kh;
-    const uint16_t* const vnew_g = a.vnew + g * a.vh;
+    const uint16_t* const knew_g = a.knew + chunk * a.kc + g * a.kh;
+    const uint16_t* const vnew_g = a.vnew + chunk * a.vc + g * a.vh;
 
     auto map_tile = [&](int tile) {  // lane 0: start the map copy of a full history tile
       const int t0 = kb + tile * kBN;
@@ -721,7 +723,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnA
           const int fr = row0 + qrl;
           const int m = fr / a.G;
           const int h = g * a.G + (fr - m * a.G);
-          const uint4* src = reinterpret_cast<const uint4*>(a.q + h * a.qh + m * a.qt);
+          const uint4* src = reinterpret_cast<const uint4*>(a.q + chunk * a.qc + h * a.qh + m * a.qt);
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             const uint4 v = src[c];
@@ -876,7 +878,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnA
         if (a.splits == 1) {
           const int m = frow / a.G;
           const int h = g * a.G + (frow - m * a.G);
-          uint16_t* dst = a.out + (static_cast<int64_t>(m) * a.HQ + h) * kDim;
+          uint16_t* dst = a.out + chunk * a.oc + (static_cast<int64_t>(m) * a.HQ + h) * kDim;
           const float inv = 1.f / l;
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
@@ -890,7 +892,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnA
         } else {
           // partial layout of part_o / part_ml: this split's 64 outputs of the row are 256
           // contiguous bytes, stored as eight whole 32-byte sectors
-          const int grp = g * a.mblocks + mb;
+          const int grp = zc * a.mblocks + mb;
           float* dst = a.ws_o + part_o(grp, rl, kTcCtaRows, a.splits, split);
 #pragma unroll
           for (int c = 0; c < kDim / 8; ++c) st_global_v8(dst + 8 * c, o + 8 * c);
@@ -911,9 +913,10 @@ __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnA
   // ================= in-kernel split merge =================
   if (a.fused) {
     // block coordinates re-read here so nothing stays live across the roles above
-    const int msplit = blockIdx.x, mrow0 = blockIdx.y * kTcCtaRows, mg = blockIdx.z;
+    const int msplit = blockIdx.x, mrow0 = blockIdx.y * kTcCtaRows, mz = blockIdx.z;
+    const int mchunk = mz / a.P.heads, mg = mz - mchunk * a.P.heads;
     const int mrows_here = min(kTcCtaRows, a.mrows - mrow0);
-    const int grp = mg * a.mblocks + blockIdx.y;
+    const int grp = mz * a.mblocks + blockIdx.y;
     uint32_t* arrive = a.sync + grp;
     uint32_t* depart = a.sync + kSyncGroups + grp;
     // shared-memory base recomputed here: nothing from the roles above stays live
@@ -939,7 +942,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnA
     if (*go) {
       const int r_begin = msplit * mrows_here / a.splits;
       const int r_end = (msplit + 1) * mrows_here / a.splits;
-      merge_rows(a, mg, grp, mrow0, r_begin, r_end, msmem, threadIdx.x);
+      merge_rows(a, mg, grp, mrow0, r_begin, r_end, a.out + mchunk * a.oc, msmem, threadIdx.x);
     }
     __syncthreads();
     // every CTA departs exactly once (also after a timeout): the last one out

@@ -115,6 +115,45 @@ class Decoder(torch.nn.Module):
             out = F.scaled_dot_product_attention(q, kk, vv, attn_mask=mask, enable_gqa=True).transpose(1, 2)
         return F.linear(out.reshape(1, n, -1), self.o[layer])
 
+    def attention_chunks(self, x, layer, cache, cos, sin):
+        """Attention of B token chunks x [B, n, hidden] side by side over the cache's
+        history: each chunk sees the history and its own earlier tokens; nothing is
+        appended (the packed path runs one batched kernel call per layer)."""
+        c = self.cfg
+        b, n = x.shape[0], x.shape[1]
+        q, k, v = F.linear(x, self.qkv[layer]).split(
+            [c.q_heads * c.head_dim, c.kv_heads * c.head_dim, c.kv_heads * c.head_dim], dim=-1)
+        q = q.view(b, n, c.q_heads, c.head_dim).transpose(1, 2)
+        k = k.view(b, n, c.kv_heads, c.head_dim).transpose(1, 2)
+        v = v.view(b, n, c.kv_heads, c.head_dim).transpose(1, 2)
+        q, k = apply_rope(q, cos, sin), apply_rope(k, cos, sin)
+        past = cache.get_seq_length(layer)
+        if isinstance(cache, GPUCache):
+            out = cache.attend_batched(q, k, v, layer, past)  # [B, n, q_heads, d]
+        else:
+            if past:
+                k = torch.cat((cache.k[layer].expand(b, -1, -1, -1), k), 2)
+                v = torch.cat((cache.v[layer].expand(b, -1, -1, -1), v), 2)
+            mask = torch.arange(past + n, device=x.device)[None, :] <= past + torch.arange(n, device=x.device)[:, None]
+            out = F.scaled_dot_product_attention(q, k, v, attn_mask=mask, enable_gqa=True).transpose(1, 2)
+        return F.linear(out.reshape(b, n, -1), self.o[layer])
+
+    def forward_chunks(self, cache, ids, logits):
+        """B equal-length token chunks (ids [B, n]) after the cache's history, side by
+        side, without appending; returns fp32 logits [B, logits, vocab] of each
+        chunk's last `logits` positions."""
+        x = self.embed[ids]
+        n = x.shape[1]
+        past = cache.get_seq_length(0)
+        cos, sin = rope_tables(self.cfg, torch.arange(past, past + n, device=x.device), x.device)
+        for layer in range(self.cfg.layers):
+            x = x + self.attention_chunks(self.rms(x, self.norm_attn[layer]), layer, cache, cos, sin)
+            h = self.rms(x, self.norm_mlp[layer])
+            gate, up = F.linear(h, self.gate_up[layer]).chunk(2, dim=-1)
+            x = x + F.linear(activation_product(gate, up), self.down[layer])
+        h = self.rms(x[:, -logits:], self.norm_out)
+        return F.linear(h, self.embed).float()
+
     def forward(self, cache, ids=None, embeds=None, logits=0):
         """Runs n new tokens (ids [1, n] or embeds [1, n, hidden]) through every layer,
         appending their K/V to `cache`; returns fp32 logits of the last `logits`

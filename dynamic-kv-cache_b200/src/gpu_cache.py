@@ -149,6 +149,18 @@ class GPUCache(DynamicCache):
                            self.dim, self.block_m, self.block_n, self.layers, self.status)
         return out
 
+    def attend_batched(self, q, k, v, layer, past):
+        """B independent query chunks over the same packed history (batched candidate
+        scoring): q [B, query_heads, n, dim], k / v [B, heads, n, dim] are each
+        chunk's own new K/V, attended natively and not appended. Returns
+        [B, n, query_heads, dim]. Not in the reference."""
+        b, _, n, _ = q.shape
+        out = torch.empty((b, n, q.shape[1], self.dim), dtype=q.dtype, device=q.device)
+        K.packed_attention_batched(q, k, v, *self._pools(), self.rows, self.codes, out, layer, past, n,
+                                   self.caps[4], self.caps[8], self.caps[16], self.heads, q.shape[1] // self.heads,
+                                   self.dim, self.block_m, self.block_n, self.layers, self.status)
+        return out
+
     def materialize(self, layer):
         """Dequantised bf16 history (k, v), each [1, heads, seen, dim] (src/gpu_cache.py:106-112)."""
         n = self.seen[layer]

@@ -42,6 +42,10 @@ def _load():
                                   I32, I32, I32, I64, I64, I64, I32, I32, I32, I32, I32, I32,
                                   P, SZ, P, P], ctypes.c_int),
         'dkv_packed_attention_workspace': ([I32, I32, I32, I32, I32], SZ),
+        'dkv_packed_attention_batched': ([P, P, P, P, P, P, P, P, P, P, P, I64, I64, I64, I64, I64, I64,
+                                          I32, I64, I64, I64, I64, I32, I32, I32, I64, I64, I64, I32, I32, I32,
+                                          I32, I32, I32, P, SZ, P, P], ctypes.c_int),
+        'dkv_packed_attention_batched_workspace': ([I32, I32, I32, I32, I32, I32], SZ),
         'dkv_packed_attention_launches': ([I32, I32, I32, I32, I32], I32),
         'dkv_reconstruct': ([P, P, P, P, P, P, P, P, I32, I32, I64, I64, I64, I32, I32, I32, P, P],
                             ctypes.c_int),
@@ -55,7 +59,8 @@ def _load():
 
 LIB = _load()
 EXPORTS = ('dkv_version', 'dkv_last_error', 'dkv_pack_rows', 'dkv_packed_attention',
-           'dkv_packed_attention_workspace', 'dkv_packed_attention_launches', 'dkv_reconstruct', 'dkv_map_fill')
+           'dkv_packed_attention_workspace', 'dkv_packed_attention_launches', 'dkv_packed_attention_batched',
+           'dkv_packed_attention_batched_workspace', 'dkv_reconstruct', 'dkv_map_fill')
 
 
 def _check(rc):
@@ -134,6 +139,27 @@ def packed_attention(q, knew, vnew, p4, m4, p8, m8, p16, rows, codes, out, layer
         _ptr(codes), _ptr(out), q.stride(1), q.stride(2), knew.stride(1), knew.stride(2),
         vnew.stride(1), vnew.stride(2), layer, past, nq, cap4, cap8, cap16, heads, group, dim,
         block_m, block_n, layers, _ptr(workspace), size, _ptr(status), _stream(q)))
+    return out
+
+
+def packed_attention_batched(q, knew, vnew, p4, m4, p8, m8, p16, rows, codes, out, layer, past, nq, cap4, cap8,
+                             cap16, heads, group, dim, block_m, block_n, layers, status=None):
+    """B query chunks over one packed history: q [B, heads*group, nq, dim], knew / vnew
+    [B, heads, nq, dim] (each chunk's own new rows, read natively, not appended), out
+    [B, nq, heads*group, dim]. No reference counterpart (batched candidate scoring)."""
+    q, knew, vnew = (_rows_ready(x) for x in (q, knew, vnew))
+    chunks = q.shape[0]
+    for x in (q, knew, vnew, out):
+        if x.shape[0] != chunks or x.stride(0) % 8:
+            raise ValueError('batched attention operands need one leading chunk dimension of 16-byte steps')
+    size = LIB.dkv_packed_attention_batched_workspace(past, nq, heads, group, dim, chunks)
+    workspace = _workspace(q.device, _stream(q), size) if size else None
+    _check(LIB.dkv_packed_attention_batched(
+        _ptr(q), _ptr(knew), _ptr(vnew), _ptr(p4), _ptr(m4), _ptr(p8), _ptr(m8), _ptr(p16), _ptr(rows),
+        _ptr(codes), _ptr(out), q.stride(1), q.stride(2), knew.stride(1), knew.stride(2), vnew.stride(1),
+        vnew.stride(2), chunks, q.stride(0), knew.stride(0), vnew.stride(0), out.stride(0), layer, past, nq,
+        cap4, cap8, cap16, heads, group, dim, block_m, block_n, layers, _ptr(workspace), size, _ptr(status),
+        _stream(q)))
     return out
 
 

@@ -76,11 +76,15 @@ class StreamingModel:
         return cache
 
     @torch.inference_mode()
-    def answer(self, question_ids, candidate_ids, cache):
+    def answer(self, question_ids, candidate_ids, cache, batched=False):
         """Candidate protocol (src/streaming.py:209-225): per candidate, a fork of
         the cache sees question + candidate; the score is the mean log-likelihood
         of the candidate tokens. Returns scores (mean), summed log-likelihoods and
-        the argmax."""
+        the argmax. batched=True (equal-length candidates; not in the reference)
+        appends the question to one fork once and runs every candidate in one
+        forward over it: the same likelihoods up to floating-point order."""
+        if batched and len({c.shape[1] for c in candidate_ids}) == 1:
+            return self._answer_batched(question_ids, candidate_ids, cache)
         means, sums = [], []
         for answer_ids in candidate_ids:
             ids = torch.cat((question_ids, answer_ids), dim=1)
@@ -90,6 +94,17 @@ class StreamingModel:
             means.append(ll.mean())
             sums.append(ll.sum())
         means, sums = torch.stack(means), torch.stack(sums)
+        values = means.tolist()
+        return dict(scores=values, summed=sums.tolist(), prediction=max(range(len(values)), key=values.__getitem__))
+
+
+    def _answer_batched(self, question_ids, candidate_ids, cache):
+        fork = cache.fork()
+        first = self.model(fork, ids=question_ids, logits=1)[0, -1].log_softmax(-1)  # predicts token 0
+        ids = torch.cat(candidate_ids, dim=0)                                         # [B, n]
+        rest = self.model.forward_chunks(fork, ids, logits=ids.shape[1])[:, :-1].log_softmax(-1)
+        ll = torch.cat((first[ids[:, :1]], rest.gather(2, ids[:, 1:, None])[..., 0]), dim=1)  # [B, n]
+        means, sums = ll.mean(1), ll.sum(1)
         values = means.tolist()
         return dict(scores=values, summed=sums.tolist(), prediction=max(range(len(values)), key=values.__getitem__))
 

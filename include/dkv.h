@@ -118,6 +118,34 @@ int dkv_packed_attention(const void* q, const void* knew, const void* vnew,
 size_t dkv_packed_attention_workspace(int32_t past, int32_t nq, int32_t heads,
                                       int32_t group, int32_t dim);
 
+/*
+ * dkv_packed_attention over `chunks` independent query chunks that share one
+ * packed history (no reference counterpart: it serves batched candidate scoring,
+ * where every candidate attends to the same prefix + question and to its own
+ * tokens only). Chunk c's q / knew / vnew / out begin qc / kc / vc / oc elements
+ * after chunk 0's (multiples of 8); each chunk has nq queries with the same
+ * causal rule as dkv_packed_attention and reads its own nq new K/V rows natively
+ * (they are not appended to the pools). Same workspace contract, sized by
+ * dkv_packed_attention_batched_workspace(); chunks = 1 is dkv_packed_attention.
+ */
+int dkv_packed_attention_batched(const void* q, const void* knew, const void* vnew,
+                                 const void* p4, const void* m4, const void* p8,
+                                 const void* m8, const void* p16,
+                                 const int32_t* rows, const uint8_t* codes, void* out,
+                                 int64_t qh, int64_t qt, int64_t kh, int64_t kt,
+                                 int64_t vh, int64_t vt, int32_t chunks,
+                                 int64_t qc, int64_t kc, int64_t vc, int64_t oc,
+                                 int32_t layer, int32_t past, int32_t nq,
+                                 int64_t cap4, int64_t cap8, int64_t cap16,
+                                 int32_t heads, int32_t group, int32_t dim,
+                                 int32_t block_m, int32_t block_n,
+                                 int32_t layers, void* workspace, size_t workspace_bytes,
+                                 int32_t* status, void* stream);
+
+/* Workspace bytes dkv_packed_attention_batched needs (0 = none). */
+size_t dkv_packed_attention_batched_workspace(int32_t past, int32_t nq, int32_t heads,
+                                              int32_t group, int32_t dim, int32_t chunks);
+
 /* Kernel launches one dkv_packed_attention call of this shape makes on the
  * current device (1 or 2; 0 for invalid shapes, -1 on a CUDA error). No
  * reference counterpart: it lets callers and benchmarks count launches. */

@@ -551,11 +551,32 @@ __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnA
           const int j = 2 * lane + e;
           const int cd = code[e];
           uint32_t raw_off = 0, moff[2] = {0, 0};
-          if (cd == kCodeNew) {  // native current-chunk row: one 128-byte copy each for K and V
+          if (cd == kCodeNew) {  // native current-chunk row, raw slot j
             raw_off = j * 128;
-            mbar_expect_tx(rbar, 256);
-            bulk_g2s(sst + kRawK + raw_off, knew_g + static_cast<int64_t>(row[e]) * a.kt, 128, rbar);
-            bulk_g2s(sst + kRawV + raw_off, vnew_g + static_cast<int64_t>(row[e]) * a.vt, 128, rbar);
+            // The tile's new tokens are one run (past .. ke): rows stored 64 elements
+            // apart are one contiguous block, fetched by a single copy from the run's
+            // first lane; other layouts take one 128-byte copy per row.
+            const int jn = max(a.past - t0, 0);                 // first new token of the tile
+            const int nn = min(ke - t0, kBN) - jn;              // new tokens in the tile
+            const bool first = j == jn;
+            if (a.kt == kDim) {
+              if (first) {
+                mbar_expect_tx(rbar, nn * 128);
+                bulk_g2s(sst + kRawK + raw_off, knew_g + static_cast<int64_t>(row[e]) * kDim, nn * 128, rbar);
+              }
+            } else {
+              mbar_expect_tx(rbar, 128);
+              bulk_g2s(sst + kRawK + raw_off, knew_g + static_cast<int64_t>(row[e]) * a.kt, 128, rbar);
+            }
+            if (a.vt == kDim) {
+              if (first) {
+                mbar_expect_tx(rbar, nn * 128);
+                bulk_g2s(sst + kRawV + raw_off, vnew_g + static_cast<int64_t>(row[e]) * kDim, nn * 128, rbar);
+              }
+            } else {
+              mbar_expect_tx(rbar, 128);
+              bulk_g2s(sst + kRawV + raw_off, vnew_g + static_cast<int64_t>(row[e]) * a.vt, 128, rbar);
+            }
           } else if (cd != 0) {
             const int j0 = 63 - __clzll(starts & ((2ull << j) - 1));  // first token of j's run
             const uint64_t after = starts & ~((2ull << j0) - 1);

@@ -96,11 +96,13 @@ enum {
   B_RAWFULL = B_EMPTY + kStages,        // raw stage landed       (loader + TMA bytes)
   B_RAWEMPTY = B_RAWFULL + kRawStages,  // raw stage consumed     (converters, 128)
   B_MAPFULL = B_RAWEMPTY + kRawStages,  // map stage landed       (loader + TMA bytes)
-  B_SFULL = B_MAPFULL + kMapStages,    // S[b] computed            (S commit)
-  B_SFREE = B_SFULL + 2,                // S[b] read                (softmax threads)
-  B_PFULL = B_SFREE + 2,                // P written                (softmax threads)
-  B_ODONE = B_PFULL + 1,                // O updated, P consumed    (PV commit)
-  B_QREADY = B_ODONE + 1,
+  // Per M-tile barriers: the two row tiles run their S -> softmax -> P V chains
+  // independently, so one tile's softmax hides the other's barrier and MMA latency.
+  B_SFULL = B_MAPFULL + kMapStages,    // S[b][mt] computed        (S commit),  index b * 2 + mt
+  B_SFREE = B_SFULL + 4,                // S[b][mt] read            (mt's softmax threads)
+  B_PFULL = B_SFREE + 4,                // P[mt] written            (mt's softmax threads)
+  B_ODONE = B_PFULL + 2,                // O[mt] updated, P[mt] read (PV commit)
+  B_QREADY = B_ODONE + 2,
   B_FINS = B_QREADY + 1,
   B_FINPV = B_FINS + 1,
   B_MERGE = B_FINPV + 1,                // split partials landed   (merge, TMA bytes)
@@ -317,12 +319,15 @@ __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnA
       mbar_init(bar(B_RAWEMPTY + s), kConvThreads);
     }
     for (int s = 0; s < kMapStages; ++s) mbar_init(bar(B_MAPFULL + s), 1);
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(bar(B_SFULL + b), 1);
-      mbar_init(bar(B_SFREE + b), soft_threads);
+    const int tile_threads[2] = {min(soft_threads, 128), max(soft_threads - 128, 32)};  // (unused tile: any count)
+    for (int mt = 0; mt < 2; ++mt) {
+      for (int b = 0; b < 2; ++b) {
+        mbar_init(bar(B_SFULL + b * 2 + mt), 1);
+        mbar_init(bar(B_SFREE + b * 2 + mt), tile_threads[mt]);
+      }
+      mbar_init(bar(B_PFULL + mt), tile_threads[mt]);
+      mbar_init(bar(B_ODONE + mt), 1);
     }
-    mbar_init(bar(B_PFULL), soft_threads);
-    mbar_init(bar(B_ODONE), 1);
     mbar_init(bar(B_QREADY), kSoftmaxWarps * 32);
     mbar_init(bar(B_FINS), 1);
     mbar_init(bar(B_FINPV), 1);
@@ -347,18 +352,18 @@ __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnA
       for (int i = 0; i < ntiles && ok; ++i) {
         const int s = i % kStages, b = i & 1;
         ok = mbar_wait(bar(B_FULL + s), (i / kStages) & 1, kWaitCycles);
-        if (ok && i >= 2) ok = mbar_wait(bar(B_SFREE + b), ((i >> 1) + 1) & 1, kWaitCycles);
-        if (!ok) break;
-        tc_fence_after();
-        for (int mt = 0; mt < mt_count; ++mt) {
+        for (int mt = 0; mt < mt_count && ok; ++mt) {
+          if (i >= 2) ok = mbar_wait(bar(B_SFREE + b * 2 + mt), ((i >> 1) + 1) & 1, kWaitCycles);
+          if (!ok) break;
+          tc_fence_after();
           const uint32_t d = tmem + kColS + (b * 2 + mt) * 64;
 #pragma unroll
           for (int k = 0; k < 4; ++k) {  // 16 dims per step = 8 TMEM columns of Q
             const uint64_t bd = sw128_desc(sbase + kOffK + s * kTile + k * 32, 16, 1024);
             umma_f16_ts(d, tmem + kColQ + mt * 32 + k * 8, bd, kIdescS, k > 0);
           }
+          umma_commit(bar(B_SFULL + b * 2 + mt));
         }
-        umma_commit(bar(B_SFULL + b));
       }
       if (!ok) {
         *abort_flag = 1;
@@ -373,20 +378,20 @@ __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnA
     if (lane == 0 && ntiles > 0) {
       bool ok = true;
       for (int i = 0; i < ntiles && ok; ++i) {
-        ok = mbar_wait(bar(B_PFULL), i & 1, kWaitCycles);
-        if (!ok) break;
-        tc_fence_after();
         const int s = i % kStages;
-        for (int mt = 0; mt < mt_count; ++mt) {
+        for (int mt = 0; mt < mt_count && ok; ++mt) {
+          ok = mbar_wait(bar(B_PFULL + mt), i & 1, kWaitCycles);
+          if (!ok) break;
+          tc_fence_after();
           const uint32_t d = tmem + kColO + mt * 64;
 #pragma unroll
           for (int k = 0; k < 4; ++k) {  // 16 keys per step = 8 TMEM columns of P
             const uint64_t bd = sw128_desc(sbase + kOffV + s * kTile + k * 2048, kTile, 1024);
             umma_f16_ts(d, tmem + kColP + mt * 32 + k * 8, bd, kIdescPV, (i > 0 || k > 0) ? 1u : 0u);
           }
+          umma_commit(bar(B_ODONE + mt));
         }
-        umma_commit(bar(B_ODONE));
-        umma_commit(bar(B_EMPTY + s));
+        if (ok) umma_commit(bar(B_EMPTY + s));  // both tiles' products have read V (and S read K)
       }
       if (!ok) {
         *abort_flag = 1;
@@ -782,7 +787,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnA
       for (int i = 0; i < ntiles; ++i) {
         const int b = i & 1;
         if (__any_sync(0xffffffffu, *abort_flag != 0)) { ok = false; break; }
-        ok = __all_sync(0xffffffffu, mbar_wait(bar(B_SFULL + b), (i >> 1) & 1, kWaitCycles));
+        ok = __all_sync(0xffffffffu, mbar_wait(bar(B_SFULL + b * 2 + mt), (i >> 1) & 1, kWaitCycles));
         if (!ok) break;
         tc_fence_after();
         float s[64];
@@ -798,7 +803,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnA
           }
         }
         tc_fence_before();
-        mbar_arrive(bar(B_SFREE + b));  // S[b] may be overwritten by S(i + 2)
+        mbar_arrive(bar(B_SFREE + b * 2 + mt));  // S[b][mt] may be overwritten by S(i + 2)
         const int t0 = kb + i * kBN;
         if (!(t0 + kBN <= ke && t0 + kBN - 1 <= a.past)) {  // boundary tile: mask
 #pragma unroll
@@ -846,7 +851,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnA
         // rescale and P(i-1) is consumed (a P store overlapping an in-flight P V
         // product corrupted the rows of warps that ran ahead, even into other columns)
         if (i > 0) {
-          ok = __all_sync(0xffffffffu, mbar_wait(bar(B_ODONE), (i - 1) & 1, kWaitCycles));
+          ok = __all_sync(0xffffffffu, mbar_wait(bar(B_ODONE + mt), (i - 1) & 1, kWaitCycles));
           if (!ok) break;
           tc_fence_after();
         }
@@ -868,7 +873,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnA
         tmem_st32(lane_base + kColP + mt * 32, pk);
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(bar(B_PFULL));
+        mbar_arrive(bar(B_PFULL + mt));
       }
       // ---- epilogue: O row from TMEM, its sum of p from registers ----
       float o[64];
@@ -876,7 +881,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) attention_tc_kernel(const AttnA
 #pragma unroll
       for (int j = 0; j < 64; ++j) o[j] = 0.f;
       if (ok && ntiles > 0) {
-        ok = __all_sync(0xffffffffu, mbar_wait(bar(B_ODONE), (ntiles - 1) & 1, kWaitCycles));
+        ok = __all_sync(0xffffffffu, mbar_wait(bar(B_ODONE + mt), (ntiles - 1) & 1, kWaitCycles));
         tc_fence_after();
         if (ok) {
           uint32_t r0[32], r1[32];

@@ -63,6 +63,11 @@ def parse():
     ap.add_argument('--configs', default='c1,c2,c4,c5',
                     help='extra BASELINE configurations reported in the same line (comma list, or "none")')
     ap.add_argument('--c5-requests', type=int, default=64, help='C5 requests in total, split across ranks')
+    ap.add_argument('--c5-batch', type=int, default=8,
+                    help='C5 requests stepped together per GPU (request batching); 8 divides 64 / 8 GPUs, so '
+                         'every GPU count forms the same batches and the scores stay bit-identical')
+    ap.add_argument('--c5-sequential', type=int, default=4,
+                    help='C5 requests per rank also run one at a time (the reference protocol) for comparison')
     ap.add_argument('--layers', type=int, default=LAYERS,
                     help='cache layers (the per-call workload is unchanged; fewer layers only shrink '
                          'the set-up for profiler captures)')
@@ -299,35 +304,62 @@ def bench_c4(device):
                     'candidate) and batched (question once, 4 candidates in one forward)'}, model
 
 
-def bench_c5(model, device, rank, world, total, dist):
+def bench_c5(model, device, rank, world, total, dist, batch, sequential):
     """C5: `total` independent requests (64 frames x 64 tokens, dynamic 4/8/16, seed = request
-    id, then 4-candidate scoring) split across ranks; scores gathered with NCCL."""
+    id, then 4-candidate scoring) split across ranks; on each rank the requests are stepped
+    `batch` at a time through one batched decoder forward per frame (request batching: one
+    pack and one attention launch per layer for the whole batch). Scores gathered with NCCL.
+    The first `sequential` requests of each rank are also run one at a time through the
+    reference's per-request protocol, timed separately, and their scores compared."""
     import hashlib
     from src.streaming import bits_for, synthetic_request
     per = total // world
-    mine = range(rank * per, (rank + 1) * per)
+    mine = list(range(rank * per, (rank + 1) * per))
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize(device)
     t0 = time.perf_counter()
     scores = []
-    for r in mine:
-        embeds, question, cands = synthetic_request(model.cfg, seed=r, frames=64, device=device)
-        cache = model.ingest(embeds, bits_for('dynamic', 64, seed=r), 'dynamic', qa_reserve=64)
-        scores.append(model.answer(question, cands, cache)['scores'])
+    for s in range(0, per, batch):
+        ids = mine[s:s + batch]
+        reqs = [synthetic_request(model.cfg, seed=r, frames=64, device=device) for r in ids]
+        caches = model.ingest_many([q[0] for q in reqs], [bits_for('dynamic', 64, seed=r) for r in ids], 'dynamic',
+                                   qa_reserve=64)
+        scores += [a['scores'] for a in model.answer_many([q[1] for q in reqs], [q[2] for q in reqs], caches)]
+        del caches
     torch.cuda.synchronize(device)
     secs = torch.tensor([time.perf_counter() - t0], device=device)
+    seq = min(sequential, per)
+    torch.cuda.synchronize(device)
+    t0 = time.perf_counter()
+    seq_scores = []
+    for r in mine[:seq]:
+        embeds, question, cands = synthetic_request(model.cfg, seed=r, frames=64, device=device)
+        cache = model.ingest(embeds, bits_for('dynamic', 64, seed=r), 'dynamic', qa_reserve=64)
+        seq_scores.append(model.answer(question, cands, cache)['scores'])
+    torch.cuda.synchronize(device)
+    seq_secs = torch.tensor([time.perf_counter() - t0], device=device)
+    diff = torch.tensor([max((abs(a - b) for x, y in zip(seq_scores, scores) for a, b in zip(x, y)), default=0.0)],
+                        device=device)
     local = torch.tensor(scores, dtype=torch.float32, device=device)
     if dist is not None:
         dist.all_reduce(secs, op=dist.ReduceOp.MAX)
+        dist.all_reduce(seq_secs, op=dist.ReduceOp.MAX)
+        dist.all_reduce(diff, op=dist.ReduceOp.MAX)
         gathered = [torch.empty_like(local) for _ in range(world)]
         dist.all_gather(gathered, local)
         local = torch.cat(gathered)
     all_scores = local.cpu().numpy()
     return {'frame_append_tokens_per_s': per * world * 64 * 64 / float(secs.item()),
-            'requests': per * world, 'seconds': float(secs.item()), 'scaling': 'strong (fixed request set)',
+            'requests': per * world, 'seconds': float(secs.item()), 'batch_per_gpu': batch,
+            'scaling': 'strong (fixed request set)',
             'scores_sha256': hashlib.sha256(all_scores.tobytes()).hexdigest(),
-            'note': 'wall time incl. frame appends and scoring, eager; scores gathered with NCCL all_gather'}
+            'sequential': {'requests_per_gpu': seq, 'seconds': float(seq_secs.item()),
+                           'frame_append_tokens_per_s': seq * world * 64 * 64 / max(float(seq_secs.item()), 1e-9),
+                           'max_abs_score_diff_vs_batched': float(diff.item())},
+            'note': 'wall time incl. frame appends and scoring, eager; batched: requests stepped together '
+                    '(one pack + one attention launch per layer per batch); sequential: the reference '
+                    'protocol, one request at a time; scores gathered with NCCL all_gather'}
 
 
 def main():
@@ -505,7 +537,8 @@ def main():
         if 'c4' in configs:
             line['c4_candidate_scoring'] = c4
     if 'c5' in configs:
-        line['c5_request_throughput'] = bench_c5(model, device, rank, world, args.c5_requests, dist)
+        line['c5_request_throughput'] = bench_c5(model, device, rank, world, args.c5_requests, dist, args.c5_batch,
+                                                 args.c5_sequential)
     if rank == 0 and 'c1' in configs:
         line['c1_cpu_reference_path'] = bench_c1()
     if rank == 0 and not args.no_cpu_baseline:

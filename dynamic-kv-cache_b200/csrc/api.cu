@@ -2,6 +2,7 @@
 // Host-side argument validation mirrors the reference's ValueError conditions;
 // nothing here allocates, synchronises or retains pointers.
 #include <cstdarg>
+#include <cstddef>
 #include <cstdio>
 #include <cstring>
 
@@ -16,7 +17,19 @@ cudaError_t launch_reconstruct(const Pools& P, const int32_t* rows, const uint8_
                                int layer, int n, int32_t* status, cudaStream_t stream);
 cudaError_t launch_map_fill(int32_t* rows, uint8_t* codes, int64_t start, int n, int64_t row, int bits,
                             cudaStream_t stream);
+cudaError_t launch_pack_many(const void* k, const void* v, const dkv_pack_target* targets, int count, int64_t kh,
+                             int64_t kt, int64_t vh, int64_t vt, int64_t kc, int64_t vc, int layer, int n, int heads,
+                             cudaStream_t stream);
 }  // namespace dkv
+
+// The request descriptors cross the C ABI by layout: keep it fixed (the Python
+// binding declares the same fields in the same order).
+static_assert(sizeof(dkv_history) == 96 && offsetof(dkv_history, past) == 80 && offsetof(dkv_history, status) == 88,
+              "dkv_history layout");
+static_assert(sizeof(dkv_pack_target) == 120 && offsetof(dkv_pack_target, bits) == 72 &&
+                  offsetof(dkv_pack_target, map_rows) == 80 && offsetof(dkv_pack_target, status) == 112,
+              "dkv_pack_target layout");
+static_assert(sizeof(dkv::HistoryTable) + sizeof(dkv::AttnArgs) <= 4096, "attention kernel parameters");
 
 namespace {
 
@@ -122,6 +135,41 @@ int32_t dkv_packed_attention_launches(int32_t past, int32_t nq, int32_t heads, i
 
 namespace {
 
+// Fills the call-wide fields of `a` (its history is set by the caller) and
+// launches the planned kernels: attention, then the combine when the splits are
+// not merged in the attention kernel.
+int launch_planned(dkv::AttnArgs& a, const dkv::AttnPlan& p, const void* q, const void* knew, const void* vnew,
+                   void* out, int64_t qh, int64_t qt, int64_t kh, int64_t kt, int64_t vh, int64_t vt, int32_t chunks,
+                   int64_t qc, int64_t kc, int64_t vc, int64_t oc, int32_t layer, int32_t nq, int32_t heads,
+                   int32_t group, void* workspace, void* stream, const dkv::HistoryTable* table) {
+  a.q = static_cast<const uint16_t*>(q);
+  a.knew = static_cast<const uint16_t*>(knew);
+  a.vnew = static_cast<const uint16_t*>(vnew);
+  a.out = static_cast<uint16_t*>(out);
+  a.qh = qh; a.qt = qt; a.kh = kh; a.kt = kt; a.vh = vh; a.vt = vt;
+  a.qc = qc; a.kc = kc; a.vc = vc; a.oc = oc;
+  a.layer = layer;
+  a.nq = nq;
+  a.G = group;
+  a.HQ = heads * group;
+  a.mrows = p.mrows;
+  a.cta_rows = p.cta_rows;
+  a.mblocks = p.mblocks;
+  a.splits = p.splits;
+  a.chunk = p.chunk;
+  if (p.workspace_bytes() > 0) {  // [merge counters][partial outputs][partial (max, sum)]
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    a.sync = reinterpret_cast<uint32_t*>(ws);
+    a.ws_o = reinterpret_cast<float*>(ws + dkv::kSyncBytes);
+    a.ws_ml = reinterpret_cast<float2*>(ws + dkv::kSyncBytes + p.ws_o_bytes);
+  }
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int zdim = heads * chunks;  // grid z: chunk * heads + KV head
+  cudaError_t e = p.tc ? dkv::launch_attention_tc(a, zdim, st, table) : dkv::launch_attention_split(a, zdim, st, table);
+  if (e == cudaSuccess && p.splits > 1 && !a.fused) e = dkv::launch_attention_combine(a, zdim, st);
+  return cuda_status(e, "packed_attention launch");
+}
+
 int attention_impl(const void* q, const void* knew, const void* vnew, const void* p4, const void* m4,
                    const void* p8, const void* m8, const void* p16, const int32_t* rows, const uint8_t* codes,
                    void* out, int64_t qh, int64_t qt, int64_t kh, int64_t kt, int64_t vh, int64_t vt, int32_t chunks,
@@ -153,45 +201,15 @@ int attention_impl(const void* q, const void* knew, const void* vnew, const void
   if (need > 0 && (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
     return fail(DKV_EWORKSPACE, "attention workspace must be 256-byte aligned");
   dkv::AttnArgs a{};
-  a.q = static_cast<const uint16_t*>(q);
-  a.knew = static_cast<const uint16_t*>(knew);
-  a.vnew = static_cast<const uint16_t*>(vnew);
-  a.P.p4 = static_cast<const uint8_t*>(p4);
-  a.P.m4 = static_cast<const float2*>(m4);
-  a.P.p8 = static_cast<const uint8_t*>(p8);
-  a.P.m8 = static_cast<const float2*>(m8);
-  a.P.p16 = static_cast<const uint16_t*>(p16);
-  a.P.cap4 = cap4;
-  a.P.cap8 = cap8;
-  a.P.cap16 = cap16;
-  a.P.heads = heads;
-  a.rows = rows;
-  a.codes = codes;
-  a.out = static_cast<uint16_t*>(out);
-  a.qh = qh; a.qt = qt; a.kh = kh; a.kt = kt; a.vh = vh; a.vt = vt;
-  a.qc = qc; a.kc = kc; a.vc = vc; a.oc = oc;
-  a.layer = layer;
-  a.past = past;
-  a.nq = nq;
-  a.G = group;
-  a.HQ = heads * group;
-  a.mrows = p.mrows;
-  a.cta_rows = p.cta_rows;
-  a.mblocks = p.mblocks;
-  a.splits = p.splits;
-  a.chunk = p.chunk;
-  if (need > 0) {  // [merge counters][partial outputs][partial (max, sum)]
-    uint8_t* ws = static_cast<uint8_t*>(workspace);
-    a.sync = reinterpret_cast<uint32_t*>(ws);
-    a.ws_o = reinterpret_cast<float*>(ws + dkv::kSyncBytes);
-    a.ws_ml = reinterpret_cast<float2*>(ws + dkv::kSyncBytes + p.ws_o_bytes);
-  }
-  a.status = status;
-  const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int zdim = heads * chunks;  // grid z: chunk * heads + KV head
-  cudaError_t e = p.tc ? dkv::launch_attention_tc(a, zdim, st) : dkv::launch_attention_split(a, zdim, st);
-  if (e == cudaSuccess && p.splits > 1 && !a.fused) e = dkv::launch_attention_combine(a, zdim, st);
-  return cuda_status(e, "packed_attention launch");
+  a.hist.P = dkv::Pools{static_cast<const uint8_t*>(p4), static_cast<const float2*>(m4),
+                        static_cast<const uint8_t*>(p8), static_cast<const float2*>(m8),
+                        static_cast<const uint16_t*>(p16), cap4, cap8, cap16, heads};
+  a.hist.rows = rows;
+  a.hist.codes = codes;
+  a.hist.status = status;
+  a.hist.past = past;
+  return launch_planned(a, p, q, knew, vnew, out, qh, qt, kh, kt, vh, vt, chunks, qc, kc, vc, oc, layer, nq, heads,
+                        group, workspace, stream, nullptr);
 }
 
 }  // namespace
@@ -221,6 +239,91 @@ int dkv_packed_attention_batched(const void* q, const void* knew, const void* vn
   return attention_impl(q, knew, vnew, p4, m4, p8, m8, p16, rows, codes, out, qh, qt, kh, kt, vh, vt, chunks, qc, kc,
                         vc, oc, layer, past, nq, cap4, cap8, cap16, heads, group, dim, block_m, block_n, layers,
                         workspace, workspace_bytes, status, stream);
+}
+
+int dkv_pack_rows_many(const void* k, const void* v, const dkv_pack_target* targets, int32_t count, int64_t kh,
+                       int64_t kt, int64_t vh, int64_t vt, int64_t kc, int64_t vc, int32_t layer, int32_t n,
+                       int32_t heads, int32_t dim, int32_t layers, void* stream) {
+  int rc = check_geometry(heads, dim, layers, layer);
+  if (rc) return rc;
+  if (count <= 0 || count > DKV_MAX_REQUESTS)
+    return fail(DKV_EINVAL, "request count %d outside [1, %d]", count, DKV_MAX_REQUESTS);
+  if (targets == nullptr) return fail(DKV_EINVAL, "null request table");
+  if (n < 0) return fail(DKV_EINVAL, "negative token count");
+  if (!rows_aligned(k, kh, kt) || !rows_aligned(v, vh, vt) || (kc % 8) || (vc % 8))
+    return fail(DKV_EINVAL, "k/v rows must be 16-byte aligned (strides multiples of 8)");
+  if (2LL * heads * n * 8 > INT32_MAX) return fail(DKV_EINVAL, "frame too large");
+  for (int r = 0; r < count; ++r) {
+    const dkv_pack_target& t = targets[r];
+    if ((rc = check_pools(t.p4, t.m4, t.p8, t.m8, t.p16, t.cap4, t.cap8, t.cap16))) return rc;
+    if (t.bits != 4 && t.bits != 8 && t.bits != 16) return fail(DKV_EINVAL, "Supported bit widths: 4, 8, 16");
+    const int64_t cap = t.bits == 4 ? t.cap4 : (t.bits == 8 ? t.cap8 : t.cap16);
+    if (t.row_start < 0 || t.row_start + n > cap)
+      return fail(DKV_ECAPACITY, "request %d: rows [%lld, %lld) exceed the %d-bit pool capacity %lld", r,
+                  (long long)t.row_start, (long long)(t.row_start + n), t.bits, (long long)cap);
+    if (t.row_start + n > INT32_MAX) return fail(DKV_ECAPACITY, "pool row exceeds int32");
+    if ((t.map_rows == nullptr) != (t.map_codes == nullptr)) return fail(DKV_EINVAL, "half a token map");
+    if (t.map_rows != nullptr && (t.map_start < 0 || t.map_start + n > t.map_capacity))
+      return fail(DKV_ECAPACITY, "GPU context limit exceeded");
+  }
+  if (n == 0) return ok();
+  return cuda_status(dkv::launch_pack_many(k, v, targets, count, kh, kt, vh, vt, kc, vc, layer, n, heads,
+                                           static_cast<cudaStream_t>(stream)),
+                     "pack_rows_many launch");
+}
+
+size_t dkv_packed_attention_many_workspace(int32_t max_past, int32_t nq, int32_t heads, int32_t group, int32_t dim,
+                                           int32_t count) {
+  if (count <= 0 || count > DKV_MAX_REQUESTS) return 0;
+  return dkv_packed_attention_batched_workspace(max_past, nq, heads, group, dim, count);
+}
+
+int dkv_packed_attention_many(const void* q, const void* knew, const void* vnew, const dkv_history* requests,
+                              int32_t count, void* out, int64_t qh, int64_t qt, int64_t kh, int64_t kt, int64_t vh,
+                              int64_t vt, int64_t qc, int64_t kc, int64_t vc, int64_t oc, int32_t layer, int32_t nq,
+                              int32_t heads, int32_t group, int32_t dim, int32_t layers, void* workspace,
+                              size_t workspace_bytes, void* stream) {
+  int rc = check_geometry(heads, dim, layers, layer);
+  if (rc) return rc;
+  if (count <= 0 || count > DKV_MAX_REQUESTS)
+    return fail(DKV_EINVAL, "request count %d outside [1, %d]", count, DKV_MAX_REQUESTS);
+  if (requests == nullptr) return fail(DKV_EINVAL, "null request table");
+  if (group <= 0) return fail(DKV_EINVAL, "query heads must be a positive multiple of KV heads");
+  if (nq < 0) return fail(DKV_EINVAL, "negative past or query length");
+  if ((qc % 8) || (kc % 8) || (vc % 8) || (oc % 8))
+    return fail(DKV_EINVAL, "chunk strides must keep rows 16-byte aligned (multiples of 8 elements)");
+  dkv::HistoryTable table{};
+  int max_past = 0;
+  for (int r = 0; r < count; ++r) {
+    const dkv_history& h = requests[r];
+    if ((rc = check_pools(h.p4, h.m4, h.p8, h.m8, h.p16, h.cap4, h.cap8, h.cap16))) return rc;
+    if (h.past < 0) return fail(DKV_EINVAL, "negative past or query length");
+    if (h.past > 0 && (h.rows == nullptr || h.codes == nullptr)) return fail(DKV_EINVAL, "null token map");
+    if (h.past > 0 && (!aligned16(h.rows) || !aligned16(h.codes)))
+      return fail(DKV_EINVAL, "token maps must be 16-byte aligned");
+    table.h[r].P = dkv::Pools{static_cast<const uint8_t*>(h.p4), static_cast<const float2*>(h.m4),
+                              static_cast<const uint8_t*>(h.p8), static_cast<const float2*>(h.m8),
+                              static_cast<const uint16_t*>(h.p16), h.cap4, h.cap8, h.cap16, heads};
+    table.h[r].rows = h.rows;
+    table.h[r].codes = h.codes;
+    table.h[r].status = h.status;
+    table.h[r].past = h.past;
+    max_past = h.past > max_past ? h.past : max_past;
+  }
+  if (nq == 0) return ok();
+  if (!rows_aligned(q, qh, qt) || !rows_aligned(knew, kh, kt) || !rows_aligned(vnew, vh, vt))
+    return fail(DKV_EINVAL, "q/k/v rows must be 16-byte aligned (head/token strides multiples of 8)");
+  if (out == nullptr || !aligned16(out)) return fail(DKV_EINVAL, "out must be 16-byte aligned");
+  const dkv::AttnPlan p = dkv::make_plan(max_past, nq, heads, group, count);
+  const size_t need = p.workspace_bytes();
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need))
+    return fail(DKV_EWORKSPACE, "attention workspace needs %zu bytes, got %zu", need, workspace_bytes);
+  if (need > 0 && (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return fail(DKV_EWORKSPACE, "attention workspace must be 256-byte aligned");
+  dkv::AttnArgs a{};
+  a.hist = table.h[0];  // heads for the grid decomposition; chunks read the table
+  return launch_planned(a, p, q, knew, vnew, out, qh, qt, kh, kt, vh, vt, count, qc, kc, vc, oc, layer, nq, heads,
+                        group, workspace, stream, &table);
 }
 
 int dkv_reconstruct(const void* p4, const void* m4, const void* p8, const void* m8, const void* p16,

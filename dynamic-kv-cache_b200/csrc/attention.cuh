@@ -63,16 +63,34 @@ inline AttnPlan make_plan(int past, int nq, int heads, int group, int chunks = 1
   return p;
 }
 
+// One request's packed history: its pools, token maps (rows / codes per logical
+// token), history length and device status word.
+struct History {
+  Pools P;
+  const int32_t* rows;
+  const uint8_t* codes;
+  int32_t* status;
+  int past;
+};
+
+// Calls over several independent requests (request batching): query chunk c
+// attends over h[c], each request with its own pools, maps and history length.
+// Passed by value as a kernel parameter (3.3 KB), so a launch needs no device
+// copy of it. Without a table every chunk reads AttnArgs::hist.
+constexpr int kMaxRequests = 32;
+struct HistoryTable {
+  History h[kMaxRequests];
+};
+struct SharedHistory {};
+
 struct AttnArgs {
   const uint16_t* q;
   const uint16_t* knew;
   const uint16_t* vnew;
-  Pools P;
-  const int32_t* rows;
-  const uint8_t* codes;
+  History hist;   // the history of every chunk, unless a HistoryTable is given
   uint16_t* out;
   int64_t qh, qt, kh, kt, vh, vt;
-  int layer, past, nq, G, HQ;
+  int layer, nq, G, HQ;
   int mrows, cta_rows, mblocks, splits, chunk;
   // Batched calls: blockIdx.z = chunk * heads + KV head; chunk c's q / knew / vnew /
   // out start qc / kc / vc / oc elements after chunk 0's (0 for a single chunk).
@@ -81,8 +99,15 @@ struct AttnArgs {
   float2* ws_ml;  // [heads * mblocks][cta_rows][even(splits)] (running max in log2 units, sum)
   uint32_t* sync;  // [2][kSyncGroups] arrival / departure counters of the in-kernel merge
   int fused;       // 1: the attention kernel merges the splits itself (no combine launch)
-  int32_t* status;
 };
+
+// The history query chunk c attends over.
+__device__ __forceinline__ const History& history_of(const AttnArgs& a, const SharedHistory&, int) {
+  return a.hist;
+}
+__device__ __forceinline__ const History& history_of(const AttnArgs&, const HistoryTable& t, int c) {
+  return t.h[c];
+}
 
 // Partials of group grp (= KV head * mblocks + row block): for each row, every
 // split's 64 outputs side by side, so the splits of a run of rows are one
@@ -127,10 +152,12 @@ __device__ __forceinline__ float merge_row_weights(Load load, int splits, float*
   return den;
 }
 
-cudaError_t launch_attention_split(const AttnArgs& a, int heads, cudaStream_t stream);
+// `table` (may be null): per-chunk histories of a call over several requests.
+cudaError_t launch_attention_split(const AttnArgs& a, int heads, cudaStream_t stream,
+                                   const HistoryTable* table = nullptr);
 // Sets a.fused when every CTA of the grid can be resident at once (one CTA per SM):
 // the split merge then runs inside the kernel and no combine launch follows.
-cudaError_t launch_attention_tc(AttnArgs& a, int heads, cudaStream_t stream);
+cudaError_t launch_attention_tc(AttnArgs& a, int heads, cudaStream_t stream, const HistoryTable* table = nullptr);
 // Whether a call with this plan merges its splits inside the tensor-core kernel
 // on the current device (one launch) or needs the combine kernel (two).
 cudaError_t attention_tc_merges_in_kernel(const AttnPlan& p, int heads, bool* fused);

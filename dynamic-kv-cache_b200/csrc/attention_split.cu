@@ -55,9 +55,9 @@ __device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], 
 
 constexpr int kTileTasks = 2 * kBN * 8;  // (K|V) x 64 keys x 8 parts of 8 dims
 
-template <int NW>
+template <int NW, class Hist>
 __global__ void __launch_bounds__(NW * 32)
-attention_split_kernel(const AttnArgs a) {
+attention_split_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ Hist hist) {
   constexpr int kThreads = NW * 32;
   constexpr int kTPT = (kTileTasks + kThreads - 1) / kThreads;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -68,8 +68,9 @@ attention_split_kernel(const AttnArgs a) {
   const int split = blockIdx.x;
   const int mb = blockIdx.y;
   const int zc = blockIdx.z;  // chunk * heads + KV head
-  const int chunk = zc / a.P.heads;
-  const int g = zc - chunk * a.P.heads;
+  const int chunk = zc / a.hist.P.heads;
+  const int g = zc - chunk * a.hist.P.heads;
+  const History& H = history_of(a, hist, chunk);
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
@@ -78,8 +79,8 @@ attention_split_kernel(const AttnArgs a) {
   const int rows_here = min(a.cta_rows, a.mrows - row0);
   const int m_max = (row0 + rows_here - 1) / a.G;
   const int kb = split * a.chunk;
-  int ke = min(kb + a.chunk, a.past + a.nq);
-  ke = min(ke, a.past + m_max + 1);  // no row of this block sees further
+  int ke = min(kb + a.chunk, H.past + a.nq);
+  ke = min(ke, H.past + m_max + 1);  // no row of this block sees further
   const int ntiles = ke > kb ? (ke - kb + kBN - 1) / kBN : 0;
 
   // ---- Q block -> shared (zero rows past the end) ----
@@ -109,10 +110,10 @@ attention_split_kernel(const AttnArgs a) {
         const int part = task & 7;
         const int t = t0 + j;
         if (t < ke) {
-          if (t < a.past) {
-            pre[i] = load_history_part(a.P, a.rows, a.codes, a.layer, kv, g, t, part, a.status);
+          if (t < H.past) {
+            pre[i] = load_history_part(H.P, H.rows, H.codes, a.layer, kv, g, t, part, H.status);
           } else {
-            const int tn = t - a.past;
+            const int tn = t - H.past;
             const uint16_t* src = kv == 0 ? a.knew + chunk * a.kc + g * a.kh + tn * a.kt
                                           : a.vnew + chunk * a.vc + g * a.vh + tn * a.vt;
             pre[i].raw = __ldg(reinterpret_cast<const uint4*>(src) + part);
@@ -141,8 +142,8 @@ attention_split_kernel(const AttnArgs a) {
   // Rows of this thread inside the block: ra (fragment rows 0-7) and ra + 8.
   const int ra = warp * 16 + (lane >> 2);
   const int rb = ra + 8;
-  const int lim_a = a.past + min(row0 + ra, a.mrows - 1) / a.G;  // last visible key
-  const int lim_b = a.past + min(row0 + rb, a.mrows - 1) / a.G;
+  const int lim_a = H.past + min(row0 + ra, a.mrows - 1) / a.G;  // last visible key
+  const int lim_b = H.past + min(row0 + rb, a.mrows - 1) / a.G;
 
   float o[8][4];
 #pragma unroll
@@ -296,13 +297,13 @@ attention_split_kernel(const AttnArgs a) {
 // order): the same bits either way. A warp per row finds the weights; then one
 // thread per (row, dim) sums its column, 16 partial loads in flight at a time,
 // and stores its bf16 output (a warp writes 64 contiguous bytes).
-__global__ void __launch_bounds__(256) attention_combine_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(256) attention_combine_kernel(const __grid_constant__ AttnArgs a) {
   __shared__ float s_w[4 * kTargetCtas], s_den[4];
   ptx::pdl_wait();  // partials of the attention grid
   ptx::pdl_trigger();
   const int zc = blockIdx.z;  // chunk * heads + KV head
-  const int chunk = zc / a.P.heads;
-  const int g = zc - chunk * a.P.heads;
+  const int chunk = zc / a.hist.P.heads;
+  const int g = zc - chunk * a.hist.P.heads;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int fr0 = blockIdx.x * 4;
   if (warp < 4 && fr0 + warp < a.mrows) {
@@ -344,32 +345,38 @@ __global__ void __launch_bounds__(256) attention_combine_kernel(const AttnArgs a
       static_cast<uint16_t>(pack_bf16x2(val, 0.f) & 0xffffu);
 }
 
-template <int NW>
-cudaError_t launch_nw(const AttnArgs& a, int heads, size_t smem, cudaStream_t stream) {
+template <int NW, class Hist>
+cudaError_t launch_nw(const AttnArgs& a, const Hist& hist, int heads, size_t smem, cudaStream_t stream) {
   static bool configured[64] = {};  // the attribute is set once per device
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!configured[dev]) {
-    e = cudaFuncSetAttribute(attention_split_kernel<NW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(attention_split_kernel<NW, Hist>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              96 * 1024);
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
   dim3 grid(a.splits, a.mblocks, heads);
-  attention_split_kernel<NW><<<grid, NW * 32, smem, stream>>>(a);
+  attention_split_kernel<NW, Hist><<<grid, NW * 32, smem, stream>>>(a, hist);
   return cudaGetLastError();
+}
+
+template <class Hist>
+cudaError_t launch_split(const AttnArgs& a, const Hist& hist, int heads, cudaStream_t stream) {
+  const int cw = a.cta_rows / 16;
+  const size_t smem = static_cast<size_t>(a.cta_rows) * 128 + 4 * kBN * 128;
+  if (cw <= 4) return launch_nw<4>(a, hist, heads, smem, stream);
+  if (cw <= 8) return launch_nw<8>(a, hist, heads, smem, stream);
+  return launch_nw<12>(a, hist, heads, smem, stream);
 }
 
 }  // namespace
 
-cudaError_t launch_attention_split(const AttnArgs& a, int heads, cudaStream_t stream) {
-  const int cw = a.cta_rows / 16;
-  const size_t smem = static_cast<size_t>(a.cta_rows) * 128 + 4 * kBN * 128;
-  if (cw <= 4) return launch_nw<4>(a, heads, smem, stream);
-  if (cw <= 8) return launch_nw<8>(a, heads, smem, stream);
-  return launch_nw<12>(a, heads, smem, stream);
+cudaError_t launch_attention_split(const AttnArgs& a, int heads, cudaStream_t stream, const HistoryTable* table) {
+  if (table != nullptr) return launch_split(a, *table, heads, stream);
+  return launch_split(a, SharedHistory{}, heads, stream);
 }
 
 cudaError_t launch_attention_combine(const AttnArgs& a, int heads, cudaStream_t stream) {

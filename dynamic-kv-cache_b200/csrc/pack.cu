@@ -13,31 +13,16 @@
 namespace dkv {
 
 constexpr int kPackThreads = 256;
+constexpr int kMaxPackRequests = DKV_MAX_REQUESTS;
 
+// Quantises part `part` (dims 8*part .. 8*part+7) of one 64-wide row held in
+// `raw` (8 bf16) and stores it at row `out_row` of pool block `block` (the
+// (layer, K|V, head) slab of `cap` rows). The eight lanes of a row must call it
+// together (row min/max by shuffles within the 8-lane group).
 template <int BITS>
-__global__ void __launch_bounds__(kPackThreads)
-pack_rows_kernel(const uint16_t* __restrict__ k, const uint16_t* __restrict__ v,
-                 uint8_t* __restrict__ p4, float2* __restrict__ m4, uint8_t* __restrict__ p8,
-                 float2* __restrict__ m8, uint16_t* __restrict__ p16, int64_t kh, int64_t kt,
-                 int64_t vh, int64_t vt, int layer, int64_t row_start, int n, int64_t cap,
-                 int heads, int32_t* status) {
-  // Launched as a programmatic dependent: the next kernel (the frame's attention,
-  // which reads the new K/V natively and only history rows of the pools) may start
-  // streaming history at once; k / v are the previous kernels' output.
-  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
-  asm volatile("griddepcontrol.wait;\n" ::: "memory");
-  const int gtid = blockIdx.x * blockDim.x + threadIdx.x;
-  const int row = gtid >> 3;
-  const int part = gtid & 7;
-  const int per_kv = heads * n;
-  if (row >= 2 * per_kv) return;  // whole 8-lane groups leave together
-  const int kv = row / per_kv;
-  const int rem = row - kv * per_kv;
-  const int head = rem / n;
-  const int token = rem - head * n;
-  const uint16_t* src = kv == 0 ? k + head * kh + token * kt : v + head * vh + token * vt;
-  const uint4 raw = __ldg(reinterpret_cast<const uint4*>(src) + part);
-
+__device__ __forceinline__ void pack_row_part(uint4 raw, int part, uint8_t* p4, float2* m4, uint8_t* p8,
+                                              float2* m8, uint16_t* p16, int64_t block, int64_t cap,
+                                              int64_t out_row, int32_t* status, int report_row) {
   float x[8];
   x[0] = bf16_lo(raw.x); x[1] = bf16_hi(raw.x);
   x[2] = bf16_lo(raw.y); x[3] = bf16_hi(raw.y);
@@ -46,10 +31,8 @@ pack_rows_kernel(const uint16_t* __restrict__ k, const uint16_t* __restrict__ v,
   bool finite = true;
 #pragma unroll
   for (int i = 0; i < 8; ++i) finite &= isfinite(x[i]);
-  if (!finite) report(status, DKV_ENONFINITE, row);
+  if (!finite) report(status, DKV_ENONFINITE, report_row);
 
-  const int64_t out_row = row_start + token;
-  const int64_t block = (static_cast<int64_t>(layer) * 2 + kv) * heads + head;
   if (BITS == 16) {
     reinterpret_cast<uint4*>(p16 + (block * cap + out_row) * kDim)[part] = raw;
     return;
@@ -91,6 +74,82 @@ pack_rows_kernel(const uint16_t* __restrict__ k, const uint16_t* __restrict__ v,
     for (int j = 0; j < 4; ++j) w |= (q[2 * j] | (q[2 * j + 1] << 4)) << (8 * j);
     reinterpret_cast<uint32_t*>(p4 + (block * cap + out_row) * kRowBytes4)[part] = w;
     if (part == 0) m4[block * cap + out_row] = make_float2(offset, scale);
+  }
+}
+
+template <int BITS>
+__global__ void __launch_bounds__(kPackThreads)
+pack_rows_kernel(const uint16_t* __restrict__ k, const uint16_t* __restrict__ v,
+                 uint8_t* __restrict__ p4, float2* __restrict__ m4, uint8_t* __restrict__ p8,
+                 float2* __restrict__ m8, uint16_t* __restrict__ p16, int64_t kh, int64_t kt,
+                 int64_t vh, int64_t vt, int layer, int64_t row_start, int n, int64_t cap,
+                 int heads, int32_t* status) {
+  // Launched as a programmatic dependent: the next kernel (the frame's attention,
+  // which reads the new K/V natively and only history rows of the pools) may start
+  // streaming history at once; k / v are the previous kernels' output.
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
+  const int gtid = blockIdx.x * blockDim.x + threadIdx.x;
+  const int row = gtid >> 3;
+  const int part = gtid & 7;
+  const int per_kv = heads * n;
+  if (row >= 2 * per_kv) return;  // whole 8-lane groups leave together
+  const int kv = row / per_kv;
+  const int rem = row - kv * per_kv;
+  const int head = rem / n;
+  const int token = rem - head * n;
+  const uint16_t* src = kv == 0 ? k + head * kh + token * kt : v + head * vh + token * vt;
+  const uint4 raw = __ldg(reinterpret_cast<const uint4*>(src) + part);
+  const int64_t block = (static_cast<int64_t>(layer) * 2 + kv) * heads + head;
+  pack_row_part<BITS>(raw, part, p4, m4, p8, m8, p16, block, cap, row_start + token, status, row);
+}
+
+// Per-request destinations of pack_rows_many_kernel (dkv_pack_target, by value).
+struct PackTable {
+  dkv_pack_target t[kMaxPackRequests];
+};
+
+static_assert(sizeof(PackTable) + 128 <= 4096, "pack_rows_many_kernel parameters");
+
+// Frames of several requests in one launch: blockIdx.y = request, each with its
+// own precision (uniform over a block, so the branch below does not diverge),
+// pools and optional token-map update.
+__global__ void __launch_bounds__(kPackThreads)
+pack_rows_many_kernel(const uint16_t* __restrict__ k, const uint16_t* __restrict__ v,
+                      const __grid_constant__ PackTable tab, int64_t kh, int64_t kt, int64_t vh, int64_t vt,
+                      int64_t kc, int64_t vc, int layer, int n, int heads) {
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
+  const dkv_pack_target& d = tab.t[blockIdx.y];
+  const int gtid = blockIdx.x * blockDim.x + threadIdx.x;
+  const int row = gtid >> 3;
+  const int part = gtid & 7;
+  const int per_kv = heads * n;
+  if (row >= 2 * per_kv) return;
+  const int kv = row / per_kv;
+  const int rem = row - kv * per_kv;
+  const int head = rem / n;
+  const int token = rem - head * n;
+  const uint16_t* src = kv == 0 ? k + blockIdx.y * kc + head * kh + token * kt
+                                : v + blockIdx.y * vc + head * vh + token * vt;
+  const uint4 raw = __ldg(reinterpret_cast<const uint4*>(src) + part);
+  const int64_t block = (static_cast<int64_t>(layer) * 2 + kv) * heads + head;
+  const int64_t out_row = d.row_start + token;
+  uint8_t* p4 = static_cast<uint8_t*>(d.p4);
+  uint8_t* p8 = static_cast<uint8_t*>(d.p8);
+  float2* m4 = static_cast<float2*>(d.m4);
+  float2* m8 = static_cast<float2*>(d.m8);
+  uint16_t* p16 = static_cast<uint16_t*>(d.p16);
+  if (d.bits == 4) {
+    pack_row_part<4>(raw, part, p4, m4, p8, m8, p16, block, d.cap4, out_row, d.status, row);
+  } else if (d.bits == 8) {
+    pack_row_part<8>(raw, part, p4, m4, p8, m8, p16, block, d.cap8, out_row, d.status, row);
+  } else {
+    pack_row_part<16>(raw, part, p4, m4, p8, m8, p16, block, d.cap16, out_row, d.status, row);
+  }
+  if (d.map_rows != nullptr && kv == 0 && head == 0 && part == 0) {
+    d.map_rows[d.map_start + token] = static_cast<int32_t>(out_row);
+    d.map_codes[d.map_start + token] = static_cast<uint8_t>(d.bits);
   }
 }
 
@@ -147,6 +206,25 @@ cudaError_t launch_pack(const void* k, const void* v, void* p4, void* m4, void* 
   auto kernel = bits == 4 ? pack_rows_kernel<4> : (bits == 8 ? pack_rows_kernel<8> : pack_rows_kernel<16>);
   return cudaLaunchKernelEx(&cfg, kernel, kk, vv, q4, s4, q8, s8, h, kh, kt, vh, vt, layer, row_start, n, cap,
                             heads, status);
+}
+
+cudaError_t launch_pack_many(const void* k, const void* v, const dkv_pack_target* targets, int count, int64_t kh,
+                             int64_t kt, int64_t vh, int64_t vt, int64_t kc, int64_t vc, int layer, int n, int heads,
+                             cudaStream_t stream) {
+  PackTable tab{};
+  for (int r = 0; r < count; ++r) tab.t[r] = targets[r];
+  const int threads = 2 * heads * n * 8;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((threads + kPackThreads - 1) / kPackThreads, count);
+  cfg.blockDim = dim3(kPackThreads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, pack_rows_many_kernel, static_cast<const uint16_t*>(k),
+                            static_cast<const uint16_t*>(v), tab, kh, kt, vh, vt, kc, vc, layer, n, heads);
 }
 
 cudaError_t launch_reconstruct(const Pools& P, const int32_t* rows, const uint8_t* codes, void* out,

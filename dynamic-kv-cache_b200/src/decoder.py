@@ -15,7 +15,7 @@ from dataclasses import dataclass
 import torch
 import torch.nn.functional as F
 
-from .gpu_cache import GPUCache
+from .gpu_cache import GPUCache, append_many, attend_many
 from .gpu_ops import activation_product, cuda_rms
 
 
@@ -137,6 +137,45 @@ class Decoder(torch.nn.Module):
             mask = torch.arange(past + n, device=x.device)[None, :] <= past + torch.arange(n, device=x.device)[:, None]
             out = F.scaled_dot_product_attention(q, k, v, attn_mask=mask, enable_gqa=True).transpose(1, 2)
         return F.linear(out.reshape(b, n, -1), self.o[layer])
+
+    def attention_many(self, x, layer, caches, cos, sin):
+        """Attention of B requests' frames x [B, n, hidden], request r over caches[r],
+        appending each frame's K/V to its own cache (one pack and one attention
+        launch for all of them)."""
+        c = self.cfg
+        b, n = x.shape[0], x.shape[1]
+        q, k, v = F.linear(x, self.qkv[layer]).split(
+            [c.q_heads * c.head_dim, c.kv_heads * c.head_dim, c.kv_heads * c.head_dim], dim=-1)
+        q = q.view(b, n, c.q_heads, c.head_dim).transpose(1, 2)
+        k = k.view(b, n, c.kv_heads, c.head_dim).transpose(1, 2)
+        v = v.view(b, n, c.kv_heads, c.head_dim).transpose(1, 2)
+        q, k = apply_rope(q, cos, sin), apply_rope(k, cos, sin)
+        pasts = append_many(caches, k, v, layer)
+        out = attend_many(caches, q, k, v, layer, pasts)  # [B, n, q_heads, d]
+        return F.linear(out.reshape(b, n, -1), self.o[layer])
+
+    def forward_many(self, caches, ids=None, embeds=None, logits=0):
+        """forward() for B independent requests stepped together (request batching,
+        not in the reference): ids [B, n] or embeds [B, n, hidden], request r appended
+        to caches[r] (GPUCache objects with their own pools; their histories may
+        differ in length). Returns fp32 logits [B, logits, vocab] (or None)."""
+        x = self.embed[ids] if embeds is None else embeds
+        b, n = x.shape[0], x.shape[1]
+        if len(caches) != b:
+            raise ValueError('one cache per request')
+        pasts = torch.tensor([c.get_seq_length(0) for c in caches], device=x.device)
+        positions = pasts[:, None] + torch.arange(n, device=x.device)[None, :]  # [B, n]
+        cos, sin = rope_tables(self.cfg, positions.reshape(-1), x.device)
+        cos, sin = cos.view(b, 1, n, -1), sin.view(b, 1, n, -1)
+        for layer in range(self.cfg.layers):
+            x = x + self.attention_many(self.rms(x, self.norm_attn[layer]), layer, caches, cos, sin)
+            h = self.rms(x, self.norm_mlp[layer])
+            gate, up = F.linear(h, self.gate_up[layer]).chunk(2, dim=-1)
+            x = x + F.linear(activation_product(gate, up), self.down[layer])
+        if not logits:
+            return None
+        h = self.rms(x[:, -logits:], self.norm_out)
+        return F.linear(h, self.embed).float()
 
     def forward_chunks(self, cache, ids, logits):
         """B equal-length token chunks (ids [B, n]) after the cache's history, side by

@@ -113,10 +113,11 @@ class GPUCache(DynamicCache):
         self.seen[layer] = past + n
         return past
 
-    def _claim(self, layer, n):
+    def _claim(self, layer, n, fill_map=True):
         """Plan bookkeeping of an n-token append to `layer` at the selected precision
         (src/gpu_cache.py:72-90): returns (past, n, first pool row); the caller
-        writes the rows and advances seen[layer]."""
+        writes the rows and advances seen[layer]. With fill_map=False the token
+        map update of a new online segment is left to the caller's pack launch."""
         past = self.seen[layer]
         if past + n > self.capacity:
             raise ValueError('GPU context limit exceeded')
@@ -126,7 +127,8 @@ class GPUCache(DynamicCache):
                 self.reserve(self.pending_bits, row + n)
                 self.plan.append((past, past + n, self.pending_bits, row))
                 self.host_counts[self.pending_bits] += n
-                K.map_fill(self.rows, self.codes, past, n, row, self.pending_bits, self.capacity)
+                if fill_map:
+                    K.map_fill(self.rows, self.codes, past, n, row, self.pending_bits, self.capacity)
             segment = self.plan[-1]
         else:
             cursor = self.cursors[layer]
@@ -259,3 +261,70 @@ def install_packed_attention(model):
         if module.__class__.__name__ == 'LlamaAttention' and not hasattr(module, '_original_forward'):
             module._original_forward = module.forward
             module.forward = types.MethodType(forward, module)
+
+
+# -- request batching (not in the reference) -------------------------------------
+# The reference serves one request per GPUCache and launches pack and attention
+# once per request and layer. These functions step B independent caches together:
+# one pack launch and one attention launch per layer for all of them (in launches
+# of at most K.MAX_REQUESTS requests), so the model around the cache runs its
+# projections and MLP on B frames at once.
+
+def _same_geometry(caches):
+    if not caches:
+        raise ValueError('no caches')
+    first = caches[0]
+    for c in caches:
+        if (c.layers, c.heads, c.dim, c.device) != (first.layers, first.heads, first.dim, first.device):
+            raise ValueError('batched caches must share layers, heads, head_dim and device')
+    return first
+
+
+def append_many(caches, k, v, layer):
+    """Packs one frame per cache for `layer`: k / v [B, heads, n, dim], request r into
+    caches[r] at that cache's selected precision (each one as GPUCache.append would:
+    bit-identical pools and maps). Returns the history lengths before the frame."""
+    first = _same_geometry(caches)
+    b, n = len(caches), k.shape[-2]
+    if k.shape[0] != b or v.shape[0] != b or k.shape[1] != first.heads or k.shape[-1] != first.dim \
+            or k.device.type != 'cuda':
+        raise ValueError('GPU cache requires CUDA, one frame per cache and the configured head dimension')
+    if len({c.p16.data_ptr() for c in caches}) != b:
+        # a cache listed twice, or forks of one cache (they write the same reserved rows)
+        raise ValueError('batched appends need caches with their own pools')
+    targets, claims = [], []
+    for c in caches:
+        new_segment = c.online and layer == 0
+        past, n, row = c._claim(layer, n, fill_map=False)
+        claims.append(past)
+        targets.append(K.PackTarget(
+            c.p4.data_ptr(), c.m4.data_ptr(), c.p8.data_ptr(), c.m8.data_ptr(), c.p16.data_ptr(),
+            c.caps[4], c.caps[8], c.caps[16], row, c.pending_bits, 0,
+            c.rows.data_ptr() if new_segment else None, c.codes.data_ptr() if new_segment else None,
+            past, c.capacity, c.status.data_ptr()))
+    for s in range(0, b, K.MAX_REQUESTS):
+        e = min(s + K.MAX_REQUESTS, b)
+        K.pack_rows_many(k[s:e], v[s:e], targets[s:e], layer, n, first.heads, first.dim, first.layers)
+    for c, past in zip(caches, claims):
+        c.seen[layer] = past + n
+    return claims
+
+
+def attend_many(caches, q, k, v, layer, pasts):
+    """Causal GQA attention of each cache's n new queries over its own packed history
+    (pasts[r] tokens) plus its own new K/V: q [B, query_heads, n, dim], k / v
+    [B, heads, n, dim]; returns [B, n, query_heads, dim]."""
+    first = _same_geometry(caches)
+    b, hq, n, _ = q.shape
+    if len(pasts) != b or hq % first.heads:
+        raise ValueError('one past per cache; query heads must be a multiple of KV heads')
+    out = torch.empty((b, n, hq, first.dim), dtype=q.dtype, device=q.device)
+    hist = [K.History(c.p4.data_ptr(), c.m4.data_ptr(), c.p8.data_ptr(), c.m8.data_ptr(), c.p16.data_ptr(),
+                      c.rows.data_ptr(), c.codes.data_ptr(), c.caps[4], c.caps[8], c.caps[16], past,
+                      c.status.data_ptr())
+            for c, past in zip(caches, pasts)]
+    for s in range(0, b, K.MAX_REQUESTS):
+        e = min(s + K.MAX_REQUESTS, b)
+        K.packed_attention_many(q[s:e], k[s:e], v[s:e], hist[s:e], out[s:e], layer, n, first.heads,
+                                hq // first.heads, first.dim, first.layers)
+    return out

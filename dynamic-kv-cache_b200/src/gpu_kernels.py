@@ -27,6 +27,23 @@ STATUS_NAMES = {DKV_EINVAL: 'invalid argument', DKV_ECAPACITY: 'capacity exceede
                 DKV_ETIMEOUT: 'kernel pipeline wait timed out'}
 
 
+_P, _I32, _I64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64
+MAX_REQUESTS = 32  # DKV_MAX_REQUESTS
+
+
+class History(ctypes.Structure):
+    """dkv_history: one request's packed history for packed_attention_many."""
+    _fields_ = [('p4', _P), ('m4', _P), ('p8', _P), ('m8', _P), ('p16', _P), ('rows', _P), ('codes', _P),
+                ('cap4', _I64), ('cap8', _I64), ('cap16', _I64), ('past', _I32), ('status', _P)]
+
+
+class PackTarget(ctypes.Structure):
+    """dkv_pack_target: one request's destination for pack_rows_many."""
+    _fields_ = [('p4', _P), ('m4', _P), ('p8', _P), ('m8', _P), ('p16', _P), ('cap4', _I64), ('cap8', _I64),
+                ('cap16', _I64), ('row_start', _I64), ('bits', _I32), ('reserved', _I32), ('map_rows', _P),
+                ('map_codes', _P), ('map_start', _I64), ('map_capacity', _I64), ('status', _P)]
+
+
 def _load():
     if not _LIB_PATH.exists():
         raise ImportError(f'{_LIB_PATH} is not built; run `python __graft_entry__.py build` '
@@ -50,6 +67,11 @@ def _load():
         'dkv_reconstruct': ([P, P, P, P, P, P, P, P, I32, I32, I64, I64, I64, I32, I32, I32, P, P],
                             ctypes.c_int),
         'dkv_map_fill': ([P, P, I64, I32, I64, I32, I64, P], ctypes.c_int),
+        'dkv_pack_rows_many': ([P, P, P, I32, I64, I64, I64, I64, I64, I64, I32, I32, I32, I32, I32, P],
+                               ctypes.c_int),
+        'dkv_packed_attention_many': ([P, P, P, P, I32, P, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64,
+                                       I32, I32, I32, I32, I32, I32, P, SZ, P], ctypes.c_int),
+        'dkv_packed_attention_many_workspace': ([I32, I32, I32, I32, I32, I32], SZ),
     }
     for name, (args, res) in sigs.items():
         fn = getattr(lib, name)
@@ -60,7 +82,8 @@ def _load():
 LIB = _load()
 EXPORTS = ('dkv_version', 'dkv_last_error', 'dkv_pack_rows', 'dkv_packed_attention',
            'dkv_packed_attention_workspace', 'dkv_packed_attention_launches', 'dkv_packed_attention_batched',
-           'dkv_packed_attention_batched_workspace', 'dkv_reconstruct', 'dkv_map_fill')
+           'dkv_packed_attention_batched_workspace', 'dkv_reconstruct', 'dkv_map_fill', 'dkv_pack_rows_many',
+           'dkv_packed_attention_many', 'dkv_packed_attention_many_workspace')
 
 
 def _check(rc):
@@ -160,6 +183,44 @@ def packed_attention_batched(q, knew, vnew, p4, m4, p8, m8, p16, rows, codes, ou
         vnew.stride(2), chunks, q.stride(0), knew.stride(0), vnew.stride(0), out.stride(0), layer, past, nq,
         cap4, cap8, cap16, heads, group, dim, block_m, block_n, layers, _ptr(workspace), size, _ptr(status),
         _stream(q)))
+    return out
+
+
+def _chunked(x, name):
+    if x.shape[0] and x.stride(0) % 8:
+        raise ValueError(f'{name}: the request dimension must step in multiples of 8 elements')
+
+
+def pack_rows_many(k, v, targets, layer, n, heads, dim, layers):
+    """Frames of len(targets) requests in one launch: k / v [B, heads, n, dim] (request r
+    packed into targets[r], a PackTarget). No reference counterpart (request batching)."""
+    k, v = _rows_ready(k), _rows_ready(v)
+    _chunked(k, 'k'), _chunked(v, 'v')
+    if len(targets) != k.shape[0] or len(targets) != v.shape[0]:
+        raise ValueError('one pack target per request')
+    table = (PackTarget * len(targets))(*targets)
+    _check(LIB.dkv_pack_rows_many(_ptr(k), _ptr(v), ctypes.addressof(table), len(targets), k.stride(1),
+                                  k.stride(2), v.stride(1), v.stride(2), k.stride(0), v.stride(0), layer, n,
+                                  heads, dim, layers, _stream(k)))
+
+
+def packed_attention_many(q, knew, vnew, histories, out, layer, nq, heads, group, dim, layers):
+    """len(histories) requests in one launch: q [B, heads*group, nq, dim] and knew / vnew
+    [B, heads, nq, dim] of request r attend over histories[r] (a History); out
+    [B, nq, heads*group, dim]. No reference counterpart (request batching)."""
+    q, knew, vnew = (_rows_ready(x) for x in (q, knew, vnew))
+    for x, name in ((q, 'q'), (knew, 'k'), (vnew, 'v'), (out, 'out')):
+        if x.shape[0] != len(histories):
+            raise ValueError('one history per request')
+        _chunked(x, name)
+    count = len(histories)
+    table = (History * count)(*histories)
+    size = LIB.dkv_packed_attention_many_workspace(max(h.past for h in histories), nq, heads, group, dim, count)
+    workspace = _workspace(q.device, _stream(q), size) if size else None
+    _check(LIB.dkv_packed_attention_many(
+        _ptr(q), _ptr(knew), _ptr(vnew), ctypes.addressof(table), count, _ptr(out), q.stride(1), q.stride(2),
+        knew.stride(1), knew.stride(2), vnew.stride(1), vnew.stride(2), q.stride(0), knew.stride(0),
+        vnew.stride(0), out.stride(0), layer, nq, heads, group, dim, layers, _ptr(workspace), size, _stream(q)))
     return out
 
 

@@ -97,6 +97,64 @@ class StreamingModel:
         values = means.tolist()
         return dict(scores=values, summed=sums.tolist(), prediction=max(range(len(values)), key=values.__getitem__))
 
+    @torch.inference_mode()
+    def ingest_many(self, frames, bits, mode, qa_reserve=192):
+        """ingest() for B requests stepped together (request batching, not in the
+        reference): frames[r] / bits[r] are request r's frame embeddings and
+        precisions; every request has the same number of frames and frame
+        lengths. Each frame step runs the B frames through the decoder at once,
+        every request appended to its own cache. Returns the B caches."""
+        b = len(frames)
+        if b == 0 or len(bits) != b or len({len(f) for f in frames}) != 1:
+            raise ValueError('request batching needs one bit list per request and equal frame counts')
+        if mode == 'native':
+            return [self.ingest(f, bt, mode, qa_reserve) for f, bt in zip(frames, bits)]
+        caches = [self.create_cache([f.shape[1] for f in fr], mode, qa_reserve) for fr in frames]
+        self.model.forward_many(caches, ids=self.prefix_ids.expand(b, -1))
+        for i in range(len(frames[0])):
+            step = [fr[i] for fr in frames]
+            if len({e.shape[1] for e in step}) != 1:
+                raise ValueError('request batching needs equal frame lengths at each step')
+            for cache, bt in zip(caches, bits):
+                cache.select(bt[i], i)
+            self.model.forward_many(caches, embeds=torch.cat(step, dim=0))
+        for cache in caches:
+            cache.select(16, -1)
+            cache.reserve(16, cache.host_counts[16] + qa_reserve)
+            if len(set(cache.seen)) != 1:
+                raise RuntimeError('Decoder layers disagree about the cache length')
+        return caches
+
+    @torch.inference_mode()
+    def answer_many(self, questions, candidates, caches):
+        """answer() (the reference's candidate protocol) for B requests at once:
+        candidate j of every request runs on a fork of that request's cache, the B
+        forks in one batched forward. questions[r] [1, q], candidates[r] a list of
+        [1, c] ids; every request has the same question and candidate lengths.
+        Returns one answer() dict per request."""
+        b = len(caches)
+        if len(questions) != b or len(candidates) != b or len({len(c) for c in candidates}) != 1:
+            raise ValueError('one question and the same number of candidates per request')
+        if not all(isinstance(c, GPUCache) for c in caches):
+            return [self.answer(q, c, cache) for q, c, cache in zip(questions, candidates, caches)]
+        means = [[] for _ in range(b)]
+        sums = [[] for _ in range(b)]
+        for j in range(len(candidates[0])):
+            answers = [c[j] for c in candidates]
+            ids = torch.cat([torch.cat((q, a), dim=1) for q, a in zip(questions, answers)], dim=0)  # [B, q + c]
+            forks = [cache.fork() for cache in caches]
+            logits = self.model.forward_many(forks, ids=ids, logits=answers[0].shape[1] + 1)
+            target = torch.cat(answers, dim=0)                                                  # [B, c]
+            ll = logits[:, :-1].log_softmax(-1).gather(2, target[..., None])[..., 0]           # [B, c]
+            for r in range(b):
+                means[r].append(ll[r].mean())
+                sums[r].append(ll[r].sum())
+        out = []
+        for r in range(b):
+            values = torch.stack(means[r]).tolist()
+            out.append(dict(scores=values, summed=torch.stack(sums[r]).tolist(),
+                            prediction=max(range(len(values)), key=values.__getitem__)))
+        return out
 
     def _answer_batched(self, question_ids, candidate_ids, cache):
         fork = cache.fork()

@@ -186,6 +186,85 @@ int dkv_packed_attention_noalloc(const void* q, const void* knew, const void* vn
                                  int32_t layers, int32_t* status, void* stream);
 
 /*
+ * ---- Request batching (no reference counterpart) ----
+ * The reference serves one request per cache and launches pack and attention
+ * once per request and layer. The entry points below take B independent
+ * requests, each with its own pools, token maps and history length, and do the
+ * work of all of them in one launch per layer: the frame appends of B streams
+ * then share every weight read and every launch of the model around the cache.
+ * At most DKV_MAX_REQUESTS requests per call (larger batches are split by the
+ * caller); the descriptors are passed to the kernels by value, so the arrays
+ * below are read on the host during the call and may be reused right after.
+ */
+#define DKV_MAX_REQUESTS 32
+
+/* One request's packed history, as read by dkv_packed_attention_many. */
+typedef struct dkv_history {
+  const void* p4;  /* pools and (offset, scale) metadata of this request, */
+  const void* m4;  /* laid out as for dkv_packed_attention                */
+  const void* p8;
+  const void* m8;
+  const void* p16;
+  const int32_t* rows;   /* token map: pool row of logical token t */
+  const uint8_t* codes;  /* token map: precision (4 / 8 / 16) of token t */
+  int64_t cap4, cap8, cap16;
+  int32_t past;          /* packed history tokens before this call's queries */
+  int32_t* status;       /* this request's device status word (may be NULL) */
+} dkv_history;
+
+/* One request's destination, as written by dkv_pack_rows_many. */
+typedef struct dkv_pack_target {
+  void* p4;
+  void* m4;
+  void* p8;
+  void* m8;
+  void* p16;
+  int64_t cap4, cap8, cap16;
+  int64_t row_start;     /* first row of the `bits` pool that the frame fills */
+  int32_t bits;          /* 4, 8 or 16 for this request's frame */
+  int32_t reserved;
+  int32_t* map_rows;     /* when not NULL: also writes the token map entries */
+  uint8_t* map_codes;    /* map_rows[map_start + i] = row_start + i and */
+  int64_t map_start;     /* map_codes[map_start + i] = bits, i in [0, n) */
+  int64_t map_capacity;  /* length of map_rows / map_codes */
+  int32_t* status;       /* this request's device status word (may be NULL) */
+} dkv_pack_target;
+
+/*
+ * dkv_pack_rows for `count` requests in one launch: request r's frame is
+ * k + r*kc, v + r*vc (bf16 [heads, n, dim] with strides (kh, kt), (vh, vt); kc and
+ * vc multiples of 8), packed at targets[r].bits into targets[r]'s pools. Every
+ * row is quantised exactly as dkv_pack_rows does it (bit-identical pools). With
+ * map pointers set it also performs dkv_map_fill's update (done once, at layer
+ * 0, by GPUCache-style callers).
+ */
+int dkv_pack_rows_many(const void* k, const void* v, const dkv_pack_target* targets, int32_t count,
+                       int64_t kh, int64_t kt, int64_t vh, int64_t vt, int64_t kc, int64_t vc,
+                       int32_t layer, int32_t n, int32_t heads, int32_t dim, int32_t layers,
+                       void* stream);
+
+/*
+ * dkv_packed_attention for `count` requests in one launch: request r's nq queries
+ * (q + r*qc, bf16 [heads*group, nq, dim], strides (qh, qt)) attend causally over
+ * requests[r]'s packed history (requests[r].past tokens; pasts may differ) plus
+ * their own nq new K/V rows (knew + r*kc, vnew + r*vc) read natively; the output
+ * goes to out + r*oc as bf16 [nq, heads*group, dim]. Chunk strides are multiples
+ * of 8 elements. Same workspace contract as dkv_packed_attention, sized by
+ * dkv_packed_attention_many_workspace() for the largest past of the batch.
+ */
+int dkv_packed_attention_many(const void* q, const void* knew, const void* vnew,
+                              const dkv_history* requests, int32_t count, void* out,
+                              int64_t qh, int64_t qt, int64_t kh, int64_t kt, int64_t vh, int64_t vt,
+                              int64_t qc, int64_t kc, int64_t vc, int64_t oc,
+                              int32_t layer, int32_t nq, int32_t heads, int32_t group, int32_t dim,
+                              int32_t layers, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Workspace bytes dkv_packed_attention_many needs (0 = none); max_past = the
+ * largest requests[r].past of the call. */
+size_t dkv_packed_attention_many_workspace(int32_t max_past, int32_t nq, int32_t heads, int32_t group,
+                                           int32_t dim, int32_t count);
+
+/*
  * Dequantised bf16 history of one layer: out[2, heads, n, dim] (K then V) for
  * logical tokens [0, n). Replaces Triton `reconstruct` (src/gpu_kernels.py:
  * 107-119), launched by GPUCache.materialize (src/gpu_cache.py:106-112).

@@ -67,3 +67,55 @@ def test_map_fill_capacity_is_the_reference_context_limit_message():
     from src import gpu_kernels as K
     rc = K.LIB.dkv_map_fill(0x1000, 0x2000, 8190, 64, 0, 16, 8192, None)
     assert rc == K.DKV_ECAPACITY and K.LIB.dkv_last_error().decode() == 'GPU context limit exceeded'
+
+
+def test_request_descriptor_layouts_match_the_header():
+    """The C side static_asserts the same sizes and offsets (csrc/api.cu)."""
+    from src import gpu_kernels as K
+    assert ctypes.sizeof(K.History) == 96 and K.History.past.offset == 80 and K.History.status.offset == 88
+    assert ctypes.sizeof(K.PackTarget) == 120 and K.PackTarget.bits.offset == 72
+    assert K.PackTarget.map_rows.offset == 80 and K.PackTarget.status.offset == 112
+    assert K.MAX_REQUESTS == int(re.search(r'#define DKV_MAX_REQUESTS (\d+)', HEADER).group(1))
+
+
+def _target(**over):
+    from src import gpu_kernels as K
+    a = dict(p4=0x3000, m4=0x4000, p8=0x5000, m8=0x6000, p16=0x7000, cap4=64, cap8=64, cap16=64, row_start=0,
+             bits=4, reserved=0, map_rows=None, map_codes=None, map_start=0, map_capacity=0, status=None)
+    a.update(over)
+    return K.PackTarget(**a)
+
+
+@pytest.mark.parametrize('count,over,code,text', [
+    (0, {}, 1, 'request count'),
+    (33, {}, 1, 'request count'),
+    (2, dict(bits=5), 1, 'bit widths'),
+    (2, dict(row_start=10), 2, 'capacity'),
+    (1, dict(map_rows=0x8000), 1, 'half a token map'),
+    (1, dict(map_rows=0x8000, map_codes=0x9000, map_start=30, map_capacity=64), 2, 'context limit'),
+])
+def test_pack_many_rejects_bad_arguments_on_host(count, over, code, text):
+    from src import gpu_kernels as K
+    table = (K.PackTarget * 33)(*[_target(**over) for _ in range(33)])
+    rc = K.LIB.dkv_pack_rows_many(0x1000, 0x2000, ctypes.addressof(table), count, 64 * 64, 64, 64 * 64, 64,
+                                  5 * 64 * 64, 5 * 64 * 64, 0, 64, 5, 64, 1, None)
+    assert rc == code
+    assert text in K.LIB.dkv_last_error().decode()
+
+
+def test_attention_many_rejects_bad_arguments_on_host():
+    from src import gpu_kernels as K
+    h = K.History(0x3000, 0x4000, 0x5000, 0x6000, 0x7000, 0x8000, 0x9000, 64, 64, 64, 100, None)
+    table = (K.History * 2)(h, h)
+    args = [0x1000, 0x2000, 0x3000, ctypes.addressof(table)]
+    rest = [0xA000, 64 * 64, 64, 64 * 64, 64, 64 * 64, 64, 15 * 64 * 64, 5 * 64 * 64, 5 * 64 * 64, 15 * 64 * 64,
+            0, 64, 5, 3, 64, 1, None, 0, None]
+    rc = K.LIB.dkv_packed_attention_many(*args, 0, *rest)
+    assert rc == K.DKV_EINVAL and 'request count' in K.LIB.dkv_last_error().decode()
+    # this shape splits its history, so the missing workspace stops the call before any launch
+    assert K.LIB.dkv_packed_attention_many_workspace(100, 64, 5, 3, 64, 2) > 0
+    rc = K.LIB.dkv_packed_attention_many(*args, 2, *rest)
+    assert rc == K.DKV_EWORKSPACE
+    table[1].past = -1
+    rc = K.LIB.dkv_packed_attention_many(*args, 2, *rest)
+    assert rc == K.DKV_EINVAL and 'negative' in K.LIB.dkv_last_error().decode()

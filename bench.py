@@ -324,7 +324,7 @@ def bench_c5(model, device, rank, world, total, dist, batch, sequential):
         ids = mine[s:s + batch]
         reqs = [synthetic_request(model.cfg, seed=r, frames=64, device=device) for r in ids]
         caches = model.ingest_many([q[0] for q in reqs], [bits_for('dynamic', 64, seed=r) for r in ids], 'dynamic',
-                                   qa_reserve=64)
+                                   qa_reserve=64, graph=True)
         scores += [a['scores'] for a in model.answer_many([q[1] for q in reqs], [q[2] for q in reqs], caches)]
         del caches
     torch.cuda.synchronize(device)
@@ -357,9 +357,10 @@ def bench_c5(model, device, rank, world, total, dist, batch, sequential):
             'sequential': {'requests_per_gpu': seq, 'seconds': float(seq_secs.item()),
                            'frame_append_tokens_per_s': seq * world * 64 * 64 / max(float(seq_secs.item()), 1e-9),
                            'max_abs_score_diff_vs_batched': float(diff.item())},
-            'note': 'wall time incl. frame appends and scoring, eager; batched: requests stepped together '
-                    '(one pack + one attention launch per layer per batch); sequential: the reference '
-                    'protocol, one request at a time; scores gathered with NCCL all_gather'}
+            'note': 'wall time incl. frame appends and scoring; batched: requests stepped together (one pack + '
+                    'one attention launch per layer per batch), frame steps replayed from one captured CUDA graph '
+                    '(FrameGraph), scoring eager; sequential: the reference protocol, one request at a time, eager; '
+                    'scores gathered with NCCL all_gather'}
 
 
 def main():

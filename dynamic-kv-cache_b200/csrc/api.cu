@@ -17,14 +17,15 @@ cudaError_t launch_reconstruct(const Pools& P, const int32_t* rows, const uint8_
                                int layer, int n, int32_t* status, cudaStream_t stream);
 cudaError_t launch_map_fill(int32_t* rows, uint8_t* codes, int64_t start, int n, int64_t row, int bits,
                             cudaStream_t stream);
-cudaError_t launch_pack_many(const void* k, const void* v, const dkv_pack_target* targets, int count, int64_t kh,
-                             int64_t kt, int64_t vh, int64_t vt, int64_t kc, int64_t vc, int layer, int n, int heads,
-                             cudaStream_t stream);
+cudaError_t launch_pack_many(const void* k, const void* v, const dkv_pack_target* targets, bool on_device, int count,
+                             int64_t kh, int64_t kt, int64_t vh, int64_t vt, int64_t kc, int64_t vc, int layer, int n,
+                             int heads, cudaStream_t stream);
 }  // namespace dkv
 
 // The request descriptors cross the C ABI by layout: keep it fixed (the Python
 // binding declares the same fields in the same order).
-static_assert(sizeof(dkv_history) == 96 && offsetof(dkv_history, past) == 80 && offsetof(dkv_history, status) == 88,
+static_assert(sizeof(dkv_history) == 96 && offsetof(dkv_history, past) == 80 &&
+                  offsetof(dkv_history, capacity) == 84 && offsetof(dkv_history, status) == 88,
               "dkv_history layout");
 static_assert(sizeof(dkv_pack_target) == 120 && offsetof(dkv_pack_target, bits) == 72 &&
                   offsetof(dkv_pack_target, map_rows) == 80 && offsetof(dkv_pack_target, status) == 112,
@@ -141,7 +142,8 @@ namespace {
 int launch_planned(dkv::AttnArgs& a, const dkv::AttnPlan& p, const void* q, const void* knew, const void* vnew,
                    void* out, int64_t qh, int64_t qt, int64_t kh, int64_t kt, int64_t vh, int64_t vt, int32_t chunks,
                    int64_t qc, int64_t kc, int64_t vc, int64_t oc, int32_t layer, int32_t nq, int32_t heads,
-                   int32_t group, void* workspace, void* stream, const dkv::HistoryTable* table) {
+                   int32_t group, void* workspace, void* stream, const dkv::HistoryTable* table,
+                   const dkv_history* device_table = nullptr) {
   a.q = static_cast<const uint16_t*>(q);
   a.knew = static_cast<const uint16_t*>(knew);
   a.vnew = static_cast<const uint16_t*>(vnew);
@@ -150,6 +152,7 @@ int launch_planned(dkv::AttnArgs& a, const dkv::AttnPlan& p, const void* q, cons
   a.qc = qc; a.kc = kc; a.vc = vc; a.oc = oc;
   a.layer = layer;
   a.nq = nq;
+  a.heads = heads;
   a.G = group;
   a.HQ = heads * group;
   a.mrows = p.mrows;
@@ -165,7 +168,8 @@ int launch_planned(dkv::AttnArgs& a, const dkv::AttnPlan& p, const void* q, cons
   }
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int zdim = heads * chunks;  // grid z: chunk * heads + KV head
-  cudaError_t e = p.tc ? dkv::launch_attention_tc(a, zdim, st, table) : dkv::launch_attention_split(a, zdim, st, table);
+  cudaError_t e = p.tc ? dkv::launch_attention_tc(a, zdim, st, table, device_table)
+                       : dkv::launch_attention_split(a, zdim, st, table, device_table);
   if (e == cudaSuccess && p.splits > 1 && !a.fused) e = dkv::launch_attention_combine(a, zdim, st);
   return cuda_status(e, "packed_attention launch");
 }
@@ -201,13 +205,7 @@ int attention_impl(const void* q, const void* knew, const void* vnew, const void
   if (need > 0 && (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
     return fail(DKV_EWORKSPACE, "attention workspace must be 256-byte aligned");
   dkv::AttnArgs a{};
-  a.hist.P = dkv::Pools{static_cast<const uint8_t*>(p4), static_cast<const float2*>(m4),
-                        static_cast<const uint8_t*>(p8), static_cast<const float2*>(m8),
-                        static_cast<const uint16_t*>(p16), cap4, cap8, cap16, heads};
-  a.hist.rows = rows;
-  a.hist.codes = codes;
-  a.hist.status = status;
-  a.hist.past = past;
+  a.hist = dkv_history{p4, m4, p8, m8, p16, rows, codes, cap4, cap8, cap16, past, past, status};
   return launch_planned(a, p, q, knew, vnew, out, qh, qt, kh, kt, vh, vt, chunks, qc, kc, vc, oc, layer, nq, heads,
                         group, workspace, stream, nullptr);
 }
@@ -267,15 +265,55 @@ int dkv_pack_rows_many(const void* k, const void* v, const dkv_pack_target* targ
       return fail(DKV_ECAPACITY, "GPU context limit exceeded");
   }
   if (n == 0) return ok();
-  return cuda_status(dkv::launch_pack_many(k, v, targets, count, kh, kt, vh, vt, kc, vc, layer, n, heads,
+  return cuda_status(dkv::launch_pack_many(k, v, targets, false, count, kh, kt, vh, vt, kc, vc, layer, n, heads,
                                            static_cast<cudaStream_t>(stream)),
                      "pack_rows_many launch");
 }
 
+int dkv_pack_rows_many_device(const void* k, const void* v, const dkv_pack_target* targets, int32_t count,
+                              int64_t kh, int64_t kt, int64_t vh, int64_t vt, int64_t kc, int64_t vc, int32_t layer,
+                              int32_t n, int32_t heads, int32_t dim, int32_t layers, void* stream) {
+  int rc = check_geometry(heads, dim, layers, layer);
+  if (rc) return rc;
+  if (count <= 0 || count > 65535) return fail(DKV_EINVAL, "request count %d outside [1, 65535]", count);
+  if (targets == nullptr || !aligned16(targets)) return fail(DKV_EINVAL, "device request table must be 16-byte aligned");
+  if (n < 0) return fail(DKV_EINVAL, "negative token count");
+  if (!rows_aligned(k, kh, kt) || !rows_aligned(v, vh, vt) || (kc % 8) || (vc % 8))
+    return fail(DKV_EINVAL, "k/v rows must be 16-byte aligned (strides multiples of 8)");
+  if (2LL * heads * n * 8 > INT32_MAX) return fail(DKV_EINVAL, "frame too large");
+  if (n == 0) return ok();
+  return cuda_status(dkv::launch_pack_many(k, v, targets, true, count, kh, kt, vh, vt, kc, vc, layer, n, heads,
+                                           static_cast<cudaStream_t>(stream)),
+                     "pack_rows_many_device launch");
+}
+
 size_t dkv_packed_attention_many_workspace(int32_t max_past, int32_t nq, int32_t heads, int32_t group, int32_t dim,
                                            int32_t count) {
-  if (count <= 0 || count > DKV_MAX_REQUESTS) return 0;
-  return dkv_packed_attention_batched_workspace(max_past, nq, heads, group, dim, count);
+  if (count <= 0 || count > 65535 || max_past < 0 || nq <= 0 || heads <= 0 || group <= 0 || dim != dkv::kDim)
+    return 0;
+  return dkv::make_plan_many(max_past, nq, heads, group, count).workspace_bytes();
+}
+
+// Shared checks and launch of the two many-request attention entry points.
+static int attention_many_launch(const void* q, const void* knew, const void* vnew, const dkv::HistoryTable* table,
+                          const dkv_history* device_table, int32_t count, int32_t max_past, void* out, int64_t qh,
+                          int64_t qt, int64_t kh, int64_t kt, int64_t vh, int64_t vt, int64_t qc, int64_t kc,
+                          int64_t vc, int64_t oc, int32_t layer, int32_t nq, int32_t heads, int32_t group,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+  if (nq == 0) return ok();
+  if (!rows_aligned(q, qh, qt) || !rows_aligned(knew, kh, kt) || !rows_aligned(vnew, vh, vt))
+    return fail(DKV_EINVAL, "q/k/v rows must be 16-byte aligned (head/token strides multiples of 8)");
+  if (out == nullptr || !aligned16(out)) return fail(DKV_EINVAL, "out must be 16-byte aligned");
+  if (static_cast<int64_t>(count) * heads > 65535) return fail(DKV_EINVAL, "chunk count out of range");
+  const dkv::AttnPlan p = dkv::make_plan_many(max_past, nq, heads, group, count);
+  const size_t need = p.workspace_bytes();
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need))
+    return fail(DKV_EWORKSPACE, "attention workspace needs %zu bytes, got %zu", need, workspace_bytes);
+  if (need > 0 && (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return fail(DKV_EWORKSPACE, "attention workspace must be 256-byte aligned");
+  dkv::AttnArgs a{};
+  return launch_planned(a, p, q, knew, vnew, out, qh, qt, kh, kt, vh, vt, count, qc, kc, vc, oc, layer, nq, heads,
+                        group, workspace, stream, table, device_table);
 }
 
 int dkv_packed_attention_many(const void* q, const void* knew, const void* vnew, const dkv_history* requests,
@@ -298,32 +336,35 @@ int dkv_packed_attention_many(const void* q, const void* knew, const void* vnew,
     const dkv_history& h = requests[r];
     if ((rc = check_pools(h.p4, h.m4, h.p8, h.m8, h.p16, h.cap4, h.cap8, h.cap16))) return rc;
     if (h.past < 0) return fail(DKV_EINVAL, "negative past or query length");
+    if (h.past > h.capacity) return fail(DKV_EINVAL, "request %d: past %d exceeds its token map (%d)", r, h.past,
+                                         h.capacity);
     if (h.past > 0 && (h.rows == nullptr || h.codes == nullptr)) return fail(DKV_EINVAL, "null token map");
     if (h.past > 0 && (!aligned16(h.rows) || !aligned16(h.codes)))
       return fail(DKV_EINVAL, "token maps must be 16-byte aligned");
-    table.h[r].P = dkv::Pools{static_cast<const uint8_t*>(h.p4), static_cast<const float2*>(h.m4),
-                              static_cast<const uint8_t*>(h.p8), static_cast<const float2*>(h.m8),
-                              static_cast<const uint16_t*>(h.p16), h.cap4, h.cap8, h.cap16, heads};
-    table.h[r].rows = h.rows;
-    table.h[r].codes = h.codes;
-    table.h[r].status = h.status;
-    table.h[r].past = h.past;
+    table.h[r] = h;
     max_past = h.past > max_past ? h.past : max_past;
   }
-  if (nq == 0) return ok();
-  if (!rows_aligned(q, qh, qt) || !rows_aligned(knew, kh, kt) || !rows_aligned(vnew, vh, vt))
-    return fail(DKV_EINVAL, "q/k/v rows must be 16-byte aligned (head/token strides multiples of 8)");
-  if (out == nullptr || !aligned16(out)) return fail(DKV_EINVAL, "out must be 16-byte aligned");
-  const dkv::AttnPlan p = dkv::make_plan(max_past, nq, heads, group, count);
-  const size_t need = p.workspace_bytes();
-  if (need > 0 && (workspace == nullptr || workspace_bytes < need))
-    return fail(DKV_EWORKSPACE, "attention workspace needs %zu bytes, got %zu", need, workspace_bytes);
-  if (need > 0 && (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
-    return fail(DKV_EWORKSPACE, "attention workspace must be 256-byte aligned");
-  dkv::AttnArgs a{};
-  a.hist = table.h[0];  // heads for the grid decomposition; chunks read the table
-  return launch_planned(a, p, q, knew, vnew, out, qh, qt, kh, kt, vh, vt, count, qc, kc, vc, oc, layer, nq, heads,
-                        group, workspace, stream, &table);
+  return attention_many_launch(q, knew, vnew, &table, nullptr, count, max_past, out, qh, qt, kh, kt, vh, vt, qc, kc,
+                               vc, oc, layer, nq, heads, group, workspace, workspace_bytes, stream);
+}
+
+int dkv_packed_attention_many_device(const void* q, const void* knew, const void* vnew, const dkv_history* requests,
+                                     int32_t count, int32_t max_past, void* out, int64_t qh, int64_t qt, int64_t kh,
+                                     int64_t kt, int64_t vh, int64_t vt, int64_t qc, int64_t kc, int64_t vc,
+                                     int64_t oc, int32_t layer, int32_t nq, int32_t heads, int32_t group,
+                                     int32_t dim, int32_t layers, void* workspace, size_t workspace_bytes,
+                                     void* stream) {
+  int rc = check_geometry(heads, dim, layers, layer);
+  if (rc) return rc;
+  if (count <= 0 || count > 65535) return fail(DKV_EINVAL, "request count %d outside [1, 65535]", count);
+  if (requests == nullptr || !aligned16(requests))
+    return fail(DKV_EINVAL, "device request table must be 16-byte aligned");
+  if (group <= 0) return fail(DKV_EINVAL, "query heads must be a positive multiple of KV heads");
+  if (nq < 0 || max_past < 0) return fail(DKV_EINVAL, "negative past or query length");
+  if ((qc % 8) || (kc % 8) || (vc % 8) || (oc % 8))
+    return fail(DKV_EINVAL, "chunk strides must keep rows 16-byte aligned (multiples of 8 elements)");
+  return attention_many_launch(q, knew, vnew, nullptr, requests, count, max_past, out, qh, qt, kh, kt, vh, vt, qc, kc,
+                               vc, oc, layer, nq, heads, group, workspace, workspace_bytes, stream);
 }
 
 int dkv_reconstruct(const void* p4, const void* m4, const void* p8, const void* m8, const void* p16,

@@ -35,6 +35,15 @@ struct AttnPlan {
 
 // `chunks` independent query chunks share the history (batched calls): they act as
 // chunks x heads groups of the same shape.
+inline void size_workspace(AttnPlan& p, int heads) {
+  p.ws_o_bytes = p.ws_ml_bytes = 0;
+  if (p.splits > 1) {
+    const size_t ctas = static_cast<size_t>(heads) * p.mblocks * p.splits;
+    p.ws_o_bytes = ctas * p.cta_rows * kDim * sizeof(float);
+    p.ws_ml_bytes = ctas * p.cta_rows * sizeof(float2) + sizeof(float2) * p.cta_rows * heads * p.mblocks;  // even split count
+  }
+}
+
 inline AttnPlan make_plan(int past, int nq, int heads, int group, int chunks = 1) {
   heads *= chunks;
   AttnPlan p{};
@@ -55,43 +64,56 @@ inline AttnPlan make_plan(int past, int nq, int heads, int group, int chunks = 1
   const int per_split = (tiles + target - 1) / target;  // tiles per split
   p.chunk = per_split * kBN;
   p.splits = (tiles + per_split - 1) / per_split;
-  if (p.splits > 1) {
-    const size_t ctas = static_cast<size_t>(heads) * p.mblocks * p.splits;
-    p.ws_o_bytes = ctas * p.cta_rows * kDim * sizeof(float);
-    p.ws_ml_bytes = ctas * p.cta_rows * sizeof(float2) + sizeof(float2) * p.cta_rows * heads * p.mblocks;  // even split count
-  }
+  size_workspace(p, heads);
   return p;
 }
 
-// One request's packed history: its pools, token maps (rows / codes per logical
-// token), history length and device status word.
-struct History {
-  Pools P;
-  const int32_t* rows;
-  const uint8_t* codes;
-  int32_t* status;
-  int past;
-};
+// Plan of a call over `count` independent requests whose histories are at most
+// max_past tokens: as many splits as fill one wave (never more than the longest
+// history has tiles), and each request divides its own history evenly among them
+// (chunk = 0), so short and long histories of one batch finish together.
+inline AttnPlan make_plan_many(int max_past, int nq, int heads, int group, int count) {
+  AttnPlan p = make_plan(max_past, nq, heads, group, count);
+  const int groups = heads * count * p.mblocks;
+  const int tiles = (max_past + nq + kBN - 1) / kBN;
+  int splits = kTargetCtas / groups;
+  if (splits > tiles) splits = tiles;
+  p.splits = splits < 1 ? 1 : splits;
+  p.chunk = 0;
+  size_workspace(p, heads * count);
+  return p;
+}
 
-// Calls over several independent requests (request batching): query chunk c
-// attends over h[c], each request with its own pools, maps and history length.
-// Passed by value as a kernel parameter (3.3 KB), so a launch needs no device
-// copy of it. Without a table every chunk reads AttnArgs::hist.
-constexpr int kMaxRequests = 32;
+// One request's packed history (the C ABI's dkv_history): pools, (offset, scale)
+// metadata, token maps rows / codes (pool row and precision of each logical
+// token), history length, map length and device status word.
+using History = dkv_history;
+
+// Where query chunk c finds its history:
+//  SharedHistory   every chunk reads AttnArgs::hist (one request; batched chunks)
+//  HistoryTable    chunk c reads h[c], passed by value as a kernel parameter
+//                  (3 KB: the launch itself carries the descriptors)
+//  DeviceHistories chunk c reads h[c] from device memory, so a CUDA graph can be
+//                  replayed with new histories written there between replays
+constexpr int kMaxRequests = DKV_MAX_REQUESTS;
+struct SharedHistory {};
 struct HistoryTable {
   History h[kMaxRequests];
 };
-struct SharedHistory {};
+struct DeviceHistories {
+  const History* h;
+};
 
 struct AttnArgs {
   const uint16_t* q;
   const uint16_t* knew;
   const uint16_t* vnew;
-  History hist;   // the history of every chunk, unless a HistoryTable is given
+  History hist;   // the history of every chunk, unless a table is given
   uint16_t* out;
   int64_t qh, qt, kh, kt, vh, vt;
-  int layer, nq, G, HQ;
-  int mrows, cta_rows, mblocks, splits, chunk;
+  int layer, nq, heads, G, HQ;  // heads: KV heads of one chunk
+  int mrows, cta_rows, mblocks, splits;
+  int chunk;  // keys per split; 0: each request splits its own history evenly (request_chunk)
   // Batched calls: blockIdx.z = chunk * heads + KV head; chunk c's q / knew / vnew /
   // out start qc / kc / vc / oc elements after chunk 0's (0 for a single chunk).
   int64_t qc, kc, vc, oc;
@@ -107,6 +129,29 @@ __device__ __forceinline__ const History& history_of(const AttnArgs& a, const Sh
 }
 __device__ __forceinline__ const History& history_of(const AttnArgs&, const HistoryTable& t, int c) {
   return t.h[c];
+}
+__device__ __forceinline__ const History& history_of(const AttnArgs&, const DeviceHistories& t, int c) {
+  return t.h[c];
+}
+
+// History length of a chunk, checked against its token map (descriptors in
+// device memory are not seen by the host): a bad one is reported and read as an
+// empty history.
+__device__ __forceinline__ int checked_past(const History& H, int chunk) {
+  const int past = H.past;
+  if (past < 0 || past > H.capacity || (past > 0 && (H.rows == nullptr || H.codes == nullptr))) {
+    report(H.status, DKV_EINVAL, chunk);
+    return 0;
+  }
+  return past;
+}
+
+// Keys per split: the plan's, or (chunk == 0) this request's own history split
+// evenly over the plan's splits.
+__device__ __forceinline__ int request_chunk(const AttnArgs& a, int past) {
+  if (a.chunk > 0) return a.chunk;
+  const int tiles = (past + a.nq + kBN - 1) / kBN;
+  return ((tiles + a.splits - 1) / a.splits) * kBN;
 }
 
 // Partials of group grp (= KV head * mblocks + row block): for each row, every
@@ -153,11 +198,14 @@ __device__ __forceinline__ float merge_row_weights(Load load, int splits, float*
 }
 
 // `table` (may be null): per-chunk histories of a call over several requests.
+// Per-chunk histories of a call over several requests: `table` (by value) or
+// `device_table` (device memory); both null: every chunk reads a.hist.
 cudaError_t launch_attention_split(const AttnArgs& a, int heads, cudaStream_t stream,
-                                   const HistoryTable* table = nullptr);
+                                   const HistoryTable* table = nullptr, const History* device_table = nullptr);
 // Sets a.fused when every CTA of the grid can be resident at once (one CTA per SM):
 // the split merge then runs inside the kernel and no combine launch follows.
-cudaError_t launch_attention_tc(AttnArgs& a, int heads, cudaStream_t stream, const HistoryTable* table = nullptr);
+cudaError_t launch_attention_tc(AttnArgs& a, int heads, cudaStream_t stream, const HistoryTable* table = nullptr,
+                                const History* device_table = nullptr);
 // Whether a call with this plan merges its splits inside the tensor-core kernel
 // on the current device (one launch) or needs the combine kernel (two).
 cudaError_t attention_tc_merges_in_kernel(const AttnPlan& p, int heads, bool* fused);

@@ -68,9 +68,16 @@ attention_split_kernel(const __grid_constant__ AttnArgs a, const __grid_constant
   const int split = blockIdx.x;
   const int mb = blockIdx.y;
   const int zc = blockIdx.z;  // chunk * heads + KV head
-  const int chunk = zc / a.hist.P.heads;
-  const int g = zc - chunk * a.hist.P.heads;
+  const int chunk = zc / a.heads;
+  const int g = zc - chunk * a.heads;
   const History& H = history_of(a, hist, chunk);
+  const int past = checked_past(H, chunk);
+  const Pools P{static_cast<const uint8_t*>(H.p4), static_cast<const float2*>(H.m4),
+                static_cast<const uint8_t*>(H.p8), static_cast<const float2*>(H.m8),
+                static_cast<const uint16_t*>(H.p16), H.cap4, H.cap8, H.cap16, a.heads};
+  const int32_t* const map_rows = H.rows;
+  const uint8_t* const map_codes = H.codes;
+  int32_t* const status = H.status;
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
@@ -78,9 +85,10 @@ attention_split_kernel(const __grid_constant__ AttnArgs a, const __grid_constant
   const int row0 = mb * a.cta_rows;
   const int rows_here = min(a.cta_rows, a.mrows - row0);
   const int m_max = (row0 + rows_here - 1) / a.G;
-  const int kb = split * a.chunk;
-  int ke = min(kb + a.chunk, H.past + a.nq);
-  ke = min(ke, H.past + m_max + 1);  // no row of this block sees further
+  const int keys = request_chunk(a, past);
+  const int kb = split * keys;
+  int ke = min(kb + keys, past + a.nq);
+  ke = min(ke, past + m_max + 1);  // no row of this block sees further
   const int ntiles = ke > kb ? (ke - kb + kBN - 1) / kBN : 0;
 
   // ---- Q block -> shared (zero rows past the end) ----
@@ -110,10 +118,10 @@ attention_split_kernel(const __grid_constant__ AttnArgs a, const __grid_constant
         const int part = task & 7;
         const int t = t0 + j;
         if (t < ke) {
-          if (t < H.past) {
-            pre[i] = load_history_part(H.P, H.rows, H.codes, a.layer, kv, g, t, part, H.status);
+          if (t < past) {
+            pre[i] = load_history_part(P, map_rows, map_codes, a.layer, kv, g, t, part, status);
           } else {
-            const int tn = t - H.past;
+            const int tn = t - past;
             const uint16_t* src = kv == 0 ? a.knew + chunk * a.kc + g * a.kh + tn * a.kt
                                           : a.vnew + chunk * a.vc + g * a.vh + tn * a.vt;
             pre[i].raw = __ldg(reinterpret_cast<const uint4*>(src) + part);
@@ -142,8 +150,8 @@ attention_split_kernel(const __grid_constant__ AttnArgs a, const __grid_constant
   // Rows of this thread inside the block: ra (fragment rows 0-7) and ra + 8.
   const int ra = warp * 16 + (lane >> 2);
   const int rb = ra + 8;
-  const int lim_a = H.past + min(row0 + ra, a.mrows - 1) / a.G;  // last visible key
-  const int lim_b = H.past + min(row0 + rb, a.mrows - 1) / a.G;
+  const int lim_a = past + min(row0 + ra, a.mrows - 1) / a.G;  // last visible key
+  const int lim_b = past + min(row0 + rb, a.mrows - 1) / a.G;
 
   float o[8][4];
 #pragma unroll
@@ -302,8 +310,8 @@ __global__ void __launch_bounds__(256) attention_combine_kernel(const __grid_con
   ptx::pdl_wait();  // partials of the attention grid
   ptx::pdl_trigger();
   const int zc = blockIdx.z;  // chunk * heads + KV head
-  const int chunk = zc / a.hist.P.heads;
-  const int g = zc - chunk * a.hist.P.heads;
+  const int chunk = zc / a.heads;
+  const int g = zc - chunk * a.heads;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int fr0 = blockIdx.x * 4;
   if (warp < 4 && fr0 + warp < a.mrows) {
@@ -374,8 +382,10 @@ cudaError_t launch_split(const AttnArgs& a, const Hist& hist, int heads, cudaStr
 
 }  // namespace
 
-cudaError_t launch_attention_split(const AttnArgs& a, int heads, cudaStream_t stream, const HistoryTable* table) {
+cudaError_t launch_attention_split(const AttnArgs& a, int heads, cudaStream_t stream, const HistoryTable* table,
+                                   const History* device_table) {
   if (table != nullptr) return launch_split(a, *table, heads, stream);
+  if (device_table != nullptr) return launch_split(a, DeviceHistories{device_table}, heads, stream);
   return launch_split(a, SharedHistory{}, heads, stream);
 }
 

@@ -281,8 +281,9 @@ __device__ __forceinline__ void merge_rows(const AttnArgs& a, int g, int grp, in
   }
 }
 
-// Hist: SharedHistory (every chunk reads a.hist) or HistoryTable (chunk c reads
-// its own request's history).
+// Hist: SharedHistory (every chunk reads a.hist), HistoryTable (chunk c reads its
+// own request's history from the kernel parameters) or DeviceHistories (from
+// device memory).
 template <class Hist>
 __global__ void __launch_bounds__(kThreadsTc, 1)
 attention_tc_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ Hist hist) {
@@ -294,9 +295,11 @@ attention_tc_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ 
   const int split = blockIdx.x;
   const int mb = blockIdx.y;
   const int zc = blockIdx.z;                  // chunk * heads + KV head
-  const int chunk = zc / a.hist.P.heads;
-  const int g = zc - chunk * a.hist.P.heads;
+  const int chunk = zc / a.heads;
+  const int g = zc - chunk * a.heads;
   const History& H = history_of(a, hist, chunk);
+  const int past = checked_past(H, chunk);
+  int32_t* const status = H.status;
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
@@ -305,9 +308,10 @@ attention_tc_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ 
   const int rows_here = min(kTcCtaRows, a.mrows - row0);
   const int mt_count = (rows_here + 127) >> 7;
   const int m_max = (row0 + rows_here - 1) / a.G;
-  const int kb = split * a.chunk;
-  int ke = min(kb + a.chunk, H.past + a.nq);
-  ke = min(ke, H.past + m_max + 1);  // no row of this block sees further
+  const int keys = request_chunk(a, past);
+  const int kb = split * keys;
+  int ke = min(kb + keys, past + a.nq);
+  ke = min(ke, past + m_max + 1);  // no row of this block sees further
   const int ntiles = ke > kb ? (ke - kb + kBN - 1) / kBN : 0;
   const int soft_threads = ((rows_here + 31) >> 5) << 5;  // threads of softmax warps with real rows
 
@@ -372,7 +376,7 @@ attention_tc_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ 
       }
       if (!ok) {
         *abort_flag = 1;
-        report(H.status, DKV_ETIMEOUT, 1);
+        report(status, DKV_ETIMEOUT, 1);
       }
       umma_commit(bar(B_FINS));  // drain this thread's MMAs before TMEM is released
       mbar_wait(bar(B_FINS), 0, kWaitCycles);
@@ -400,7 +404,7 @@ attention_tc_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ 
       }
       if (!ok) {
         *abort_flag = 1;
-        report(H.status, DKV_ETIMEOUT, 2);
+        report(status, DKV_ETIMEOUT, 2);
       }
       umma_commit(bar(B_FINPV));
       mbar_wait(bar(B_FINPV), 0, kWaitCycles);
@@ -410,20 +414,27 @@ attention_tc_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ 
     // ================= loader: token maps and packed runs by TMA =================
     // Per-CTA block bases (layer, K|V, this head) of every pool, and the parity of
     // each meta block's first pair index, so the per-tile work is 32-bit math.
-    const int64_t blk_k = (static_cast<int64_t>(a.layer) * 2) * H.P.heads + g;  // (layer, K, head)
-    const int64_t blk_v = blk_k + H.P.heads;                                    // (layer, V, head)
-    const int cap4 = static_cast<int>(H.P.cap4), cap8 = static_cast<int>(H.P.cap8);
-    const int cap16 = static_cast<int>(H.P.cap16);
-    const uint8_t* const pk4 = H.P.p4 + blk_k * cap4 * kRowBytes4;
-    const uint8_t* const pv4 = H.P.p4 + blk_v * cap4 * kRowBytes4;
-    const uint8_t* const pk8 = H.P.p8 + blk_k * cap8 * kRowBytes8;
-    const uint8_t* const pv8 = H.P.p8 + blk_v * cap8 * kRowBytes8;
-    const uint8_t* const pk16 = reinterpret_cast<const uint8_t*>(H.P.p16 + blk_k * cap16 * kDim);
-    const uint8_t* const pv16 = reinterpret_cast<const uint8_t*>(H.P.p16 + blk_v * cap16 * kDim);
-    const float2* const mk4 = H.P.m4 + blk_k * cap4;
-    const float2* const mv4 = H.P.m4 + blk_v * cap4;
-    const float2* const mk8 = H.P.m8 + blk_k * cap8;
-    const float2* const mv8 = H.P.m8 + blk_v * cap8;
+    const int64_t blk_k = (static_cast<int64_t>(a.layer) * 2) * a.heads + g;  // (layer, K, head)
+    const int64_t blk_v = blk_k + a.heads;                                    // (layer, V, head)
+    const int cap4 = static_cast<int>(H.cap4), cap8 = static_cast<int>(H.cap8);
+    const int cap16 = static_cast<int>(H.cap16);
+    const uint8_t* const p4 = static_cast<const uint8_t*>(H.p4);
+    const uint8_t* const p8 = static_cast<const uint8_t*>(H.p8);
+    const uint8_t* const p16 = static_cast<const uint8_t*>(H.p16);
+    const float2* const m4 = static_cast<const float2*>(H.m4);
+    const float2* const m8 = static_cast<const float2*>(H.m8);
+    const int32_t* const map_rows = H.rows;
+    const uint8_t* const map_codes = H.codes;
+    const uint8_t* const pk4 = p4 + blk_k * cap4 * kRowBytes4;
+    const uint8_t* const pv4 = p4 + blk_v * cap4 * kRowBytes4;
+    const uint8_t* const pk8 = p8 + blk_k * cap8 * kRowBytes8;
+    const uint8_t* const pv8 = p8 + blk_v * cap8 * kRowBytes8;
+    const uint8_t* const pk16 = p16 + blk_k * cap16 * kRowBytes16;
+    const uint8_t* const pv16 = p16 + blk_v * cap16 * kRowBytes16;
+    const float2* const mk4 = m4 + blk_k * cap4;
+    const float2* const mv4 = m4 + blk_v * cap4;
+    const float2* const mk8 = m8 + blk_k * cap8;
+    const float2* const mv8 = m8 + blk_v * cap8;
     const int pbk4 = static_cast<int>((blk_k * cap4) & 1), pbv4 = static_cast<int>((blk_v * cap4) & 1);
     const int pbk8 = static_cast<int>((blk_k * cap8) & 1), pbv8 = static_cast<int>((blk_v * cap8) & 1);
     // selectors (no dynamic array indexing: keeps everything in registers)
@@ -438,10 +449,10 @@ attention_tc_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ 
     auto map_tile = [&](int tile) {  // lane 0: start the map copy of a full history tile
       const int t0 = kb + tile * kBN;
       const int slot = tile % kMapStages;
-      if (t0 + kBN <= H.past) {
+      if (t0 + kBN <= past) {
         mbar_expect_tx(bar(B_MAPFULL + slot), kMapStage);
-        bulk_g2s(sbase + kOffMap + slot * kMapStage, H.codes + t0, kBN, bar(B_MAPFULL + slot));
-        bulk_g2s(sbase + kOffMap + slot * kMapStage + kBN, H.rows + t0, kBN * 4, bar(B_MAPFULL + slot));
+        bulk_g2s(sbase + kOffMap + slot * kMapStage, map_codes + t0, kBN, bar(B_MAPFULL + slot));
+        bulk_g2s(sbase + kOffMap + slot * kMapStage + kBN, map_rows + t0, kBN * 4, bar(B_MAPFULL + slot));
       }
       mbar_arrive(bar(B_MAPFULL + slot));
     };
@@ -479,10 +490,10 @@ attention_tc_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ 
       }
       fence_proxy_async_smem();  // converters' reads of this raw stage precede the TMA writes
       const int t0 = kb + i * kBN;
-      if (t0 + kBN > H.past) pdl_wait();  // current-chunk K/V come from the previous kernels
+      if (t0 + kBN > past) pdl_wait();  // current-chunk K/V come from the previous kernels
       const uint8_t* mcodes = smem + kOffMap + slot * kMapStage;
       const int32_t* mrows = reinterpret_cast<const int32_t*>(mcodes + kBN);
-      const bool full_map = t0 + kBN <= H.past;
+      const bool full_map = t0 + kBN <= past;
       // --- classify this lane's two tokens j = 2 lane + e ---
       int code[2], row[2];
 #pragma unroll
@@ -492,23 +503,23 @@ attention_tc_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ 
         if (t >= ke) {
           code[e] = 0;
           row[e] = 0;
-        } else if (t >= H.past) {
+        } else if (t >= past) {
           code[e] = kCodeNew;
-          row[e] = t - H.past;
+          row[e] = t - past;
         } else {
           if (full_map) {
             code[e] = mcodes[j];
             row[e] = mrows[j];
           } else {  // the tile holding `past`: its map was not prefetched
-            code[e] = __ldg(H.codes + t);
-            row[e] = __ldg(H.rows + t);
+            code[e] = __ldg(map_codes + t);
+            row[e] = __ldg(map_rows + t);
           }
           const int cap = code[e] == 4 ? cap4 : (code[e] == 8 ? cap8 : cap16);
           if (code[e] != 4 && code[e] != 8 && code[e] != 16) {
-            report(H.status, DKV_EPLAN, t);
+            report(status, DKV_EPLAN, t);
             code[e] = 0;
           } else if (row[e] < 0 || row[e] >= cap) {
-            report(H.status, DKV_ECAPACITY, t);
+            report(status, DKV_ECAPACITY, t);
             code[e] = 0;
           }
         }
@@ -566,7 +577,7 @@ attention_tc_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ 
             // The tile's new tokens are one run (past .. ke): rows stored 64 elements
             // apart are one contiguous block, fetched by a single copy from the run's
             // first lane; other layouts take one 128-byte copy per row.
-            const int jn = max(H.past - t0, 0);                 // first new token of the tile
+            const int jn = max(past - t0, 0);                 // first new token of the tile
             const int nn = min(ke - t0, kBN) - jn;              // new tokens in the tile
             const bool first = j == jn;
             if (a.kt == kDim) {
@@ -631,7 +642,7 @@ attention_tc_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ 
     }
     if (!ok && lane == 0) {
       *abort_flag = 1;
-      report(H.status, DKV_ETIMEOUT, 3);
+      report(status, DKV_ETIMEOUT, 3);
     }
   } else if (warp >= kConvWarp0) {
     // ================= converters: raw runs -> swizzled bf16 K / V tiles =================
@@ -740,7 +751,7 @@ attention_tc_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ 
     }
     if (!ok) {
       *abort_flag = 1;
-      report(H.status, DKV_ETIMEOUT, 4);
+      report(status, DKV_ETIMEOUT, 4);
     }
   } else {
     // ---- Q rows -> this thread's TMEM lane (zeros past the last row) ----
@@ -782,7 +793,7 @@ attention_tc_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ 
     const int rl = mt * 128 + quad * 32 + lane;  // row inside the block
     if (mt * 128 + quad * 32 < rows_here) {
       const int fr = row0 + min(rl, rows_here - 1);
-      const int lim = H.past + fr / a.G;  // last key this row may see
+      const int lim = past + fr / a.G;  // last key this row may see
       const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
       const uint32_t col_o = kColO + mt * 64;
       float l_run = 0.f;  // sum of p of this row, scaled like O
@@ -810,7 +821,7 @@ attention_tc_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ 
         tc_fence_before();
         mbar_arrive(bar(B_SFREE + b * 2 + mt));  // S[b][mt] may be overwritten by S(i + 2)
         const int t0 = kb + i * kBN;
-        if (!(t0 + kBN <= ke && t0 + kBN - 1 <= H.past)) {  // boundary tile: mask
+        if (!(t0 + kBN <= ke && t0 + kBN - 1 <= past)) {  // boundary tile: mask
 #pragma unroll
           for (int j = 0; j < 64; ++j) {
             const int t = t0 + j;
@@ -903,7 +914,7 @@ attention_tc_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ 
       }
       if (!ok) {
         *abort_flag = 1;
-        report(H.status, DKV_ETIMEOUT, 5);
+        report(status, DKV_ETIMEOUT, 5);
       } else if (rl < rows_here) {
         const int frow = row0 + rl;
         if (a.splits == 1) {
@@ -945,7 +956,7 @@ attention_tc_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ 
   if (a.fused) {
     // block coordinates re-read here so nothing stays live across the roles above
     const int msplit = blockIdx.x, mrow0 = blockIdx.y * kTcCtaRows, mz = blockIdx.z;
-    const int mchunk = mz / a.hist.P.heads, mg = mz - mchunk * a.hist.P.heads;
+    const int mchunk = mz / a.heads, mg = mz - mchunk * a.heads;
     const int mrows_here = min(kTcCtaRows, a.mrows - mrow0);
     const int grp = mz * a.mblocks + blockIdx.y;
     uint32_t* arrive = a.sync + grp;
@@ -966,14 +977,14 @@ attention_tc_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ 
         }
         __nanosleep(64);
       }
-      if (!ready) report(H.status, DKV_ETIMEOUT, 6);
+      if (!ready) report(status, DKV_ETIMEOUT, 6);
       *go = ready;
     }
     __syncthreads();
     if (*go) {
       const int r_begin = msplit * mrows_here / a.splits;
       const int r_end = (msplit + 1) * mrows_here / a.splits;
-      merge_rows(a, mg, grp, mrow0, r_begin, r_end, a.out + mchunk * a.oc, msmem, threadIdx.x, H.status);
+      merge_rows(a, mg, grp, mrow0, r_begin, r_end, a.out + mchunk * a.oc, msmem, threadIdx.x, status);
     }
     __syncthreads();
     // every CTA departs exactly once (also after a timeout): the last one out
@@ -1002,14 +1013,21 @@ cudaError_t configure(int& dev) {
     e = cudaFuncSetAttribute(attention_tc_kernel<HistoryTable>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kSmemTc);
     if (e != cudaSuccess) return e;
-    int per_sm = 0, per_sm_table = 0, sms = 0;
+    e = cudaFuncSetAttribute(attention_tc_kernel<DeviceHistories>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kSmemTc);
+    if (e != cudaSuccess) return e;
+    int per_sm = 0, per_sm_table = 0, per_sm_device = 0, sms = 0;
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attention_tc_kernel<SharedHistory>, kThreadsTc,
                                                       kSmemTc);
     if (e != cudaSuccess) return e;
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm_table, attention_tc_kernel<HistoryTable>, kThreadsTc,
                                                       kSmemTc);
     if (e != cudaSuccess) return e;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm_device, attention_tc_kernel<DeviceHistories>,
+                                                      kThreadsTc, kSmemTc);
+    if (e != cudaSuccess) return e;
     per_sm = per_sm < per_sm_table ? per_sm : per_sm_table;
+    per_sm = per_sm < per_sm_device ? per_sm : per_sm_device;
     e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return e;
     g_resident[dev] = per_sm * sms;
@@ -1043,7 +1061,8 @@ cudaError_t attention_tc_merges_in_kernel(const AttnPlan& p, int heads, bool* fu
   return e;
 }
 
-cudaError_t launch_attention_tc(AttnArgs& a, int heads, cudaStream_t stream, const HistoryTable* table) {
+cudaError_t launch_attention_tc(AttnArgs& a, int heads, cudaStream_t stream, const HistoryTable* table,
+                                const History* device_table) {
   int dev = 0;
   cudaError_t e = configure(dev);
   if (e != cudaSuccess) return e;
@@ -1063,6 +1082,8 @@ cudaError_t launch_attention_tc(AttnArgs& a, int heads, cudaStream_t stream, con
   cfg.attrs = attr;                                                 // previous kernel's tail
   cfg.numAttrs = 1;
   if (table != nullptr) return cudaLaunchKernelEx(&cfg, attention_tc_kernel<HistoryTable>, a, *table);
+  if (device_table != nullptr)
+    return cudaLaunchKernelEx(&cfg, attention_tc_kernel<DeviceHistories>, a, DeviceHistories{device_table});
   return cudaLaunchKernelEx(&cfg, attention_tc_kernel<SharedHistory>, a, SharedHistory{});
 }
 

@@ -104,23 +104,46 @@ pack_rows_kernel(const uint16_t* __restrict__ k, const uint16_t* __restrict__ v,
   pack_row_part<BITS>(raw, part, p4, m4, p8, m8, p16, block, cap, row_start + token, status, row);
 }
 
-// Per-request destinations of pack_rows_many_kernel (dkv_pack_target, by value).
+// Per-request destinations of pack_rows_many_kernel: by value in the kernel
+// parameters (PackTable), or in device memory (DevicePackTargets: a CUDA graph
+// replays with new destinations written there between replays).
 struct PackTable {
   dkv_pack_target t[kMaxPackRequests];
+  __device__ const dkv_pack_target& operator[](int r) const { return t[r]; }
+};
+struct DevicePackTargets {
+  const dkv_pack_target* t;
+  __device__ const dkv_pack_target& operator[](int r) const { return t[r]; }
 };
 
 static_assert(sizeof(PackTable) + 128 <= 4096, "pack_rows_many_kernel parameters");
 
 // Frames of several requests in one launch: blockIdx.y = request, each with its
 // own precision (uniform over a block, so the branch below does not diverge),
-// pools and optional token-map update.
+// pools and optional token-map update. Destinations are checked here as well as
+// on the host (device-resident ones are not seen by the host): a bad one is
+// reported to its status word and skipped.
+template <class Targets>
 __global__ void __launch_bounds__(kPackThreads)
 pack_rows_many_kernel(const uint16_t* __restrict__ k, const uint16_t* __restrict__ v,
-                      const __grid_constant__ PackTable tab, int64_t kh, int64_t kt, int64_t vh, int64_t vt,
+                      const __grid_constant__ Targets tab, int64_t kh, int64_t kt, int64_t vh, int64_t vt,
                       int64_t kc, int64_t vc, int layer, int n, int heads) {
   asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
   asm volatile("griddepcontrol.wait;\n" ::: "memory");
-  const dkv_pack_target& d = tab.t[blockIdx.y];
+  const dkv_pack_target& d = tab[blockIdx.y];
+  const int bits = d.bits;
+  const int64_t cap = bits == 4 ? d.cap4 : (bits == 8 ? d.cap8 : d.cap16);
+  const int64_t row_start = d.row_start;
+  const bool pool_ok = bits == 4 ? (d.p4 != nullptr && d.m4 != nullptr)
+                                 : (bits == 8 ? (d.p8 != nullptr && d.m8 != nullptr) : d.p16 != nullptr);
+  if ((bits != 4 && bits != 8 && bits != 16) || !pool_ok) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) report(d.status, DKV_EINVAL, blockIdx.y);
+    return;
+  }
+  if (row_start < 0 || row_start + n > cap) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) report(d.status, DKV_ECAPACITY, blockIdx.y);
+    return;
+  }
   const int gtid = blockIdx.x * blockDim.x + threadIdx.x;
   const int row = gtid >> 3;
   const int part = gtid & 7;
@@ -134,22 +157,27 @@ pack_rows_many_kernel(const uint16_t* __restrict__ k, const uint16_t* __restrict
                                 : v + blockIdx.y * vc + head * vh + token * vt;
   const uint4 raw = __ldg(reinterpret_cast<const uint4*>(src) + part);
   const int64_t block = (static_cast<int64_t>(layer) * 2 + kv) * heads + head;
-  const int64_t out_row = d.row_start + token;
+  const int64_t out_row = row_start + token;
   uint8_t* p4 = static_cast<uint8_t*>(d.p4);
   uint8_t* p8 = static_cast<uint8_t*>(d.p8);
   float2* m4 = static_cast<float2*>(d.m4);
   float2* m8 = static_cast<float2*>(d.m8);
   uint16_t* p16 = static_cast<uint16_t*>(d.p16);
-  if (d.bits == 4) {
-    pack_row_part<4>(raw, part, p4, m4, p8, m8, p16, block, d.cap4, out_row, d.status, row);
-  } else if (d.bits == 8) {
-    pack_row_part<8>(raw, part, p4, m4, p8, m8, p16, block, d.cap8, out_row, d.status, row);
+  if (bits == 4) {
+    pack_row_part<4>(raw, part, p4, m4, p8, m8, p16, block, cap, out_row, d.status, row);
+  } else if (bits == 8) {
+    pack_row_part<8>(raw, part, p4, m4, p8, m8, p16, block, cap, out_row, d.status, row);
   } else {
-    pack_row_part<16>(raw, part, p4, m4, p8, m8, p16, block, d.cap16, out_row, d.status, row);
+    pack_row_part<16>(raw, part, p4, m4, p8, m8, p16, block, cap, out_row, d.status, row);
   }
   if (d.map_rows != nullptr && kv == 0 && head == 0 && part == 0) {
-    d.map_rows[d.map_start + token] = static_cast<int32_t>(out_row);
-    d.map_codes[d.map_start + token] = static_cast<uint8_t>(d.bits);
+    const int64_t at = d.map_start + token;
+    if (d.map_codes == nullptr || d.map_start < 0 || d.map_start + n > d.map_capacity) {
+      report(d.status, DKV_ECAPACITY, blockIdx.y);
+    } else {
+      d.map_rows[at] = static_cast<int32_t>(out_row);
+      d.map_codes[at] = static_cast<uint8_t>(bits);
+    }
   }
 }
 
@@ -208,11 +236,10 @@ cudaError_t launch_pack(const void* k, const void* v, void* p4, void* m4, void* 
                             heads, status);
 }
 
-cudaError_t launch_pack_many(const void* k, const void* v, const dkv_pack_target* targets, int count, int64_t kh,
-                             int64_t kt, int64_t vh, int64_t vt, int64_t kc, int64_t vc, int layer, int n, int heads,
-                             cudaStream_t stream) {
-  PackTable tab{};
-  for (int r = 0; r < count; ++r) tab.t[r] = targets[r];
+template <class Targets>
+cudaError_t launch_pack_many_with(const void* k, const void* v, const Targets& tab, int count, int64_t kh,
+                                  int64_t kt, int64_t vh, int64_t vt, int64_t kc, int64_t vc, int layer, int n,
+                                  int heads, cudaStream_t stream) {
   const int threads = 2 * heads * n * 8;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((threads + kPackThreads - 1) / kPackThreads, count);
@@ -223,8 +250,20 @@ cudaError_t launch_pack_many(const void* k, const void* v, const dkv_pack_target
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, pack_rows_many_kernel, static_cast<const uint16_t*>(k),
+  return cudaLaunchKernelEx(&cfg, pack_rows_many_kernel<Targets>, static_cast<const uint16_t*>(k),
                             static_cast<const uint16_t*>(v), tab, kh, kt, vh, vt, kc, vc, layer, n, heads);
+}
+
+// targets: host array (copied into the launch) or, with on_device, device memory.
+cudaError_t launch_pack_many(const void* k, const void* v, const dkv_pack_target* targets, bool on_device, int count,
+                             int64_t kh, int64_t kt, int64_t vh, int64_t vt, int64_t kc, int64_t vc, int layer, int n,
+                             int heads, cudaStream_t stream) {
+  if (on_device)
+    return launch_pack_many_with(k, v, DevicePackTargets{targets}, count, kh, kt, vh, vt, kc, vc, layer, n, heads,
+                                 stream);
+  PackTable tab{};
+  for (int r = 0; r < count; ++r) tab.t[r] = targets[r];
+  return launch_pack_many_with(k, v, tab, count, kh, kt, vh, vt, kc, vc, layer, n, heads, stream);
 }
 
 cudaError_t launch_reconstruct(const Pools& P, const int32_t* rows, const uint8_t* codes, void* out,

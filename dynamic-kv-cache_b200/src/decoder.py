@@ -15,7 +15,8 @@ from dataclasses import dataclass
 import torch
 import torch.nn.functional as F
 
-from .gpu_cache import GPUCache, append_many, attend_many
+from . import gpu_kernels as K
+from .gpu_cache import GPUCache, RequestBatch, append_many, attend_many
 from .gpu_ops import activation_product, cuda_rms
 
 
@@ -177,6 +178,36 @@ class Decoder(torch.nn.Module):
         h = self.rms(x[:, -logits:], self.norm_out)
         return F.linear(h, self.embed).float()
 
+    def forward_device(self, batch, x, logits=0):
+        """One frame step of the B requests of `batch` (a RequestBatch whose
+        prepare() has run): x [B, n, hidden]. Like forward_many, but every cache
+        operation reads the batch's device-resident descriptors, so the whole step
+        can be captured once as a CUDA graph and replayed (FrameGraph)."""
+        c = self.cfg
+        b, n = x.shape[0], x.shape[1]
+        cos, sin = rope_tables(c, batch.positions.reshape(-1), x.device)
+        cos, sin = cos.view(b, 1, n, -1), sin.view(b, 1, n, -1)
+        for layer in range(c.layers):
+            h = self.rms(x, self.norm_attn[layer])
+            q, k, v = F.linear(h, self.qkv[layer]).split(
+                [c.q_heads * c.head_dim, c.kv_heads * c.head_dim, c.kv_heads * c.head_dim], dim=-1)
+            q = q.view(b, n, c.q_heads, c.head_dim).transpose(1, 2)
+            k = k.view(b, n, c.kv_heads, c.head_dim).transpose(1, 2)
+            v = v.view(b, n, c.kv_heads, c.head_dim).transpose(1, 2)
+            q, k = apply_rope(q, cos, sin), apply_rope(k, cos, sin)
+            K.pack_rows_many_device(k, v, batch.targets_ptr, b, layer, n, c.kv_heads, c.head_dim, c.layers)
+            out = torch.empty((b, n, c.q_heads, c.head_dim), dtype=x.dtype, device=x.device)
+            K.packed_attention_many_device(q, k, v, batch.histories_ptr, b, batch.max_past, out, layer, n, c.kv_heads,
+                                           c.q_heads // c.kv_heads, c.head_dim, c.layers)
+            x = x + F.linear(out.reshape(b, n, -1), self.o[layer])
+            h = self.rms(x, self.norm_mlp[layer])
+            gate, up = F.linear(h, self.gate_up[layer]).chunk(2, dim=-1)
+            x = x + F.linear(activation_product(gate, up), self.down[layer])
+        if not logits:
+            return None
+        h = self.rms(x[:, -logits:], self.norm_out)
+        return F.linear(h, self.embed).float()
+
     def forward_chunks(self, cache, ids, logits):
         """B equal-length token chunks (ids [B, n]) after the cache's history, side by
         side, without appending; returns fp32 logits [B, logits, vocab] of each
@@ -210,3 +241,45 @@ class Decoder(torch.nn.Module):
             return None
         h = self.rms(x[:, -logits:], self.norm_out)
         return F.linear(h, self.embed).float()
+
+
+class FrameGraph:
+    """Frame steps of B requests replayed from one CUDA graph (the graph-captured
+    append of every layer; not in the reference, which launches each layer's
+    kernels from Python on every frame). The first step runs eagerly (it is also
+    the warm-up); the graph of the whole decoder step is then captured once and
+    every later step is: host bookkeeping + one descriptor copy (RequestBatch),
+    one input copy, one graph replay. Steps must keep the frame length n; the
+    caches' precision may change per step (select() before step())."""
+
+    def __init__(self, model, caches, n, logits=0, max_past=None):
+        self.model, self.n, self.logits = model, n, logits
+        self.batch = RequestBatch(caches, n, max_past)
+        dev = self.batch.device
+        self.x = torch.empty((len(caches), n, model.cfg.hidden), dtype=model.embed.dtype, device=dev)
+        self.stream = torch.cuda.Stream(dev)
+        self.graph = None
+        self.out = None
+
+    def step(self, embeds=None, ids=None):
+        """Appends one frame (embeds [B, n, hidden] or ids [B, n]) to every cache;
+        returns the logits of the last `logits` positions (None if 0). The returned
+        tensor is the graph's output buffer: the next step overwrites it."""
+        x = self.model.embed[ids] if embeds is None else embeds
+        if tuple(x.shape) != tuple(self.x.shape):
+            raise ValueError(f'frame step expects inputs of shape {tuple(self.x.shape)}')
+        self.batch.prepare()
+        self.x.copy_(x)
+        if self.graph is not None:
+            self.graph.replay()
+            return self.out
+        current = torch.cuda.current_stream(self.batch.device)
+        self.stream.wait_stream(current)
+        with torch.cuda.stream(self.stream):
+            out = self.model.forward_device(self.batch, self.x, self.logits)  # the eager first step (warm-up)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=self.stream):
+                self.out = self.model.forward_device(self.batch, self.x, self.logits)
+        current.wait_stream(self.stream)
+        self.graph = graph
+        return out

@@ -8,6 +8,7 @@ maps `rows`/`codes` and `accounting()` read exactly as the reference's do. The
 Triton launches are replaced by the sm_100a kernels of libdkv.so (gpu_kernels),
 and the per-token map update is one device launch (map_fill).
 """
+import ctypes
 import types
 
 import torch
@@ -141,6 +142,23 @@ class GPUCache(DynamicCache):
                              f'bits {self.pending_bits}')
         return past, n, segment[3] + past - segment[0]
 
+    def _claim_frame(self, n):
+        """The claims of one n-token append on every layer at once (the bookkeeping
+        append() does layer by layer, for a frame whose rows are written by a
+        device-descriptor launch). Every layer must hold the same history.
+        Returns (past, first pool row) and advances every layer."""
+        past = self.seen[0]
+        if any(s != past for s in self.seen):
+            raise ValueError('GPU cache layers disagree about the history length')
+        row = None
+        for layer in range(self.layers) if not self.online else (0,):
+            _, _, r = self._claim(layer, n, fill_map=False)
+            if row is not None and r != row:
+                raise ValueError('GPU cache plan rows differ between layers')
+            row = r
+        self.seen = [past + n] * self.layers
+        return past, row
+
     def attend(self, q, k, v, layer, past):
         """Causal GQA attention of the n new queries over the packed history plus
         the native new K/V; returns [1, n, query_heads, dim] (src/gpu_cache.py:96-104)."""
@@ -270,6 +288,19 @@ def install_packed_attention(model):
 # of at most K.MAX_REQUESTS requests), so the model around the cache runs its
 # projections and MLP on B frames at once.
 
+def _history(c, past):
+    return K.History(c.p4.data_ptr(), c.m4.data_ptr(), c.p8.data_ptr(), c.m8.data_ptr(), c.p16.data_ptr(),
+                     c.rows.data_ptr(), c.codes.data_ptr(), c.caps[4], c.caps[8], c.caps[16], past, c.capacity,
+                     c.status.data_ptr())
+
+
+def _pack_target(c, past, row, new_segment):
+    return K.PackTarget(c.p4.data_ptr(), c.m4.data_ptr(), c.p8.data_ptr(), c.m8.data_ptr(), c.p16.data_ptr(),
+                        c.caps[4], c.caps[8], c.caps[16], row, c.pending_bits, 0,
+                        c.rows.data_ptr() if new_segment else None, c.codes.data_ptr() if new_segment else None,
+                        past, c.capacity, c.status.data_ptr())
+
+
 def _same_geometry(caches):
     if not caches:
         raise ValueError('no caches')
@@ -294,14 +325,9 @@ def append_many(caches, k, v, layer):
         raise ValueError('batched appends need caches with their own pools')
     targets, claims = [], []
     for c in caches:
-        new_segment = c.online and layer == 0
         past, n, row = c._claim(layer, n, fill_map=False)
         claims.append(past)
-        targets.append(K.PackTarget(
-            c.p4.data_ptr(), c.m4.data_ptr(), c.p8.data_ptr(), c.m8.data_ptr(), c.p16.data_ptr(),
-            c.caps[4], c.caps[8], c.caps[16], row, c.pending_bits, 0,
-            c.rows.data_ptr() if new_segment else None, c.codes.data_ptr() if new_segment else None,
-            past, c.capacity, c.status.data_ptr()))
+        targets.append(_pack_target(c, past, row, c.online and layer == 0))
     for s in range(0, b, K.MAX_REQUESTS):
         e = min(s + K.MAX_REQUESTS, b)
         K.pack_rows_many(k[s:e], v[s:e], targets[s:e], layer, n, first.heads, first.dim, first.layers)
@@ -319,12 +345,62 @@ def attend_many(caches, q, k, v, layer, pasts):
     if len(pasts) != b or hq % first.heads:
         raise ValueError('one past per cache; query heads must be a multiple of KV heads')
     out = torch.empty((b, n, hq, first.dim), dtype=q.dtype, device=q.device)
-    hist = [K.History(c.p4.data_ptr(), c.m4.data_ptr(), c.p8.data_ptr(), c.m8.data_ptr(), c.p16.data_ptr(),
-                      c.rows.data_ptr(), c.codes.data_ptr(), c.caps[4], c.caps[8], c.caps[16], past,
-                      c.status.data_ptr())
-            for c, past in zip(caches, pasts)]
+    hist = [_history(c, past) for c, past in zip(caches, pasts)]
     for s in range(0, b, K.MAX_REQUESTS):
         e = min(s + K.MAX_REQUESTS, b)
         K.packed_attention_many(q[s:e], k[s:e], v[s:e], hist[s:e], out[s:e], layer, n, first.heads,
                                 hq // first.heads, first.dim, first.layers)
     return out
+
+
+class RequestBatch:
+    """Device-resident descriptors of B caches that append n-token frames together,
+    for CUDA-graph replay of whole frame steps (not in the reference). The pack
+    destinations (dkv_pack_target), histories (dkv_history) and rotary positions
+    of the next step live in one device buffer that the *_many_device kernels
+    read; `prepare()` does every cache's host bookkeeping for the step (the claims
+    GPUCache.append makes on each layer, pool growth included) and refreshes the
+    buffer with one stream-ordered copy from pinned memory. A graph captured over
+    the kernels therefore replays correctly step after step. The histories are
+    planned for at most `max_past` tokens (default: the caches' capacity)."""
+
+    def __init__(self, caches, n, max_past=None):
+        first = _same_geometry(caches)
+        if len({c.p16.data_ptr() for c in caches}) != len(caches):
+            raise ValueError('batched appends need caches with their own pools')
+        self.caches, self.n, self.count = list(caches), n, len(caches)
+        self.layers, self.heads, self.dim, self.device = first.layers, first.heads, first.dim, first.device
+        self.max_past = max(c.capacity for c in caches) if max_past is None else max_past
+        b = self.count
+        self._hist_off = (b * ctypes.sizeof(K.PackTarget) + 255) // 256 * 256
+        self._pos_off = (self._hist_off + b * ctypes.sizeof(K.History) + 255) // 256 * 256
+        total = self._pos_off + b * n * 8
+        self.host = torch.empty(total, dtype=torch.uint8).pin_memory()
+        self.dev = torch.empty(total, dtype=torch.uint8, device=self.device)
+        base = self.host.data_ptr()
+        self._targets = (K.PackTarget * b).from_address(base)
+        self._hists = (K.History * b).from_address(base + self._hist_off)
+        self._positions = self.host[self._pos_off:].view(torch.int64).view(b, n)
+        self.targets_ptr = self.dev.data_ptr()
+        self.histories_ptr = self.dev.data_ptr() + self._hist_off
+        self.positions = self.dev[self._pos_off:].view(torch.int64).view(b, n)  # [B, n] on the device
+        self._copied = None
+        self._ramp = torch.arange(n, dtype=torch.int64)
+
+    def prepare(self):
+        """Claims the next n-token frame of every cache at its selected precision on
+        all layers and writes the step's descriptors to the device (ordered on the
+        current stream before whatever is launched next). Returns the pasts."""
+        if self._copied is not None:
+            self._copied.synchronize()  # the previous step's copy has left the pinned buffer
+        pasts = []
+        for r, c in enumerate(self.caches):
+            past, row = c._claim_frame(self.n)
+            self._targets[r] = _pack_target(c, past, row, c.online)
+            self._hists[r] = _history(c, past)
+            self._positions[r] = self._ramp + past
+            pasts.append(past)
+        self.dev.copy_(self.host, non_blocking=True)
+        self._copied = torch.cuda.Event()
+        self._copied.record()
+        return pasts

@@ -34,7 +34,8 @@ MAX_REQUESTS = 32  # DKV_MAX_REQUESTS
 class History(ctypes.Structure):
     """dkv_history: one request's packed history for packed_attention_many."""
     _fields_ = [('p4', _P), ('m4', _P), ('p8', _P), ('m8', _P), ('p16', _P), ('rows', _P), ('codes', _P),
-                ('cap4', _I64), ('cap8', _I64), ('cap16', _I64), ('past', _I32), ('status', _P)]
+                ('cap4', _I64), ('cap8', _I64), ('cap16', _I64), ('past', _I32), ('capacity', _I32),
+                ('status', _P)]
 
 
 class PackTarget(ctypes.Structure):
@@ -72,6 +73,10 @@ def _load():
         'dkv_packed_attention_many': ([P, P, P, P, I32, P, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64,
                                        I32, I32, I32, I32, I32, I32, P, SZ, P], ctypes.c_int),
         'dkv_packed_attention_many_workspace': ([I32, I32, I32, I32, I32, I32], SZ),
+        'dkv_pack_rows_many_device': ([P, P, P, I32, I64, I64, I64, I64, I64, I64, I32, I32, I32, I32, I32, P],
+                                      ctypes.c_int),
+        'dkv_packed_attention_many_device': ([P, P, P, P, I32, I32, P, I64, I64, I64, I64, I64, I64, I64, I64, I64,
+                                              I64, I32, I32, I32, I32, I32, I32, P, SZ, P], ctypes.c_int),
     }
     for name, (args, res) in sigs.items():
         fn = getattr(lib, name)
@@ -83,7 +88,8 @@ LIB = _load()
 EXPORTS = ('dkv_version', 'dkv_last_error', 'dkv_pack_rows', 'dkv_packed_attention',
            'dkv_packed_attention_workspace', 'dkv_packed_attention_launches', 'dkv_packed_attention_batched',
            'dkv_packed_attention_batched_workspace', 'dkv_reconstruct', 'dkv_map_fill', 'dkv_pack_rows_many',
-           'dkv_packed_attention_many', 'dkv_packed_attention_many_workspace')
+           'dkv_packed_attention_many', 'dkv_packed_attention_many_workspace', 'dkv_pack_rows_many_device',
+           'dkv_packed_attention_many_device')
 
 
 def _check(rc):
@@ -219,6 +225,36 @@ def packed_attention_many(q, knew, vnew, histories, out, layer, nq, heads, group
     workspace = _workspace(q.device, _stream(q), size) if size else None
     _check(LIB.dkv_packed_attention_many(
         _ptr(q), _ptr(knew), _ptr(vnew), ctypes.addressof(table), count, _ptr(out), q.stride(1), q.stride(2),
+        knew.stride(1), knew.stride(2), vnew.stride(1), vnew.stride(2), q.stride(0), knew.stride(0),
+        vnew.stride(0), out.stride(0), layer, nq, heads, group, dim, layers, _ptr(workspace), size, _stream(q)))
+    return out
+
+
+def pack_rows_many_device(k, v, targets_ptr, count, layer, n, heads, dim, layers):
+    """pack_rows_many with the `count` PackTargets in device memory at targets_ptr
+    (CUDA-graph replay reads whatever was written there before each replay)."""
+    k, v = _rows_ready(k), _rows_ready(v)
+    _chunked(k, 'k'), _chunked(v, 'v')
+    if k.shape[0] != count or v.shape[0] != count:
+        raise ValueError('one frame per request')
+    _check(LIB.dkv_pack_rows_many_device(_ptr(k), _ptr(v), targets_ptr, count, k.stride(1), k.stride(2),
+                                         v.stride(1), v.stride(2), k.stride(0), v.stride(0), layer, n, heads, dim,
+                                         layers, _stream(k)))
+
+
+def packed_attention_many_device(q, knew, vnew, histories_ptr, count, max_past, out, layer, nq, heads, group, dim,
+                                 layers):
+    """packed_attention_many with the `count` Histories in device memory at
+    histories_ptr, planned for histories of at most max_past tokens."""
+    q, knew, vnew = (_rows_ready(x) for x in (q, knew, vnew))
+    for x, name in ((q, 'q'), (knew, 'k'), (vnew, 'v'), (out, 'out')):
+        if x.shape[0] != count:
+            raise ValueError('one history per request')
+        _chunked(x, name)
+    size = LIB.dkv_packed_attention_many_workspace(max_past, nq, heads, group, dim, count)
+    workspace = _workspace(q.device, _stream(q), size) if size else None
+    _check(LIB.dkv_packed_attention_many_device(
+        _ptr(q), _ptr(knew), _ptr(vnew), histories_ptr, count, max_past, _ptr(out), q.stride(1), q.stride(2),
         knew.stride(1), knew.stride(2), vnew.stride(1), vnew.stride(2), q.stride(0), knew.stride(0),
         vnew.stride(0), out.stride(0), layer, nq, heads, group, dim, layers, _ptr(workspace), size, _stream(q)))
     return out

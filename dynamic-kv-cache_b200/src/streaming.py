@@ -18,7 +18,7 @@ import random
 
 import torch
 
-from .decoder import SMOLLM2_360M, Decoder, NativeCache
+from .decoder import SMOLLM2_360M, Decoder, FrameGraph, NativeCache
 from .gpu_cache import GPUCache
 
 MODES = ['native', 'fused16', '8', '4', 'dynamic', 'original', 'random']
@@ -98,12 +98,14 @@ class StreamingModel:
         return dict(scores=values, summed=sums.tolist(), prediction=max(range(len(values)), key=values.__getitem__))
 
     @torch.inference_mode()
-    def ingest_many(self, frames, bits, mode, qa_reserve=192):
+    def ingest_many(self, frames, bits, mode, qa_reserve=192, graph=False):
         """ingest() for B requests stepped together (request batching, not in the
         reference): frames[r] / bits[r] are request r's frame embeddings and
         precisions; every request has the same number of frames and frame
         lengths. Each frame step runs the B frames through the decoder at once,
-        every request appended to its own cache. Returns the B caches."""
+        every request appended to its own cache. graph=True replays the frame
+        steps from one captured CUDA graph (FrameGraph; frames of equal length).
+        Returns the B caches."""
         b = len(frames)
         if b == 0 or len(bits) != b or len({len(f) for f in frames}) != 1:
             raise ValueError('request batching needs one bit list per request and equal frame counts')
@@ -111,13 +113,18 @@ class StreamingModel:
             return [self.ingest(f, bt, mode, qa_reserve) for f, bt in zip(frames, bits)]
         caches = [self.create_cache([f.shape[1] for f in fr], mode, qa_reserve) for fr in frames]
         self.model.forward_many(caches, ids=self.prefix_ids.expand(b, -1))
+        lengths = {e.shape[1] for fr in frames for e in fr}
+        stepper = FrameGraph(self.model, caches, lengths.pop()) if graph and len(lengths) == 1 else None
         for i in range(len(frames[0])):
             step = [fr[i] for fr in frames]
             if len({e.shape[1] for e in step}) != 1:
                 raise ValueError('request batching needs equal frame lengths at each step')
             for cache, bt in zip(caches, bits):
                 cache.select(bt[i], i)
-            self.model.forward_many(caches, embeds=torch.cat(step, dim=0))
+            if stepper is not None:
+                stepper.step(embeds=torch.cat(step, dim=0))
+            else:
+                self.model.forward_many(caches, embeds=torch.cat(step, dim=0))
         for cache in caches:
             cache.select(16, -1)
             cache.reserve(16, cache.host_counts[16] + qa_reserve)

@@ -209,6 +209,7 @@ typedef struct dkv_history {
   const uint8_t* codes;  /* token map: precision (4 / 8 / 16) of token t */
   int64_t cap4, cap8, cap16;
   int32_t past;          /* packed history tokens before this call's queries */
+  int32_t capacity;      /* length of rows / codes (past must not exceed it) */
   int32_t* status;       /* this request's device status word (may be NULL) */
 } dkv_history;
 
@@ -260,9 +261,39 @@ int dkv_packed_attention_many(const void* q, const void* knew, const void* vnew,
                               int32_t layers, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Workspace bytes dkv_packed_attention_many needs (0 = none); max_past = the
- * largest requests[r].past of the call. */
+ * largest requests[r].past of the call. The history is divided into as many
+ * splits as fill one wave of the GPU (no more than the longest history has
+ * 64-key tiles); each request splits its own history evenly among them. */
 size_t dkv_packed_attention_many_workspace(int32_t max_past, int32_t nq, int32_t heads, int32_t group,
                                            int32_t dim, int32_t count);
+
+/*
+ * Device-resident descriptors, for CUDA-graph replay: the same two operations
+ * with `targets` / `requests` in device memory (16-byte aligned arrays of
+ * `count` structs, count <= 65535). A captured graph keeps reading the same
+ * arrays, so a caller replays it step after step after writing that step's
+ * descriptors there (rows claimed, history lengths, pools after growth) with a
+ * stream-ordered copy. The host cannot check device-resident descriptors: the
+ * kernels do (precision, pool and map ranges, history length against the map
+ * capacity) and report a bad one to its status word instead of using it.
+ * dkv_packed_attention_many_device plans for histories of at most max_past
+ * tokens (the workspace, from dkv_packed_attention_many_workspace(max_past, ...),
+ * and the split count are fixed by it); a longer history is still attended
+ * completely, in longer splits. With the same max_past and count as a
+ * dkv_packed_attention_many call over the same histories, the output is
+ * bit-identical to it.
+ */
+int dkv_pack_rows_many_device(const void* k, const void* v, const dkv_pack_target* targets, int32_t count,
+                              int64_t kh, int64_t kt, int64_t vh, int64_t vt, int64_t kc, int64_t vc,
+                              int32_t layer, int32_t n, int32_t heads, int32_t dim, int32_t layers,
+                              void* stream);
+
+int dkv_packed_attention_many_device(const void* q, const void* knew, const void* vnew,
+                                     const dkv_history* requests, int32_t count, int32_t max_past, void* out,
+                                     int64_t qh, int64_t qt, int64_t kh, int64_t kt, int64_t vh, int64_t vt,
+                                     int64_t qc, int64_t kc, int64_t vc, int64_t oc,
+                                     int32_t layer, int32_t nq, int32_t heads, int32_t group, int32_t dim,
+                                     int32_t layers, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Dequantised bf16 history of one layer: out[2, heads, n, dim] (K then V) for

@@ -73,6 +73,7 @@ def test_request_descriptor_layouts_match_the_header():
     """The C side static_asserts the same sizes and offsets (csrc/api.cu)."""
     from src import gpu_kernels as K
     assert ctypes.sizeof(K.History) == 96 and K.History.past.offset == 80 and K.History.status.offset == 88
+    assert K.History.capacity.offset == 84
     assert ctypes.sizeof(K.PackTarget) == 120 and K.PackTarget.bits.offset == 72
     assert K.PackTarget.map_rows.offset == 80 and K.PackTarget.status.offset == 112
     assert K.MAX_REQUESTS == int(re.search(r'#define DKV_MAX_REQUESTS (\d+)', HEADER).group(1))
@@ -105,7 +106,7 @@ def test_pack_many_rejects_bad_arguments_on_host(count, over, code, text):
 
 def test_attention_many_rejects_bad_arguments_on_host():
     from src import gpu_kernels as K
-    h = K.History(0x3000, 0x4000, 0x5000, 0x6000, 0x7000, 0x8000, 0x9000, 64, 64, 64, 100, None)
+    h = K.History(0x3000, 0x4000, 0x5000, 0x6000, 0x7000, 0x8000, 0x9000, 64, 64, 64, 100, 128, None)
     table = (K.History * 2)(h, h)
     args = [0x1000, 0x2000, 0x3000, ctypes.addressof(table)]
     rest = [0xA000, 64 * 64, 64, 64 * 64, 64, 64 * 64, 64, 15 * 64 * 64, 5 * 64 * 64, 5 * 64 * 64, 15 * 64 * 64,
@@ -116,6 +117,16 @@ def test_attention_many_rejects_bad_arguments_on_host():
     assert K.LIB.dkv_packed_attention_many_workspace(100, 64, 5, 3, 64, 2) > 0
     rc = K.LIB.dkv_packed_attention_many(*args, 2, *rest)
     assert rc == K.DKV_EWORKSPACE
+    table[1].past = 129
+    rc = K.LIB.dkv_packed_attention_many(*args, 2, *rest)
+    assert rc == K.DKV_EINVAL and 'exceeds its token map' in K.LIB.dkv_last_error().decode()
     table[1].past = -1
     rc = K.LIB.dkv_packed_attention_many(*args, 2, *rest)
     assert rc == K.DKV_EINVAL and 'negative' in K.LIB.dkv_last_error().decode()
+    # device-resident tables: only what the host can see is checked before the launch
+    dev = [0x1000, 0x2000, 0x3000, 0x10008, 2, 100]  # table address not 16-byte aligned
+    rc = K.LIB.dkv_packed_attention_many_device(*dev, *rest)
+    assert rc == K.DKV_EINVAL and 'aligned' in K.LIB.dkv_last_error().decode()
+    rc = K.LIB.dkv_pack_rows_many_device(0x1000, 0x2000, 0x10008, 2, 64 * 64, 64, 64 * 64, 64, 5 * 64 * 64,
+                                         5 * 64 * 64, 0, 64, 5, 64, 1, None)
+    assert rc == K.DKV_EINVAL and 'aligned' in K.LIB.dkv_last_error().decode()

@@ -140,3 +140,138 @@ def test_batched_requests_match_oracle_decoder(cuda, mode):
         assert max(abs(a - b) for a, b in zip(got[r]['scores'], alone['scores'])) < 2e-2
         assert caches[r].seen[0] == model.prefix_ids.shape[1] + 5 * 64
         assert [s[2] for s in caches[r].plan[1:]] == bits[r]
+
+
+def _device_tables(caches, pasts, rows=None):
+    """Pack targets / histories of the caches in device memory (16-byte aligned)."""
+    import ctypes
+    from src.gpu_cache import _history, _pack_target
+    b = len(caches)
+    hist = (K.History * b)(*[_history(c, p) for c, p in zip(caches, pasts)])
+    dev_h = torch.frombuffer(bytearray(bytes(hist)), dtype=torch.uint8).cuda()
+    dev_t = None
+    if rows is not None:
+        tg = (K.PackTarget * b)(*[_pack_target(c, p, r, c.online) for c, p, r in zip(caches, pasts, rows)])
+        dev_t = torch.frombuffer(bytearray(bytes(tg)), dtype=torch.uint8).cuda()
+    assert ctypes.sizeof(K.History) * b == dev_h.numel()
+    return dev_h, dev_t
+
+
+@pytest.mark.parametrize('pasts,n', [((0, 100, 1000, 3000), 64), ((513, 77, 4000), 5)])
+def test_device_descriptors_match_host_descriptors(cuda, pasts, n):
+    """The device-table attention is bit-identical to the by-value one for the same
+    plan bound, and the device-table pack to the host-table pack."""
+    heads, group = 5, 3
+    hist = [_history(71 + i, p, heads=heads, layers=1) for i, p in enumerate(pasts)]
+    caches = [h[0] for h in hist]
+    b = len(pasts)
+    gen = torch.Generator().manual_seed(3)
+    q = torch.randn(b, heads * group, n, 64, generator=gen).bfloat16().cuda()
+    kn = torch.randn(b, heads, n, 64, generator=gen).bfloat16().cuda()
+    vn = torch.randn(b, heads, n, 64, generator=gen).bfloat16().cuda()
+    ref = attend_many(caches, q, kn, vn, 0, list(pasts))
+    dev_h, _ = _device_tables(caches, pasts)
+    out = torch.empty_like(ref)
+    K.packed_attention_many_device(q, kn, vn, dev_h.data_ptr(), b, max(pasts), out, 0, n, heads, group, 64, 1)
+    torch.cuda.synchronize()
+    for c in caches:
+        c.check()
+    assert torch.equal(out, ref)
+    # a larger plan bound changes only the split count: still the oracle's result
+    K.packed_attention_many_device(q, kn, vn, dev_h.data_ptr(), b, 8000, out, 0, n, heads, group, 64, 1)
+    for r in range(b):
+        expected = oracle_attention(hist[r][1], q[r:r + 1].cpu(), kn[r:r + 1].cpu(), vn[r:r + 1].cpu())
+        assert_attention_close(out[r:r + 1], expected, atol=0.01, rtol=0.01)
+    # pack through device tables: same pools as the host-table launch on twin caches
+    twins = [_history(71 + i, p, heads=heads, layers=1)[0] for i, p in enumerate(pasts)]
+    for c, bt in zip(caches + twins, (4, 8, 16, 4)[:b] * 2):
+        c.select(bt, 77)
+    append_many(twins, kn, vn, 0)
+    claims = [c._claim_frame(n) for c in caches]
+    _, dev_t = _device_tables(caches, [p for p, _ in claims], [r for _, r in claims])
+    K.pack_rows_many_device(kn, vn, dev_t.data_ptr(), b, 0, n, heads, 64, 1)
+    for c, t in zip(caches, twins):
+        c.check()
+        total = c.seen[0]
+        assert torch.equal(c.rows[:total], t.rows[:total]) and torch.equal(c.codes[:total], t.codes[:total])
+        for x, y in zip(c.materialize(0), t.materialize(0)):
+            assert torch.equal(x, y)
+
+
+def test_device_descriptor_errors_are_reported_not_used(cuda):
+    """A history longer than its token map and a pack row range beyond the pool are
+    reported to the request's status word; the kernels skip them."""
+    c, _, _, _ = _history(5, 256, layers=1)
+    h = (K.History * 1)(K.History(c.p4.data_ptr(), c.m4.data_ptr(), c.p8.data_ptr(), c.m8.data_ptr(),
+                                   c.p16.data_ptr(), c.rows.data_ptr(), c.codes.data_ptr(), c.caps[4], c.caps[8],
+                                   c.caps[16], c.capacity + 1, c.capacity, c.status.data_ptr()))
+    dev_h = torch.frombuffer(bytearray(bytes(h)), dtype=torch.uint8).cuda()
+    q = torch.zeros(1, 15, 64, 64, dtype=torch.bfloat16, device='cuda')
+    kv = torch.zeros(1, 5, 64, 64, dtype=torch.bfloat16, device='cuda')
+    out = torch.empty(1, 64, 15, 64, dtype=torch.bfloat16, device='cuda')
+    K.packed_attention_many_device(q, kv, kv, dev_h.data_ptr(), 1, 256, out, 0, 64, 5, 3, 64, 1)
+    with pytest.raises(ValueError, match='invalid argument'):
+        c.check()
+    from src.gpu_cache import _pack_target
+    t = (K.PackTarget * 1)(_pack_target(c, 256, c.caps[16] - 10, False))
+    t[0].bits = 16
+    dev_t = torch.frombuffer(bytearray(bytes(t)), dtype=torch.uint8).cuda()
+    K.pack_rows_many_device(kv, kv, dev_t.data_ptr(), 1, 0, 64, 5, 64, 1)
+    with pytest.raises(ValueError, match='capacity'):
+        c.check()
+
+
+@pytest.mark.parametrize('mode', ['fused16', 'dynamic'])
+def test_frame_graph_ingest_matches_eager_batched_ingest(cuda, mode):
+    """Frames appended by replaying one captured graph give the same caches and
+    scores as the eager batched ingest (the first frames' plan bound differs, so
+    within floating-point order; then identical precision plans)."""
+    model = StreamingModel(TINY, device='cuda', seed=21)
+    reqs = [synthetic_request(TINY, seed=s, frames=6, frame_tokens=64, question_tokens=12, candidates=3,
+                              candidate_tokens=6, device='cuda') for s in (1, 2, 3)]
+    bits = [bits_for(mode, 6, seed=s) for s in (1, 2, 3)]
+    eager = model.ingest_many([r[0] for r in reqs], bits, mode, qa_reserve=64)
+    graphed = model.ingest_many([r[0] for r in reqs], bits, mode, qa_reserve=64, graph=True)
+    oracle = OracleDecoder(TINY, decoder_params(model.model))
+    got = model.answer_many([r[1] for r in reqs], [r[2] for r in reqs], graphed)
+    want = model.answer_many([r[1] for r in reqs], [r[2] for r in reqs], eager)
+    for r, (embeds, question, cands) in enumerate(reqs):
+        graphed[r].check()
+        assert graphed[r].plan == eager[r].plan and graphed[r].seen == eager[r].seen
+        for x, y in zip(graphed[r].materialize(0), eager[r].materialize(0)):  # layer 0 K/V precede any attention
+            assert torch.equal(x, y)
+        means, _ = oracle.request(model.prefix_ids, embeds, bits[r], question, cands)
+        assert max(abs(a - b) for a, b in zip(got[r]['scores'], means)) < 2e-2, (got[r]['scores'], means)
+        assert max(abs(a - b) for a, b in zip(got[r]['scores'], want[r]['scores'])) < 2e-2
+
+
+def test_frame_graph_replay_matches_its_eager_step(cuda):
+    """Replaying the captured step computes exactly what the eager device-descriptor
+    step computes for the same frame."""
+    from src.decoder import FrameGraph
+    model = StreamingModel(TINY, device='cuda', seed=3)
+    gen = torch.Generator().manual_seed(8)
+    frames = [(torch.randn(2, 64, TINY.hidden, generator=gen) * 0.02).bfloat16().cuda() for _ in range(4)]
+
+    def caches():
+        cs = [model.create_cache([64] * 4, 'dynamic', qa_reserve=64) for _ in range(2)]
+        model.model.forward_many(cs, ids=model.prefix_ids.expand(2, -1))
+        return cs
+
+    a, b = caches(), caches()
+    ga = FrameGraph(model.model, a, 64, logits=3, max_past=512)
+    gb = FrameGraph(model.model, b, 64, logits=3, max_past=512)
+    with torch.inference_mode():
+        for i, x in enumerate(frames):
+            for c, bt in zip(a + b, (4, 16, 4, 16) if i % 2 else (8, 4, 8, 4)):
+                c.select(bt, i)
+            la = ga.step(embeds=x).clone()  # eager at i = 0, replayed afterwards
+            gb.batch.prepare()             # b: the eager device-descriptor step every time
+            gb.x.copy_(x)
+            lb = model.model.forward_device(gb.batch, gb.x, 3)
+            assert torch.equal(la, lb), i
+    for x, y in zip(a, b):
+        x.check()
+        for layer in range(TINY.layers):
+            for p, q in zip(x.materialize(layer), y.materialize(layer)):
+                assert torch.equal(p, q)

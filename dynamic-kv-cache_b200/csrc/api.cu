@@ -143,7 +143,8 @@ int launch_planned(dkv::AttnArgs& a, const dkv::AttnPlan& p, const void* q, cons
                    void* out, int64_t qh, int64_t qt, int64_t kh, int64_t kt, int64_t vh, int64_t vt, int32_t chunks,
                    int64_t qc, int64_t kc, int64_t vc, int64_t oc, int32_t layer, int32_t nq, int32_t heads,
                    int32_t group, void* workspace, void* stream, const dkv::HistoryTable* table,
-                   const dkv_history* device_table = nullptr) {
+                   const dkv_history* device_table = nullptr, const dkv_pack_target* pack = nullptr,
+                   bool pack_on_device = false) {
   a.q = static_cast<const uint16_t*>(q);
   a.knew = static_cast<const uint16_t*>(knew);
   a.vnew = static_cast<const uint16_t*>(vnew);
@@ -168,6 +169,19 @@ int launch_planned(dkv::AttnArgs& a, const dkv::AttnPlan& p, const void* q, cons
   }
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int zdim = heads * chunks;  // grid z: chunk * heads + KV head
+  if (pack != nullptr) {  // append + attend: the tensor-core kernel packs too, else a pack launch first
+    if (p.tc && pack_on_device) {
+      a.pack_mode = 2;
+      a.pack_table = pack;
+    } else if (p.tc && chunks == 1) {
+      a.pack_mode = 1;
+      a.pack = *pack;
+    } else {
+      const cudaError_t e = dkv::launch_pack_many(knew, vnew, pack, pack_on_device, chunks, kh, kt, vh, vt, kc, vc,
+                                                  layer, nq, heads, st);
+      if (e != cudaSuccess) return cuda_status(e, "pack launch");
+    }
+  }
   cudaError_t e = p.tc ? dkv::launch_attention_tc(a, zdim, st, table, device_table)
                        : dkv::launch_attention_split(a, zdim, st, table, device_table);
   if (e == cudaSuccess && p.splits > 1 && !a.fused) e = dkv::launch_attention_combine(a, zdim, st);
@@ -180,7 +194,7 @@ int attention_impl(const void* q, const void* knew, const void* vnew, const void
                    int64_t qc, int64_t kc, int64_t vc, int64_t oc, int32_t layer, int32_t past, int32_t nq,
                    int64_t cap4, int64_t cap8, int64_t cap16, int32_t heads, int32_t group, int32_t dim,
                    int32_t block_m, int32_t block_n, int32_t layers, void* workspace, size_t workspace_bytes,
-                   int32_t* status, void* stream) {
+                   int32_t* status, void* stream, const dkv_pack_target* pack = nullptr) {
   int rc = check_geometry(heads, dim, layers, layer);
   if (rc) return rc;
   if ((rc = check_pools(p4, m4, p8, m8, p16, cap4, cap8, cap16))) return rc;
@@ -207,7 +221,7 @@ int attention_impl(const void* q, const void* knew, const void* vnew, const void
   dkv::AttnArgs a{};
   a.hist = dkv_history{p4, m4, p8, m8, p16, rows, codes, cap4, cap8, cap16, past, past, status};
   return launch_planned(a, p, q, knew, vnew, out, qh, qt, kh, kt, vh, vt, chunks, qc, kc, vc, oc, layer, nq, heads,
-                        group, workspace, stream, nullptr);
+                        group, workspace, stream, nullptr, nullptr, pack, false);
 }
 
 }  // namespace
@@ -299,7 +313,8 @@ static int attention_many_launch(const void* q, const void* knew, const void* vn
                           const dkv_history* device_table, int32_t count, int32_t max_past, void* out, int64_t qh,
                           int64_t qt, int64_t kh, int64_t kt, int64_t vh, int64_t vt, int64_t qc, int64_t kc,
                           int64_t vc, int64_t oc, int32_t layer, int32_t nq, int32_t heads, int32_t group,
-                          void* workspace, size_t workspace_bytes, void* stream) {
+                          void* workspace, size_t workspace_bytes, void* stream,
+                          const dkv_pack_target* device_pack = nullptr) {
   if (nq == 0) return ok();
   if (!rows_aligned(q, qh, qt) || !rows_aligned(knew, kh, kt) || !rows_aligned(vnew, vh, vt))
     return fail(DKV_EINVAL, "q/k/v rows must be 16-byte aligned (head/token strides multiples of 8)");
@@ -311,9 +326,10 @@ static int attention_many_launch(const void* q, const void* knew, const void* vn
     return fail(DKV_EWORKSPACE, "attention workspace needs %zu bytes, got %zu", need, workspace_bytes);
   if (need > 0 && (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
     return fail(DKV_EWORKSPACE, "attention workspace must be 256-byte aligned");
+  if (2LL * heads * nq * 8 > INT32_MAX) return fail(DKV_EINVAL, "frame too large");
   dkv::AttnArgs a{};
   return launch_planned(a, p, q, knew, vnew, out, qh, qt, kh, kt, vh, vt, count, qc, kc, vc, oc, layer, nq, heads,
-                        group, workspace, stream, table, device_table);
+                        group, workspace, stream, table, device_table, device_pack, device_pack != nullptr);
 }
 
 int dkv_packed_attention_many(const void* q, const void* knew, const void* vnew, const dkv_history* requests,
@@ -365,6 +381,53 @@ int dkv_packed_attention_many_device(const void* q, const void* knew, const void
     return fail(DKV_EINVAL, "chunk strides must keep rows 16-byte aligned (multiples of 8 elements)");
   return attention_many_launch(q, knew, vnew, nullptr, requests, count, max_past, out, qh, qt, kh, kt, vh, vt, qc, kc,
                                vc, oc, layer, nq, heads, group, workspace, workspace_bytes, stream);
+}
+
+int dkv_append_attention(const void* q, const void* knew, const void* vnew, void* p4, void* m4, void* p8, void* m8,
+                         void* p16, int32_t* rows, uint8_t* codes, void* out, int64_t qh, int64_t qt, int64_t kh,
+                         int64_t kt, int64_t vh, int64_t vt, int32_t layer, int32_t past, int32_t nq,
+                         int64_t row_start, int32_t bits, int32_t fill_map, int64_t map_capacity, int64_t cap4,
+                         int64_t cap8, int64_t cap16, int32_t heads, int32_t group, int32_t dim, int32_t block_m,
+                         int32_t block_n, int32_t layers, void* workspace, size_t workspace_bytes, int32_t* status,
+                         void* stream) {
+  int rc = check_geometry(heads, dim, layers, layer);
+  if (rc) return rc;
+  if ((rc = check_pools(p4, m4, p8, m8, p16, cap4, cap8, cap16))) return rc;
+  if (bits != 4 && bits != 8 && bits != 16) return fail(DKV_EINVAL, "Supported bit widths: 4, 8, 16");
+  if (nq < 0 || past < 0) return fail(DKV_EINVAL, "negative past or query length");
+  const int64_t cap = bits == 4 ? cap4 : (bits == 8 ? cap8 : cap16);
+  if (row_start < 0 || row_start + nq > cap)
+    return fail(DKV_ECAPACITY, "rows [%lld, %lld) exceed the %d-bit pool capacity %lld", (long long)row_start,
+                (long long)(row_start + nq), bits, (long long)cap);
+  if (row_start + nq > INT32_MAX) return fail(DKV_ECAPACITY, "pool row exceeds int32");
+  if (fill_map && (rows == nullptr || codes == nullptr)) return fail(DKV_EINVAL, "null token map");
+  if (fill_map && past + static_cast<int64_t>(nq) > map_capacity)
+    return fail(DKV_ECAPACITY, "GPU context limit exceeded");
+  if (2LL * heads * nq * 8 > INT32_MAX) return fail(DKV_EINVAL, "frame too large");
+  const dkv_pack_target t{p4, m4, p8, m8, p16, cap4, cap8, cap16, row_start, bits, 0,
+                          fill_map ? rows : nullptr, fill_map ? codes : nullptr, past, map_capacity, status};
+  return attention_impl(q, knew, vnew, p4, m4, p8, m8, p16, rows, codes, out, qh, qt, kh, kt, vh, vt, 1, 0, 0, 0, 0,
+                        layer, past, nq, cap4, cap8, cap16, heads, group, dim, block_m, block_n, layers, workspace,
+                        workspace_bytes, status, stream, &t);
+}
+
+int dkv_append_attention_many_device(const void* q, const void* knew, const void* vnew,
+                                     const dkv_pack_target* targets, const dkv_history* requests, int32_t count,
+                                     int32_t max_past, void* out, int64_t qh, int64_t qt, int64_t kh, int64_t kt,
+                                     int64_t vh, int64_t vt, int64_t qc, int64_t kc, int64_t vc, int64_t oc,
+                                     int32_t layer, int32_t nq, int32_t heads, int32_t group, int32_t dim,
+                                     int32_t layers, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_geometry(heads, dim, layers, layer);
+  if (rc) return rc;
+  if (count <= 0 || count > 65535) return fail(DKV_EINVAL, "request count %d outside [1, 65535]", count);
+  if (requests == nullptr || !aligned16(requests) || targets == nullptr || !aligned16(targets))
+    return fail(DKV_EINVAL, "device request tables must be 16-byte aligned");
+  if (group <= 0) return fail(DKV_EINVAL, "query heads must be a positive multiple of KV heads");
+  if (nq < 0 || max_past < 0) return fail(DKV_EINVAL, "negative past or query length");
+  if ((qc % 8) || (kc % 8) || (vc % 8) || (oc % 8))
+    return fail(DKV_EINVAL, "chunk strides must keep rows 16-byte aligned (multiples of 8 elements)");
+  return attention_many_launch(q, knew, vnew, nullptr, requests, count, max_past, out, qh, qt, kh, kt, vh, vt, qc, kc,
+                               vc, oc, layer, nq, heads, group, workspace, workspace_bytes, stream, targets);
 }
 
 int dkv_reconstruct(const void* p4, const void* m4, const void* p8, const void* m8, const void* p16,

@@ -121,7 +121,17 @@ struct AttnArgs {
   float2* ws_ml;  // [heads * mblocks][cta_rows][even(splits)] (running max in log2 units, sum)
   uint32_t* sync;  // [2][kSyncGroups] arrival / departure counters of the in-kernel merge
   int fused;       // 1: the attention kernel merges the splits itself (no combine launch)
+  // Fused pack of the call's new K/V rows into the pools (append + attend in one
+  // launch; tensor-core kernel only): 0 none, 1 every chunk's frame into `pack`,
+  // 2 chunk c's frame into pack_table[c] (device memory).
+  int pack_mode;
+  dkv_pack_target pack;
+  const dkv_pack_target* pack_table;
 };
+
+__device__ __forceinline__ const dkv_pack_target* pack_of(const AttnArgs& a, int chunk) {
+  return a.pack_mode == 1 ? &a.pack : (a.pack_mode == 2 ? a.pack_table + chunk : nullptr);
+}
 
 // The history query chunk c attends over.
 __device__ __forceinline__ const History& history_of(const AttnArgs& a, const SharedHistory&, int) {

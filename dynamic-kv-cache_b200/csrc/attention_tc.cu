@@ -41,6 +41,7 @@
 #include <cstring>
 
 #include "attention.cuh"
+#include "pack_row.cuh"
 #include "tc_ptx.cuh"
 
 namespace dkv {
@@ -952,7 +953,34 @@ attention_tc_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ 
     tmem_dealloc(tmem, kTmemCols);
   }
 
+  // The fused pack (append + attend in one launch): the CTAs of this (chunk, KV
+  // head) share the head's 2 x nq new rows; a CTA packs its share while the other
+  // splits of its group finish (after publishing its partial), or after its
+  // epilogue when there is no in-kernel merge. The rows written (>= past) are not
+  // read by this call, which takes the new K/V natively.
+  auto fused_pack = [&]() {
+    const int pchunk = blockIdx.z / a.heads, pg = blockIdx.z - pchunk * a.heads;
+    const dkv_pack_target* d = pack_of(a, pchunk);
+    if (d == nullptr) return;
+    pdl_wait();  // the new K/V are the previous kernel's output
+    if (!pack_target_ok(*d, a.nq)) {
+      if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) report_bad_target(*d, a.nq, pchunk);
+      return;
+    }
+    const int ctas = gridDim.x * gridDim.y, j = blockIdx.x + gridDim.x * blockIdx.y;
+    const int rows = 2 * a.nq, per = (rows + ctas - 1) / ctas;
+    const int r_end = min((j + 1) * per, rows);
+    const uint16_t* k = a.knew + pchunk * a.kc;
+    const uint16_t* v = a.vnew + pchunk * a.vc;
+    for (int r = j * per + (threadIdx.x >> 3); r < r_end; r += kThreadsTc / 8) {  // r: kv * nq + token
+      const int kv = r >= a.nq;
+      pack_frame_row(*d, k, v, a.kh, a.kt, a.vh, a.vt, a.layer, a.nq, a.heads, kv, pg, r - kv * a.nq,
+                     threadIdx.x & 7, r);
+    }
+  };
+
   // ================= in-kernel split merge =================
+  if (!a.fused) fused_pack();
   if (a.fused) {
     // block coordinates re-read here so nothing stays live across the roles above
     const int msplit = blockIdx.x, mrow0 = blockIdx.y * kTcCtaRows, mz = blockIdx.z;
@@ -968,6 +996,9 @@ attention_tc_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ 
       // release at GPU scope, cumulative over the partials every thread of this CTA
       // stored before the barrier above: whoever acquires this arrival sees them
       red_add_release(arrive, 1u);
+    }
+    fused_pack();
+    if (tid == 0) {
       const long long start = clock64();
       int ready = 1;
       while (ld_acquire(arrive) < static_cast<uint32_t>(a.splits)) {

@@ -8,74 +8,12 @@
 // eight consecutive threads; thread `part` owns dims 8*part..8*part+7 and moves
 // them with one 128-bit (bf16), 64-bit (int8) or 32-bit (int4) access, so a warp
 // touches four whole rows with fully coalesced traffic.
-#include "dkv_common.cuh"
+#include "pack_row.cuh"
 
 namespace dkv {
 
 constexpr int kPackThreads = 256;
 constexpr int kMaxPackRequests = DKV_MAX_REQUESTS;
-
-// Quantises part `part` (dims 8*part .. 8*part+7) of one 64-wide row held in
-// `raw` (8 bf16) and stores it at row `out_row` of pool block `block` (the
-// (layer, K|V, head) slab of `cap` rows). The eight lanes of a row must call it
-// together (row min/max by shuffles within the 8-lane group).
-template <int BITS>
-__device__ __forceinline__ void pack_row_part(uint4 raw, int part, uint8_t* p4, float2* m4, uint8_t* p8,
-                                              float2* m8, uint16_t* p16, int64_t block, int64_t cap,
-                                              int64_t out_row, int32_t* status, int report_row) {
-  float x[8];
-  x[0] = bf16_lo(raw.x); x[1] = bf16_hi(raw.x);
-  x[2] = bf16_lo(raw.y); x[3] = bf16_hi(raw.y);
-  x[4] = bf16_lo(raw.z); x[5] = bf16_hi(raw.z);
-  x[6] = bf16_lo(raw.w); x[7] = bf16_hi(raw.w);
-  bool finite = true;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) finite &= isfinite(x[i]);
-  if (!finite) report(status, DKV_ENONFINITE, report_row);
-
-  if (BITS == 16) {
-    reinterpret_cast<uint4*>(p16 + (block * cap + out_row) * kDim)[part] = raw;
-    return;
-  }
-
-  // Row min/max over the 8 lanes of this row's group.
-  const unsigned lane = threadIdx.x & 31;
-  const unsigned mask = 0xffu << (lane & 24);
-  float mn = x[0], mx = x[0];
-#pragma unroll
-  for (int i = 1; i < 8; ++i) { mn = fminf(mn, x[i]); mx = fmaxf(mx, x[i]); }
-#pragma unroll
-  for (int off = 1; off < 8; off <<= 1) {
-    mn = fminf(mn, __shfl_xor_sync(mask, mn, off, 8));
-    mx = fmaxf(mx, __shfl_xor_sync(mask, mx, off, 8));
-  }
-  // Operation order of src/kv_quantization.py:63-66, every step IEEE fp32
-  // round-to-nearest (explicit intrinsics: no contraction into FMA).
-  constexpr float kLevels = static_cast<float>((1 << BITS) - 1);
-  const float offset = mn;
-  const float span = __fsub_rn(mx, offset);
-  const float scale = span > 0.f ? __fdiv_rn(span, kLevels) : 1.f;
-  uint32_t q[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    float t = rintf(__fdiv_rn(__fsub_rn(x[i], offset), scale));  // round half to even
-    t = fminf(fmaxf(t, 0.f), kLevels);
-    q[i] = static_cast<uint32_t>(t);
-  }
-  if (BITS == 8) {
-    uint2 w;
-    w.x = q[0] | (q[1] << 8) | (q[2] << 16) | (q[3] << 24);
-    w.y = q[4] | (q[5] << 8) | (q[6] << 16) | (q[7] << 24);
-    reinterpret_cast<uint2*>(p8 + (block * cap + out_row) * kRowBytes8)[part] = w;
-    if (part == 0) m8[block * cap + out_row] = make_float2(offset, scale);
-  } else {
-    uint32_t w = 0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) w |= (q[2 * j] | (q[2 * j + 1] << 4)) << (8 * j);
-    reinterpret_cast<uint32_t*>(p4 + (block * cap + out_row) * kRowBytes4)[part] = w;
-    if (part == 0) m4[block * cap + out_row] = make_float2(offset, scale);
-  }
-}
 
 template <int BITS>
 __global__ void __launch_bounds__(kPackThreads)
@@ -131,54 +69,14 @@ pack_rows_many_kernel(const uint16_t* __restrict__ k, const uint16_t* __restrict
   asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
   asm volatile("griddepcontrol.wait;\n" ::: "memory");
   const dkv_pack_target& d = tab[blockIdx.y];
-  const int bits = d.bits;
-  const int64_t cap = bits == 4 ? d.cap4 : (bits == 8 ? d.cap8 : d.cap16);
-  const int64_t row_start = d.row_start;
-  const bool pool_ok = bits == 4 ? (d.p4 != nullptr && d.m4 != nullptr)
-                                 : (bits == 8 ? (d.p8 != nullptr && d.m8 != nullptr) : d.p16 != nullptr);
-  if ((bits != 4 && bits != 8 && bits != 16) || !pool_ok) {
-    if (blockIdx.x == 0 && threadIdx.x == 0) report(d.status, DKV_EINVAL, blockIdx.y);
-    return;
-  }
-  if (row_start < 0 || row_start + n > cap) {
-    if (blockIdx.x == 0 && threadIdx.x == 0) report(d.status, DKV_ECAPACITY, blockIdx.y);
+  if (!pack_target_ok(d, n)) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) report_bad_target(d, n, blockIdx.y);
     return;
   }
   const int gtid = blockIdx.x * blockDim.x + threadIdx.x;
   const int row = gtid >> 3;
-  const int part = gtid & 7;
-  const int per_kv = heads * n;
-  if (row >= 2 * per_kv) return;
-  const int kv = row / per_kv;
-  const int rem = row - kv * per_kv;
-  const int head = rem / n;
-  const int token = rem - head * n;
-  const uint16_t* src = kv == 0 ? k + blockIdx.y * kc + head * kh + token * kt
-                                : v + blockIdx.y * vc + head * vh + token * vt;
-  const uint4 raw = __ldg(reinterpret_cast<const uint4*>(src) + part);
-  const int64_t block = (static_cast<int64_t>(layer) * 2 + kv) * heads + head;
-  const int64_t out_row = row_start + token;
-  uint8_t* p4 = static_cast<uint8_t*>(d.p4);
-  uint8_t* p8 = static_cast<uint8_t*>(d.p8);
-  float2* m4 = static_cast<float2*>(d.m4);
-  float2* m8 = static_cast<float2*>(d.m8);
-  uint16_t* p16 = static_cast<uint16_t*>(d.p16);
-  if (bits == 4) {
-    pack_row_part<4>(raw, part, p4, m4, p8, m8, p16, block, cap, out_row, d.status, row);
-  } else if (bits == 8) {
-    pack_row_part<8>(raw, part, p4, m4, p8, m8, p16, block, cap, out_row, d.status, row);
-  } else {
-    pack_row_part<16>(raw, part, p4, m4, p8, m8, p16, block, cap, out_row, d.status, row);
-  }
-  if (d.map_rows != nullptr && kv == 0 && head == 0 && part == 0) {
-    const int64_t at = d.map_start + token;
-    if (d.map_codes == nullptr || d.map_start < 0 || d.map_start + n > d.map_capacity) {
-      report(d.status, DKV_ECAPACITY, blockIdx.y);
-    } else {
-      d.map_rows[at] = static_cast<int32_t>(out_row);
-      d.map_codes[at] = static_cast<uint8_t>(bits);
-    }
-  }
+  if (row >= 2 * heads * n) return;  // whole 8-lane groups leave together
+  pack_target_row(d, k + blockIdx.y * kc, v + blockIdx.y * vc, kh, kt, vh, vt, layer, n, heads, row, gtid & 7);
 }
 
 __global__ void __launch_bounds__(kPackThreads)

@@ -107,8 +107,7 @@ class Decoder(torch.nn.Module):
         v = v.view(1, n, c.kv_heads, c.head_dim).transpose(1, 2)
         q, k = apply_rope(q, cos, sin), apply_rope(k, cos, sin)
         if isinstance(cache, GPUCache):
-            past = cache.append(k, v, layer)
-            out = cache.attend(q, k, v, layer, past)  # [1, n, q_heads, d]
+            out = cache.append_attend(q, k, v, layer)  # append + attend in one call; [1, n, q_heads, d]
         else:
             past = cache.get_seq_length(layer)
             kk, vv = cache.update(k, v, layer)
@@ -195,10 +194,9 @@ class Decoder(torch.nn.Module):
             k = k.view(b, n, c.kv_heads, c.head_dim).transpose(1, 2)
             v = v.view(b, n, c.kv_heads, c.head_dim).transpose(1, 2)
             q, k = apply_rope(q, cos, sin), apply_rope(k, cos, sin)
-            K.pack_rows_many_device(k, v, batch.targets_ptr, b, layer, n, c.kv_heads, c.head_dim, c.layers)
             out = torch.empty((b, n, c.q_heads, c.head_dim), dtype=x.dtype, device=x.device)
-            K.packed_attention_many_device(q, k, v, batch.histories_ptr, b, batch.max_past, out, layer, n, c.kv_heads,
-                                           c.q_heads // c.kv_heads, c.head_dim, c.layers)
+            K.append_attention_many_device(q, k, v, batch.targets_ptr, batch.histories_ptr, b, batch.max_past, out,
+                                           layer, n, c.kv_heads, c.q_heads // c.kv_heads, c.head_dim, c.layers)
             x = x + F.linear(out.reshape(b, n, -1), self.o[layer])
             h = self.rms(x, self.norm_mlp[layer])
             gate, up = F.linear(h, self.gate_up[layer]).chunk(2, dim=-1)
@@ -260,6 +258,11 @@ class FrameGraph:
         self.stream = torch.cuda.Stream(dev)
         self.graph = None
         self.out = None
+
+    def rebind(self, caches):
+        """Serves another set of caches (same count and geometry) with the same
+        captured graph: the next steps append to them."""
+        self.batch.rebind(caches)
 
     def step(self, embeds=None, ids=None):
         """Appends one frame (embeds [B, n, hidden] or ids [B, n]) to every cache;

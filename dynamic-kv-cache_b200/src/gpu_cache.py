@@ -114,6 +114,24 @@ class GPUCache(DynamicCache):
         self.seen[layer] = past + n
         return past
 
+    def append_attend(self, q, k, v, layer):
+        """append() then attend() of one frame in one call (one launch on the
+        tensor-core path): returns [1, n, query_heads, dim], bit-identical to the
+        two calls. The reference's attention forward makes the two calls back to
+        back (src/gpu_cache.py:172-173)."""
+        if k.shape[0] != 1 or k.shape[-1] != self.dim or k.device.type != 'cuda':
+            raise ValueError('GPU cache requires CUDA, batch one and the configured head dimension')
+        n = q.shape[-2]
+        new_segment = self.online and layer == 0
+        past, n, row = self._claim(layer, k.shape[-2], fill_map=False)
+        out = torch.empty((1, n, q.shape[1], self.dim), dtype=q.dtype, device=q.device)
+        K.append_attention(q, k, v, *self._pools(), self.rows, self.codes, out, layer, past, n, row,
+                           self.pending_bits, new_segment, self.capacity, self.caps[4], self.caps[8], self.caps[16],
+                           self.heads, q.shape[1] // self.heads, self.dim, self.block_m, self.block_n, self.layers,
+                           self.status)
+        self.seen[layer] = past + n
+        return out
+
     def _claim(self, layer, n, fill_map=True):
         """Plan bookkeeping of an n-token append to `layer` at the selected precision
         (src/gpu_cache.py:72-90): returns (past, n, first pool row); the caller
@@ -386,6 +404,17 @@ class RequestBatch:
         self.positions = self.dev[self._pos_off:].view(torch.int64).view(b, n)  # [B, n] on the device
         self._copied = None
         self._ramp = torch.arange(n, dtype=torch.int64)
+
+    def rebind(self, caches):
+        """Points the batch at another set of caches of the same count and geometry
+        (a captured graph reads only the device buffer, so it serves them too)."""
+        first = _same_geometry(caches)
+        if len(caches) != self.count or (first.layers, first.heads, first.dim, first.device) != \
+                (self.layers, self.heads, self.dim, self.device):
+            raise ValueError('rebinding needs as many caches of the same geometry')
+        if len({c.p16.data_ptr() for c in caches}) != len(caches):
+            raise ValueError('batched appends need caches with their own pools')
+        self.caches = list(caches)
 
     def prepare(self):
         """Claims the next n-token frame of every cache at its selected precision on

@@ -77,6 +77,11 @@ def _load():
                                       ctypes.c_int),
         'dkv_packed_attention_many_device': ([P, P, P, P, I32, I32, P, I64, I64, I64, I64, I64, I64, I64, I64, I64,
                                               I64, I32, I32, I32, I32, I32, I32, P, SZ, P], ctypes.c_int),
+        'dkv_append_attention': ([P, P, P, P, P, P, P, P, P, P, P, I64, I64, I64, I64, I64, I64, I32, I32, I32, I64,
+                                  I32, I32, I64, I64, I64, I64, I32, I32, I32, I32, I32, I32, P, SZ, P, P],
+                                 ctypes.c_int),
+        'dkv_append_attention_many_device': ([P, P, P, P, P, I32, I32, P, I64, I64, I64, I64, I64, I64, I64, I64, I64,
+                                              I64, I32, I32, I32, I32, I32, I32, P, SZ, P], ctypes.c_int),
     }
     for name, (args, res) in sigs.items():
         fn = getattr(lib, name)
@@ -89,7 +94,7 @@ EXPORTS = ('dkv_version', 'dkv_last_error', 'dkv_pack_rows', 'dkv_packed_attenti
            'dkv_packed_attention_workspace', 'dkv_packed_attention_launches', 'dkv_packed_attention_batched',
            'dkv_packed_attention_batched_workspace', 'dkv_reconstruct', 'dkv_map_fill', 'dkv_pack_rows_many',
            'dkv_packed_attention_many', 'dkv_packed_attention_many_workspace', 'dkv_pack_rows_many_device',
-           'dkv_packed_attention_many_device')
+           'dkv_packed_attention_many_device', 'dkv_append_attention', 'dkv_append_attention_many_device')
 
 
 def _check(rc):
@@ -256,6 +261,38 @@ def packed_attention_many_device(q, knew, vnew, histories_ptr, count, max_past, 
     _check(LIB.dkv_packed_attention_many_device(
         _ptr(q), _ptr(knew), _ptr(vnew), histories_ptr, count, max_past, _ptr(out), q.stride(1), q.stride(2),
         knew.stride(1), knew.stride(2), vnew.stride(1), vnew.stride(2), q.stride(0), knew.stride(0),
+        vnew.stride(0), out.stride(0), layer, nq, heads, group, dim, layers, _ptr(workspace), size, _stream(q)))
+    return out
+
+
+def append_attention(q, knew, vnew, p4, m4, p8, m8, p16, rows, codes, out, layer, past, nq, row_start, bits,
+                     fill_map, map_capacity, cap4, cap8, cap16, heads, group, dim, block_m, block_n, layers,
+                     status=None):
+    """pack_rows (+ map_fill) and packed_attention of one frame in one launch."""
+    q, knew, vnew = _rows_ready(q), _rows_ready(knew), _rows_ready(vnew)
+    size = attention_workspace_bytes(past, nq, heads, group, dim)
+    workspace = _workspace(q.device, _stream(q), size) if size else None
+    _check(LIB.dkv_append_attention(
+        _ptr(q), _ptr(knew), _ptr(vnew), _ptr(p4), _ptr(m4), _ptr(p8), _ptr(m8), _ptr(p16), _ptr(rows),
+        _ptr(codes), _ptr(out), q.stride(1), q.stride(2), knew.stride(1), knew.stride(2), vnew.stride(1),
+        vnew.stride(2), layer, past, nq, row_start, bits, int(fill_map), map_capacity, cap4, cap8, cap16, heads,
+        group, dim, block_m, block_n, layers, _ptr(workspace), size, _ptr(status), _stream(q)))
+    return out
+
+
+def append_attention_many_device(q, knew, vnew, targets_ptr, histories_ptr, count, max_past, out, layer, nq, heads,
+                                 group, dim, layers):
+    """pack_rows_many_device + packed_attention_many_device in one launch."""
+    q, knew, vnew = (_rows_ready(x) for x in (q, knew, vnew))
+    for x, name in ((q, 'q'), (knew, 'k'), (vnew, 'v'), (out, 'out')):
+        if x.shape[0] != count:
+            raise ValueError('one history per request')
+        _chunked(x, name)
+    size = LIB.dkv_packed_attention_many_workspace(max_past, nq, heads, group, dim, count)
+    workspace = _workspace(q.device, _stream(q), size) if size else None
+    _check(LIB.dkv_append_attention_many_device(
+        _ptr(q), _ptr(knew), _ptr(vnew), targets_ptr, histories_ptr, count, max_past, _ptr(out), q.stride(1),
+        q.stride(2), knew.stride(1), knew.stride(2), vnew.stride(1), vnew.stride(2), q.stride(0), knew.stride(0),
         vnew.stride(0), out.stride(0), layer, nq, heads, group, dim, layers, _ptr(workspace), size, _stream(q)))
     return out
 

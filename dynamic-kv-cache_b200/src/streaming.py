@@ -46,6 +46,18 @@ class StreamingModel:
         self.model = Decoder(cfg, device=device, seed=seed)
         gen = torch.Generator().manual_seed(seed + 1)
         self.prefix_ids = torch.randint(0, cfg.vocab, (1, prefix_tokens), generator=gen).to(self.device)
+        self._frame_graphs = {}  # (requests, frame tokens) -> FrameGraph, captured once and rebound
+
+    def frame_graph(self, caches, n):
+        """The FrameGraph for len(caches) requests of n-token frames, captured on first
+        use and rebound to `caches` afterwards."""
+        key = (len(caches), n)
+        fg = self._frame_graphs.get(key)
+        if fg is None:
+            fg = self._frame_graphs[key] = FrameGraph(self.model, caches, n)
+        else:
+            fg.rebind(caches)
+        return fg
 
     def create_cache(self, frame_lengths, mode, qa_reserve=192, max_tokens=8192):
         """GPUCache with an online plan (or a native cache for mode 'native'),
@@ -114,7 +126,7 @@ class StreamingModel:
         caches = [self.create_cache([f.shape[1] for f in fr], mode, qa_reserve) for fr in frames]
         self.model.forward_many(caches, ids=self.prefix_ids.expand(b, -1))
         lengths = {e.shape[1] for fr in frames for e in fr}
-        stepper = FrameGraph(self.model, caches, lengths.pop()) if graph and len(lengths) == 1 else None
+        stepper = self.frame_graph(caches, lengths.pop()) if graph and len(lengths) == 1 else None
         for i in range(len(frames[0])):
             step = [fr[i] for fr in frames]
             if len({e.shape[1] for e in step}) != 1:

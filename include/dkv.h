@@ -296,6 +296,44 @@ int dkv_packed_attention_many_device(const void* q, const void* knew, const void
                                      int32_t layers, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Append + attend in one launch (no reference counterpart as one call: the
+ * reference's attention forward runs pack_rows then packed_attention back to
+ * back, src/gpu_cache.py:172-173). Packs the nq new rows knew / vnew into rows
+ * [row_start, row_start + nq) of the `bits` pool exactly as dkv_pack_rows does
+ * (with fill_map, also the token-map update of dkv_map_fill at [past, past + nq)),
+ * and computes dkv_packed_attention over the `past` history tokens plus the new
+ * rows read natively. On the tensor-core path (group * nq >= 49) one kernel does
+ * both: its blocks pack their share of the new rows while they wait for the
+ * other history splits. Otherwise a pack launch precedes the attention.
+ * Results are bit-identical to dkv_pack_rows (+ dkv_map_fill) followed by
+ * dkv_packed_attention; same workspace contract as dkv_packed_attention.
+ */
+int dkv_append_attention(const void* q, const void* knew, const void* vnew,
+                         void* p4, void* m4, void* p8, void* m8, void* p16,
+                         int32_t* rows, uint8_t* codes, void* out,
+                         int64_t qh, int64_t qt, int64_t kh, int64_t kt, int64_t vh, int64_t vt,
+                         int32_t layer, int32_t past, int32_t nq,
+                         int64_t row_start, int32_t bits, int32_t fill_map, int64_t map_capacity,
+                         int64_t cap4, int64_t cap8, int64_t cap16,
+                         int32_t heads, int32_t group, int32_t dim,
+                         int32_t block_m, int32_t block_n, int32_t layers,
+                         void* workspace, size_t workspace_bytes, int32_t* status, void* stream);
+
+/*
+ * dkv_append_attention for `count` requests with device-resident descriptors
+ * (CUDA-graph replay of frame steps): request r's frame is packed into
+ * targets[r] and its queries attend over requests[r] plus its new rows. Same as
+ * dkv_pack_rows_many_device followed by dkv_packed_attention_many_device.
+ */
+int dkv_append_attention_many_device(const void* q, const void* knew, const void* vnew,
+                                     const dkv_pack_target* targets, const dkv_history* requests,
+                                     int32_t count, int32_t max_past, void* out,
+                                     int64_t qh, int64_t qt, int64_t kh, int64_t kt, int64_t vh, int64_t vt,
+                                     int64_t qc, int64_t kc, int64_t vc, int64_t oc,
+                                     int32_t layer, int32_t nq, int32_t heads, int32_t group, int32_t dim,
+                                     int32_t layers, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Dequantised bf16 history of one layer: out[2, heads, n, dim] (K then V) for
  * logical tokens [0, n). Replaces Triton `reconstruct` (src/gpu_kernels.py:
  * 107-119), launched by GPUCache.materialize (src/gpu_cache.py:106-112).

@@ -275,3 +275,25 @@ def test_frame_graph_replay_matches_its_eager_step(cuda):
         for layer in range(TINY.layers):
             for p, q in zip(x.materialize(layer), y.materialize(layer)):
                 assert torch.equal(p, q)
+
+
+def test_frame_graph_is_reused_for_the_next_batch(cuda):
+    """The captured frame step is rebound to the next batch's caches: the second
+    batch ingested through the same graph equals its eager ingest."""
+    model = StreamingModel(TINY, device='cuda', seed=5)
+    sets = [[synthetic_request(TINY, seed=s, frames=4, frame_tokens=64, question_tokens=12, candidates=2,
+                               candidate_tokens=6, device='cuda') for s in seeds] for seeds in ((11, 12), (13, 14))]
+    bits = [[bits_for('dynamic', 4, seed=s) for s in seeds] for seeds in ((11, 12), (13, 14))]
+    model.ingest_many([r[0] for r in sets[0]], bits[0], 'dynamic', qa_reserve=64, graph=True)
+    graph = model._frame_graphs[(2, 64)].graph
+    graphed = model.ingest_many([r[0] for r in sets[1]], bits[1], 'dynamic', qa_reserve=64, graph=True)
+    assert model._frame_graphs[(2, 64)].graph is graph  # captured once
+    eager = model.ingest_many([r[0] for r in sets[1]], bits[1], 'dynamic', qa_reserve=64)
+    got = model.answer_many([r[1] for r in sets[1]], [r[2] for r in sets[1]], graphed)
+    want = model.answer_many([r[1] for r in sets[1]], [r[2] for r in sets[1]], eager)
+    for g, e, a, b in zip(graphed, eager, got, want):
+        g.check()
+        assert g.plan == e.plan and g.seen == e.seen
+        for x, y in zip(g.materialize(0), e.materialize(0)):
+            assert torch.equal(x, y)
+        assert max(abs(p - q) for p, q in zip(a['scores'], b['scores'])) < 2e-2

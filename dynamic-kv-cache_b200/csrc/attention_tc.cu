@@ -55,12 +55,19 @@ constexpr int kMapStages = 6;  // token-map ring filled by TMA
 constexpr int kSoftmaxWarps = 8;
 constexpr int kSWarp = 8;
 constexpr int kPVWarp = 9;
-constexpr int kLoadWarp0 = 10;  // two loader warps: even / odd tiles
-constexpr int kLoadWarps = 2;
-constexpr int kConvWarp0 = kLoadWarp0 + kLoadWarps;
+// Warp w runs on SM sub-partition w % 4, and the softmax warp of TMEM lanes
+// 32q..32q+31 must sit on sub-partition q. At the usual 192 stacked rows (3 query
+// heads x 64 queries) both row tiles have rows on sub-partitions 0 and 1 but only
+// the first on 2 and 3, so the four converter warps (the heaviest other role) sit
+// on 2 and 3 (warps 10, 11, 14, 15) and the two loader warps on 0 and 1 (12, 13).
+constexpr int kLoadWarps = 2;   // even / odd tiles
 constexpr int kConvWarps = 4;
-constexpr int kThreadsTc = (kConvWarp0 + kConvWarps) * 32;  // 512
+constexpr int kThreadsTc = 16 * 32;  // 512
 constexpr int kConvThreads = kConvWarps * 32;
+__device__ __forceinline__ bool is_load_warp(int w) { return w == 12 || w == 13; }
+__device__ __forceinline__ int load_index(int w) { return w - 12; }
+__device__ __forceinline__ bool is_conv_warp(int w) { return w == 10 || w == 11 || w == 14 || w == 15; }
+__device__ __forceinline__ int conv_index(int w) { return w - 10 - (w >= 14 ? 2 : 0); }
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0;    // S[buf][mt] at columns (buf * 2 + mt) * 64
 constexpr uint32_t kColO = 256;  // O[mt] (64 fp32) at columns 256 + mt * 64
@@ -411,7 +418,7 @@ attention_tc_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ 
       mbar_wait(bar(B_FINPV), 0, kWaitCycles);
     }
     __syncwarp();
-  } else if (warp >= kLoadWarp0 && warp < kConvWarp0) {
+  } else if (is_load_warp(warp)) {
     // ================= loader: token maps and packed runs by TMA =================
     // Per-CTA block bases (layer, K|V, this head) of every pool, and the parity of
     // each meta block's first pair index, so the per-tile work is 32-bit math.
@@ -474,7 +481,7 @@ attention_tc_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ 
       return par;
     };
 
-    const int lw = warp - kLoadWarp0;  // this warp's tiles: lw, lw + 2, ...
+    const int lw = load_index(warp);  // this warp's tiles: lw, lw + 2, ...
     if (lane == 0) {
       for (int t = lw; t < kMapStages && t < ntiles; t += kLoadWarps) map_tile(t);
     }
@@ -645,9 +652,9 @@ attention_tc_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ 
       *abort_flag = 1;
       report(status, DKV_ETIMEOUT, 3);
     }
-  } else if (warp >= kConvWarp0) {
+  } else if (is_conv_warp(warp)) {
     // ================= converters: raw runs -> swizzled bf16 K / V tiles =================
-    const int ctid = tid - kConvWarp0 * 32;
+    const int ctid = conv_index(warp) * 32 + lane;
     const int c = ctid & 7;    // 8-dim part
     const int jb = ctid >> 3;  // tokens jb + 16 k
     bool ok = true;

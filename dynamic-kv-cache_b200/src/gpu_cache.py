@@ -405,6 +405,11 @@ class RequestBatch:
         self._copied = None
         self._ramp = torch.arange(n, dtype=torch.int64)
 
+    def release(self):
+        """Drops the references to the caches (the device buffer stays for the next
+        rebind), so a kept batch does not hold finished requests' pools."""
+        self.caches = []
+
     def rebind(self, caches):
         """Points the batch at another set of caches of the same count and geometry
         (a captured graph reads only the device buffer, so it serves them too)."""
@@ -420,6 +425,8 @@ class RequestBatch:
         """Claims the next n-token frame of every cache at its selected precision on
         all layers and writes the step's descriptors to the device (ordered on the
         current stream before whatever is launched next). Returns the pasts."""
+        if len(self.caches) != self.count:
+            raise ValueError('request batch has no caches bound (rebind before stepping)')
         if self._copied is not None:
             self._copied.synchronize()  # the previous step's copy has left the pinned buffer
         pasts = []

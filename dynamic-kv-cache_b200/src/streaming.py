@@ -137,6 +137,8 @@ class StreamingModel:
                 stepper.step(embeds=torch.cat(step, dim=0))
             else:
                 self.model.forward_many(caches, embeds=torch.cat(step, dim=0))
+        if stepper is not None:
+            stepper.batch.release()  # the graph is kept for the next batch, the caches are not
         for cache in caches:
             cache.select(16, -1)
             cache.reserve(16, cache.host_counts[16] + qa_reserve)

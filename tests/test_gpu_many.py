@@ -288,6 +288,10 @@ def test_frame_graph_is_reused_for_the_next_batch(cuda):
     graph = model._frame_graphs[(2, 64)].graph
     graphed = model.ingest_many([r[0] for r in sets[1]], bits[1], 'dynamic', qa_reserve=64, graph=True)
     assert model._frame_graphs[(2, 64)].graph is graph  # captured once
+    assert model._frame_graphs[(2, 64)].batch.caches == []  # finished caches are not kept alive
+    with pytest.raises(ValueError, match='no caches bound'):
+        model._frame_graphs[(2, 64)].step(embeds=torch.zeros(2, 64, TINY.hidden, dtype=torch.bfloat16,
+                                                                device='cuda'))
     eager = model.ingest_many([r[0] for r in sets[1]], bits[1], 'dynamic', qa_reserve=64)
     got = model.answer_many([r[1] for r in sets[1]], [r[2] for r in sets[1]], graphed)
     want = model.answer_many([r[1] for r in sets[1]], [r[2] for r in sets[1]], eager)

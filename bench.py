@@ -47,7 +47,7 @@ ROW_BYTES = {4: 32 + 8, 8: 64 + 8, 16: 128}  # code bytes + (offset, scale) per 
 METRIC = 'packed-KV attention HBM GB/s at 8K ctx'
 # DRAM bytes (read + write) of attention_tc_kernel for one call of this shape,
 # from the ncu capture summarised in profiles/attention_tc_kernel_c3_8k.md.
-NCU_TRAFFIC_BYTES = 5_800_448  # dram__bytes_read.sum + write of one attention_tc_kernel launch (profiles/attention_tc_kernel_c3_8k.md)
+NCU_TRAFFIC_BYTES = 5_805_824  # dram__bytes_read.sum + write of one attention_tc_kernel launch (profiles/attention_tc_kernel_c3_8k.md)
 WORKLOAD = 'C3 frame-append attention, 8K ctx, 32-layer cache'
 
 

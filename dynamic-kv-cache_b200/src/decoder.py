@@ -66,7 +66,8 @@ def rope_tables(cfg, positions, device):
 
 
 def apply_rope(x, cos, sin):
-    """HF Llama rotate-half rotary embedding on [1, heads, n, d] (computed in fp32)."""
+    """HF Llama rotate-half rotary embedding over the last dimension (computed in
+    fp32; cos / sin broadcast against x)."""
     half = x.shape[-1] // 2
     xf = x.float()
     rot = torch.cat((-xf[..., half:], xf[..., :half]), dim=-1)
@@ -97,15 +98,29 @@ class Decoder(torch.nn.Module):
     def rms(self, x, weight):
         return cuda_rms(x, weight, self.cfg.rms_eps)
 
+    def project_qkv(self, x, layer, cos, sin):
+        """q [B, q_heads, n, d] and k / v [B, kv_heads, n, d] of x [B, n, hidden]: one
+        joined projection and one rotary pass over the query and key heads together
+        (cos / sin [B or 1, n, 1, d]); q, k and v are strided views, which the cache
+        kernels take as they are."""
+        c = self.cfg
+        b, n = x.shape[0], x.shape[1]
+        h = F.linear(x, self.qkv[layer]).view(b, n, c.q_heads + 2 * c.kv_heads, c.head_dim)
+        qk = apply_rope(h[:, :, :c.q_heads + c.kv_heads], cos, sin)
+        q = qk[:, :, :c.q_heads].transpose(1, 2)
+        k = qk[:, :, c.q_heads:].transpose(1, 2)
+        v = h[:, :, c.q_heads + c.kv_heads:].transpose(1, 2)
+        return q, k, v
+
+    def rotary(self, positions, b, n, device):
+        """cos / sin [b, n, 1, d] of positions [b * n] (or [n] for b = 1)."""
+        cos, sin = rope_tables(self.cfg, positions.reshape(-1), device)
+        return cos.view(b, n, 1, -1), sin.view(b, n, 1, -1)
+
     def attention(self, x, layer, cache, cos, sin):
         c = self.cfg
         n = x.shape[1]
-        q, k, v = F.linear(x, self.qkv[layer]).split(
-            [c.q_heads * c.head_dim, c.kv_heads * c.head_dim, c.kv_heads * c.head_dim], dim=-1)
-        q = q.view(1, n, c.q_heads, c.head_dim).transpose(1, 2)
-        k = k.view(1, n, c.kv_heads, c.head_dim).transpose(1, 2)
-        v = v.view(1, n, c.kv_heads, c.head_dim).transpose(1, 2)
-        q, k = apply_rope(q, cos, sin), apply_rope(k, cos, sin)
+        q, k, v = self.project_qkv(x, layer, cos, sin)
         if isinstance(cache, GPUCache):
             out = cache.append_attend(q, k, v, layer)  # append + attend in one call; [1, n, q_heads, d]
         else:
@@ -121,12 +136,7 @@ class Decoder(torch.nn.Module):
         appended (the packed path runs one batched kernel call per layer)."""
         c = self.cfg
         b, n = x.shape[0], x.shape[1]
-        q, k, v = F.linear(x, self.qkv[layer]).split(
-            [c.q_heads * c.head_dim, c.kv_heads * c.head_dim, c.kv_heads * c.head_dim], dim=-1)
-        q = q.view(b, n, c.q_heads, c.head_dim).transpose(1, 2)
-        k = k.view(b, n, c.kv_heads, c.head_dim).transpose(1, 2)
-        v = v.view(b, n, c.kv_heads, c.head_dim).transpose(1, 2)
-        q, k = apply_rope(q, cos, sin), apply_rope(k, cos, sin)
+        q, k, v = self.project_qkv(x, layer, cos, sin)
         past = cache.get_seq_length(layer)
         if isinstance(cache, GPUCache):
             out = cache.attend_batched(q, k, v, layer, past)  # [B, n, q_heads, d]
@@ -142,14 +152,8 @@ class Decoder(torch.nn.Module):
         """Attention of B requests' frames x [B, n, hidden], request r over caches[r],
         appending each frame's K/V to its own cache (one pack and one attention
         launch for all of them)."""
-        c = self.cfg
         b, n = x.shape[0], x.shape[1]
-        q, k, v = F.linear(x, self.qkv[layer]).split(
-            [c.q_heads * c.head_dim, c.kv_heads * c.head_dim, c.kv_heads * c.head_dim], dim=-1)
-        q = q.view(b, n, c.q_heads, c.head_dim).transpose(1, 2)
-        k = k.view(b, n, c.kv_heads, c.head_dim).transpose(1, 2)
-        v = v.view(b, n, c.kv_heads, c.head_dim).transpose(1, 2)
-        q, k = apply_rope(q, cos, sin), apply_rope(k, cos, sin)
+        q, k, v = self.project_qkv(x, layer, cos, sin)
         pasts = append_many(caches, k, v, layer)
         out = attend_many(caches, q, k, v, layer, pasts)  # [B, n, q_heads, d]
         return F.linear(out.reshape(b, n, -1), self.o[layer])
@@ -165,8 +169,7 @@ class Decoder(torch.nn.Module):
             raise ValueError('one cache per request')
         pasts = torch.tensor([c.get_seq_length(0) for c in caches], device=x.device)
         positions = pasts[:, None] + torch.arange(n, device=x.device)[None, :]  # [B, n]
-        cos, sin = rope_tables(self.cfg, positions.reshape(-1), x.device)
-        cos, sin = cos.view(b, 1, n, -1), sin.view(b, 1, n, -1)
+        cos, sin = self.rotary(positions, b, n, x.device)
         for layer in range(self.cfg.layers):
             x = x + self.attention_many(self.rms(x, self.norm_attn[layer]), layer, caches, cos, sin)
             h = self.rms(x, self.norm_mlp[layer])
@@ -184,16 +187,9 @@ class Decoder(torch.nn.Module):
         can be captured once as a CUDA graph and replayed (FrameGraph)."""
         c = self.cfg
         b, n = x.shape[0], x.shape[1]
-        cos, sin = rope_tables(c, batch.positions.reshape(-1), x.device)
-        cos, sin = cos.view(b, 1, n, -1), sin.view(b, 1, n, -1)
+        cos, sin = self.rotary(batch.positions, b, n, x.device)
         for layer in range(c.layers):
-            h = self.rms(x, self.norm_attn[layer])
-            q, k, v = F.linear(h, self.qkv[layer]).split(
-                [c.q_heads * c.head_dim, c.kv_heads * c.head_dim, c.kv_heads * c.head_dim], dim=-1)
-            q = q.view(b, n, c.q_heads, c.head_dim).transpose(1, 2)
-            k = k.view(b, n, c.kv_heads, c.head_dim).transpose(1, 2)
-            v = v.view(b, n, c.kv_heads, c.head_dim).transpose(1, 2)
-            q, k = apply_rope(q, cos, sin), apply_rope(k, cos, sin)
+            q, k, v = self.project_qkv(self.rms(x, self.norm_attn[layer]), layer, cos, sin)
             out = torch.empty((b, n, c.q_heads, c.head_dim), dtype=x.dtype, device=x.device)
             K.append_attention_many_device(q, k, v, batch.targets_ptr, batch.histories_ptr, b, batch.max_past, out,
                                            layer, n, c.kv_heads, c.q_heads // c.kv_heads, c.head_dim, c.layers)
@@ -213,7 +209,7 @@ class Decoder(torch.nn.Module):
         x = self.embed[ids]
         n = x.shape[1]
         past = cache.get_seq_length(0)
-        cos, sin = rope_tables(self.cfg, torch.arange(past, past + n, device=x.device), x.device)
+        cos, sin = self.rotary(torch.arange(past, past + n, device=x.device), 1, n, x.device)
         for layer in range(self.cfg.layers):
             x = x + self.attention_chunks(self.rms(x, self.norm_attn[layer]), layer, cache, cos, sin)
             h = self.rms(x, self.norm_mlp[layer])
@@ -229,7 +225,7 @@ class Decoder(torch.nn.Module):
         x = self.embed[ids] if embeds is None else embeds
         n = x.shape[1]
         past = cache.get_seq_length(0)
-        cos, sin = rope_tables(self.cfg, torch.arange(past, past + n, device=x.device), x.device)
+        cos, sin = self.rotary(torch.arange(past, past + n, device=x.device), 1, n, x.device)
         for layer in range(self.cfg.layers):
             x = x + self.attention(self.rms(x, self.norm_attn[layer]), layer, cache, cos, sin)
             h = self.rms(x, self.norm_mlp[layer])

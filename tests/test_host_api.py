@@ -91,3 +91,44 @@ def test_accounting_matches_reference_audit_formulas():
 def test_non_bf16_pool_dtype_is_rejected():
     with pytest.raises(ValueError, match='bfloat16'):
         GPUCache(device='cpu', dtype=torch.float16)
+
+
+def _layer_by_layer(c, n):
+    rows = [c._claim(layer, n, fill_map=False)[2] for layer in range(c.layers)]
+    past = c.seen[0]
+    c.seen = [past + n] * c.layers
+    return past, rows
+
+
+def test_claim_frame_equals_the_claims_of_every_layer_offline():
+    plan = [(4, 64), (16, 64), (8, 30), (8, 34), (4, 64)]
+    a = GPUCache(plan, layers=3, device='cpu')
+    b = GPUCache(plan, layers=3, device='cpu')
+    for bits, n in [(4, 64), (16, 64), (8, 30), (8, 34), (4, 64)]:
+        a.select(bits), b.select(bits)
+        past, row = a._claim_frame(n)
+        past_b, rows = _layer_by_layer(b, n)
+        assert past == past_b and rows == [row] * 3
+        assert a.seen == b.seen and a.cursors == b.cursors
+    with pytest.raises(ValueError, match='context limit'):
+        a._claim_frame(1)
+
+
+def test_claim_frame_online_grows_and_records_the_segment_once():
+    a = GPUCache(None, layers=4, device='cpu', max_tokens=512)
+    for i, bits in enumerate([4, 8, 4, 16, 4]):
+        a.select(bits, i)
+        past, row = a._claim_frame(64)
+        assert past == 64 * i and a.seen == [64 * (i + 1)] * 4
+        assert a.plan[-1] == (past, past + 64, bits, row)
+    assert a.host_counts == {4: 192, 8: 64, 16: 64}
+    assert a.caps[4] >= 192 and a.p4.shape[3] == a.caps[4]
+    with pytest.raises(ValueError, match='Cache append does not match plan|context limit'):
+        a._claim_frame(512)
+
+
+def test_claim_frame_rejects_layers_out_of_step():
+    a = GPUCache(None, layers=2, device='cpu', max_tokens=512)
+    a.seen = [64, 0]
+    with pytest.raises(ValueError, match='disagree'):
+        a._claim_frame(64)

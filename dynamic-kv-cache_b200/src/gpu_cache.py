@@ -99,6 +99,22 @@ class GPUCache(DynamicCache):
     def __len__(self):
         return self.layers
 
+    # transformers 5.x asks every cache for these (the reference targets 4.51, whose
+    # DynamicCache had no per-layer objects); here every layer is full attention
+    @property
+    def is_sliding(self):
+        return [False] * self.layers
+
+    @property
+    def is_compileable(self):
+        return False
+
+    def get_mask_sizes(self, query, layer_idx=0):
+        """(kv_length, kv_offset) of the causal mask for `query` new tokens (a count
+        or their cache positions)."""
+        q = query if isinstance(query, int) else query.shape[0]
+        return q + self.seen[layer_idx], 0
+
     # -- hot path -----------------------------------------------------------------
     def _pools(self):
         return (self.p4, self.m4, self.p8, self.m8, self.p16)
@@ -282,9 +298,8 @@ def install_packed_attention(model):
         k = k.view(*shape, -1, module.head_dim).transpose(1, 2)
         v = v.view(*shape, -1, module.head_dim).transpose(1, 2)
         q, k = apply_rotary_pos_emb(q, k, *position_embeddings)
-        if fused:
-            past = cache.append(k, v, module.layer_idx)
-            output = cache.attend(q, k, v, module.layer_idx, past)
+        if fused:  # the reference's append + attend (:172-173), here one call and one launch
+            output = cache.append_attend(q, k, v, module.layer_idx)
         else:
             k, v = cache.update(k, v, module.layer_idx, {'cache_position': cache_position})
             mask = None if attention_mask is None else attention_mask[:, :, :, :k.shape[-2]]

@@ -132,3 +132,23 @@ def test_claim_frame_rejects_layers_out_of_step():
     a.seen = [64, 0]
     with pytest.raises(ValueError, match='disagree'):
         a._claim_frame(64)
+
+
+def _tiny_llama():
+    from transformers import LlamaConfig, LlamaForCausalLM
+    cfg = LlamaConfig(hidden_size=384, num_attention_heads=6, num_key_value_heads=2, intermediate_size=512,
+                      vocab_size=1000, num_hidden_layers=2, head_dim=64)
+    torch.manual_seed(0)
+    return LlamaForCausalLM(cfg).to(torch.bfloat16)
+
+
+def test_hf_llama_forward_reaches_the_packed_attention():
+    """install_packed_attention on the installed transformers: the model's mask
+    and cache bookkeeping accept a GPUCache up to the kernel call (which needs CUDA)."""
+    from src.gpu_cache import install_packed_attention
+    model = _tiny_llama()
+    install_packed_attention(model)
+    cache = GPUCache(None, layers=2, heads=2, device='cpu')
+    with pytest.raises(ValueError, match='requires CUDA'):
+        model(torch.randint(0, 1000, (1, 64)), past_key_values=cache, use_cache=True)
+    assert cache.get_mask_sizes(64, 0) == (64, 0) and cache.is_sliding == [False, False]

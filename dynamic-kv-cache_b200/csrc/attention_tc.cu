@@ -224,6 +224,45 @@ __device__ __forceinline__ void convert_uniform(const uint8_t* st, uint8_t* dstK
   }
 }
 
+// Few rows per CTA (one (row, dim) per thread, as with many splits): each thread
+// loads its column of every split's partial straight into registers before the
+// weights are computed, so the partials' and the (max, sum) pairs' trips to L2
+// overlap; same arithmetic in the same order as merge_rows.
+constexpr int kMergeRegs = 32;
+__device__ __forceinline__ void merge_rows_direct(const AttnArgs& a, int g, int grp, int row0, int r_begin, int nr,
+                                                  uint16_t* out, uint8_t* smem, int tid) {
+  const int S = a.splits;
+  float* s_w = reinterpret_cast<float*>(smem + kOffQ) + 2 * (kMergePairs + kTcCtaRows);  // [nr][S]
+  float* s_den = s_w + kMergePairs;                                                       // [nr]
+  const int warp = tid >> 5, lane = tid & 31;
+  const bool mine = tid < nr * kDim;
+  const int r = tid >> 6, d = tid & (kDim - 1);
+  float ov[kMergeRegs];
+  if (mine) {  // partials published by the other splits: plain loads after the acquire
+    const float* col = a.ws_o + part_o(grp, r_begin + r, kTcCtaRows, S, 0) + d;
+#pragma unroll
+    for (int u = 0; u < kMergeRegs; ++u) ov[u] = u < S ? col[u * kDim] : 0.f;
+  }
+  for (int rr = warp; rr < nr; rr += kThreadsTc / 32) {
+    const float2* ml = a.ws_ml + part_ml(grp, r_begin + rr, kTcCtaRows, S, 0);
+    const float den = merge_row_weights([&](int sp) { return ml[sp]; }, S, s_w + rr * S, lane);
+    if (lane == 0) s_den[rr] = den;
+  }
+  __syncthreads();
+  if (mine) {
+    const float* w = s_w + r * S;
+    float acc = 0.f;
+#pragma unroll
+    for (int u = 0; u < kMergeRegs; ++u)
+      if (u < S) acc = __fmaf_rn(w[u], ov[u], acc);
+    const float val = __fdiv_rn(acc, s_den[r]);
+    const int frow = row0 + r_begin + r;
+    const int m = frow / a.G;
+    const int h = g * a.G + (frow - m * a.G);
+    out[(static_cast<int64_t>(m) * a.HQ + h) * kDim + d] = static_cast<uint16_t>(pack_bf16x2(val, 0.f) & 0xffffu);
+  }
+}
+
 // Rows [r_begin, r_end) of group grp (rows counted from row0), merged from all
 // splits' partials and written to `out` (merge_row_weights, then the fused
 // multiply-add chain in split order: bit-identical to the combine kernel). The
@@ -235,6 +274,10 @@ __device__ __forceinline__ void merge_rows(const AttnArgs& a, int g, int grp, in
                                            uint16_t* out, uint8_t* smem, int tid, int32_t* status) {
   const int nr = r_end - r_begin;
   if (nr <= 0) return;
+  if (nr * kDim <= kThreadsTc && a.splits <= kMergeRegs) {
+    merge_rows_direct(a, g, grp, row0, r_begin, nr, out, smem, tid);
+    return;
+  }
   const uint32_t sbase = smem_addr(smem);
   const uint32_t mbar = sbase + kOffBar + 8 * B_MERGE;
   const int S = a.splits, Se = even_splits(S);

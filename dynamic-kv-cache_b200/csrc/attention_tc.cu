@@ -369,30 +369,22 @@ attention_tc_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ 
   auto bar = [&](int i) { return sbase + kOffBar + 8 * i; };
 
   // ---- set-up: barriers and TMEM, then every role starts at once ----
-  if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(bar(B_FULL + s), kConvThreads);
-      mbar_init(bar(B_EMPTY + s), 1);
-    }
-    for (int s = 0; s < kRawStages; ++s) {
-      mbar_init(bar(B_RAWFULL + s), 1);
-      mbar_init(bar(B_RAWEMPTY + s), kConvThreads);
-    }
-    for (int s = 0; s < kMapStages; ++s) mbar_init(bar(B_MAPFULL + s), 1);
+  if (warp == 0) {  // each lane initialises a share of the barriers
     const int tile_threads[2] = {min(soft_threads, 128), max(soft_threads - 128, 32)};  // (unused tile: any count)
-    for (int mt = 0; mt < 2; ++mt) {
-      for (int b = 0; b < 2; ++b) {
-        mbar_init(bar(B_SFULL + b * 2 + mt), 1);
-        mbar_init(bar(B_SFREE + b * 2 + mt), tile_threads[mt]);
+    for (int idx = lane; idx < B_COUNT; idx += 32) {
+      uint32_t cnt = 1;  // single-arrival barriers: MMA commits, TMA completions, loader arrivals
+      if ((idx >= B_FULL && idx < B_FULL + kStages) || (idx >= B_RAWEMPTY && idx < B_RAWEMPTY + kRawStages)) {
+        cnt = kConvThreads;
+      } else if (idx >= B_SFREE && idx < B_SFREE + 4) {
+        cnt = tile_threads[(idx - B_SFREE) & 1];
+      } else if (idx >= B_PFULL && idx < B_PFULL + 2) {
+        cnt = tile_threads[idx - B_PFULL];
+      } else if (idx == B_QREADY) {
+        cnt = kSoftmaxWarps * 32;
       }
-      mbar_init(bar(B_PFULL + mt), tile_threads[mt]);
-      mbar_init(bar(B_ODONE + mt), 1);
+      mbar_init(bar(idx), cnt);
     }
-    mbar_init(bar(B_QREADY), kSoftmaxWarps * 32);
-    mbar_init(bar(B_FINS), 1);
-    mbar_init(bar(B_FINPV), 1);
-    mbar_init(bar(B_MERGE), 1);
-    *abort_flag = 0;
+    if (lane == 0) *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
   if (warp == kSWarp) {

@@ -47,7 +47,7 @@ ROW_BYTES = {4: 32 + 8, 8: 64 + 8, 16: 128}  # code bytes + (offset, scale) per 
 METRIC = 'packed-KV attention HBM GB/s at 8K ctx'
 # DRAM bytes (read + write) of attention_tc_kernel for one call of this shape,
 # from the ncu capture summarised in profiles/attention_tc_kernel_c3_8k.md.
-NCU_TRAFFIC_BYTES = 5_805_824  # dram__bytes_read.sum + write of one attention_tc_kernel launch (profiles/attention_tc_kernel_c3_8k.md)
+NCU_TRAFFIC_BYTES = 5_805_056  # dram__bytes_read.sum + write of one attention_tc_kernel launch (profiles/attention_tc_kernel_c3_8k.md)
 WORKLOAD = 'C3 frame-append attention, 8K ctx, 32-layer cache'
 
 
@@ -272,6 +272,34 @@ def bench_c2(device):
         launches = (8192 // FRAME) * LAYERS
         out[str(bits)] = {'GB_per_s': launches * pack_bytes(bits) / (ms * 1e-3) / 1e9,
                           'us_per_layer_append': 1e3 * ms / launches, 'final_cap': cache.caps[bits]}
+        cache.check()
+        # the same 32 per-layer pack launches of one frame replayed from a CUDA graph
+        # (rows 0..63 rewritten each time): the kernel without the eager Python calls
+        from src import gpu_kernels as K
+        stream = torch.cuda.Stream(device)
+
+        def frame():
+            for layer in range(LAYERS):
+                K.pack_rows(k[layer], v[layer], *cache._pools(), layer, 0, FRAME, cache.caps[4], cache.caps[8],
+                            cache.caps[16], HEADS, DIM, bits, LAYERS, cache.status)
+
+        stream.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(stream):
+            frame()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                frame()
+            for _ in range(3):
+                graph.replay()
+            start.record(stream)
+            for _ in range(50):
+                graph.replay()
+            end.record(stream)
+        torch.cuda.synchronize(device)
+        gms = start.elapsed_time(end) / 50
+        out[str(bits)].update({'GB_per_s_graph': LAYERS * pack_bytes(bits) / (gms * 1e-3) / 1e9,
+                               'us_per_layer_append_graph': 1e3 * gms / LAYERS})
+        del graph
         cache.check()
     return out
 

@@ -144,12 +144,13 @@ __device__ __forceinline__ const History& history_of(const AttnArgs&, const Devi
   return t.h[c];
 }
 
-// History length of a chunk, checked against its token map (descriptors in
-// device memory are not seen by the host): a bad one is reported and read as an
+// History length of a chunk, checked against its token map and pools (descriptors
+// in device memory are not seen by the host): a bad one is reported and read as an
 // empty history.
 __device__ __forceinline__ int checked_past(const History& H, int chunk) {
   const int past = H.past;
-  if (past < 0 || past > H.capacity || (past > 0 && (H.rows == nullptr || H.codes == nullptr))) {
+  const bool pools = H.p4 != nullptr && H.m4 != nullptr && H.p8 != nullptr && H.m8 != nullptr && H.p16 != nullptr;
+  if (past < 0 || past > H.capacity || (past > 0 && (H.rows == nullptr || H.codes == nullptr || !pools))) {
     report(H.status, DKV_EINVAL, chunk);
     return 0;
   }

@@ -212,6 +212,11 @@ def test_device_descriptor_errors_are_reported_not_used(cuda):
     K.packed_attention_many_device(q, kv, kv, dev_h.data_ptr(), 1, 256, out, 0, 64, 5, 3, 64, 1)
     with pytest.raises(ValueError, match='invalid argument'):
         c.check()
+    h[0].past, h[0].p8 = 256, None  # a null pool in a device descriptor: reported, the history not read
+    dev_h = torch.frombuffer(bytearray(bytes(h)), dtype=torch.uint8).cuda()
+    K.packed_attention_many_device(q, kv, kv, dev_h.data_ptr(), 1, 256, out, 0, 64, 5, 3, 64, 1)
+    with pytest.raises(ValueError, match='invalid argument'):
+        c.check()
     from src.gpu_cache import _pack_target
     t = (K.PackTarget * 1)(_pack_target(c, 256, c.caps[16] - 10, False))
     t[0].bits = 16

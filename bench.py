@@ -16,7 +16,7 @@ Printed (rank 0, one JSON line):
              (device-resident inputs; the 32-layer sweep replayed as a CUDA graph)
   e2e        same metric through the public API (GPUCache.attend) with pinned host
              buffers: per layer H2D of q/k/v and D2H of the output inside the timing
-  frame_append_tokens_per_s  pack + attend of a 64-token frame on all 32 layers
+  frame_append_tokens_per_s  pack + attend of a 64-token frame on all 32 layers (one fused launch each)
   roofline   dominant op (attention) vs measured HBM peak; roofline_tensor vs bf16
   cpu_baseline  the reference CPU path (dequantise + torch SDPA, oracle port) on a
              bounded sample of the same workload, all host cores
@@ -467,7 +467,7 @@ def main():
     value = world * LAYERS * bytes_call * args.steps / (ms_total * 1e-3) / 1e9
     us_call = 1e3 * ms_step / LAYERS
 
-    # ---- frame append (pack + attend on a fork, 32 layers), captured and replayed ----
+    # ---- frame append (fused pack + attend on a fork, 32 layers), captured and replayed ----
     branch = cache.fork()
     branch.select(16)
     fa_outs = [None] * LAYERS
@@ -475,9 +475,8 @@ def main():
     def frame_sweep():
         b = branch.fork()
         b.select(16)
-        for layer in range(LAYERS):
-            p = b.append(kn[layer], vn[layer], layer)
-            fa_outs[layer] = b.attend(q[layer], kn[layer], vn[layer], layer, p)
+        for layer in range(LAYERS):  # append + attend of the frame: one fused launch per layer
+            fa_outs[layer] = b.append_attend(q[layer], kn[layer], vn[layer], layer)
 
     with torch.cuda.stream(stream):
         for _ in range(2):

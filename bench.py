@@ -304,6 +304,67 @@ def bench_c2(device):
     return out
 
 
+def cpu_config_baselines(model, seconds=2.0):
+    """CPU baselines of C2, C4 and C5 (rank 0, all host threads): the oracle port of
+    the reference CPU path on bounded samples, extrapolated as stated in each entry."""
+    import dataclasses
+    import numpy as np
+    from oracle import kvq
+    from oracle.decoder import OracleDecoder, decoder_params
+    torch.set_num_threads(os.cpu_count())
+    gen = torch.Generator().manual_seed(5)
+    to_bits = lambda t: t.bfloat16().contiguous().view(torch.int16).numpy().view(np.uint16)
+    out = {'cores': os.cpu_count(), 'kind': 'port'}
+    # C2: the reference quantiser on one (layer, 64-token append): K and V of 5 heads
+    k, v = to_bits(torch.randn(1, HEADS, FRAME, DIM, generator=gen)), to_bits(torch.randn(1, HEADS, FRAME, DIM, generator=gen))
+    c2 = {}
+    for bits in (4, 8, 16):
+        kvq.pack(k, bits)
+        calls, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds / 3:
+            kvq.pack(k, bits), kvq.pack(v, bits)
+            calls += 1
+        dt = (time.perf_counter() - t0) / calls
+        c2[str(bits)] = {'GB_per_s': pack_bytes(bits) / dt / 1e9, 'us_per_layer_append': 1e6 * dt}
+    out['c2'] = dict(c2, sample='kv_quantization.pack port (numpy) on the K and V of one (layer, 64-token append)')
+    # C4 / C5: the decoder restatement on 2 of the 32 layers over a synthetic packed history
+    cfg = dataclasses.replace(model.cfg, layers=2)
+    params = {n: t for n, t in decoder_params(model.model).items()
+              if not (n.split('.')[-1].isdigit() and int(n.split('.')[-1]) >= 2)}
+    oracle = OracleDecoder(cfg, params)
+    rnd = random.Random(5)
+
+    def history(frames):
+        hist = [[] for _ in range(cfg.layers)]
+        for _ in range(frames):
+            b = rnd.choices(MIX[0], weights=MIX[1])[0]
+            for layer in range(cfg.layers):
+                hist[layer].append((kvq.pack(to_bits(torch.randn(1, HEADS, FRAME, DIM, generator=gen)), b),
+                                    kvq.pack(to_bits(torch.randn(1, HEADS, FRAME, DIM, generator=gen)), b)))
+        return hist
+
+    def timed(hist, n, past, logits):
+        x = oracle.p['embed'][torch.randint(0, cfg.vocab, (n,), generator=gen)][None]
+        oracle.forward(hist, x, past, logits=logits)
+        reps, t0 = 0, time.perf_counter()
+        while reps < 1 or time.perf_counter() - t0 < seconds / 3:
+            oracle.forward(hist, x, past, logits=logits)
+            reps += 1
+        return (time.perf_counter() - t0) / reps * model.cfg.layers / cfg.layers
+
+    scaled = f'{cfg.layers} of {model.cfg.layers} layers timed and scaled by {model.cfg.layers / cfg.layers:g}'
+    cand = timed(history(96), 56, 96 * FRAME, 25)
+    out['c4'] = {'ms_per_4_candidates': 4e3 * cand,
+                 'sample': f'one 56-token question + candidate forward over a 6144-token packed history, {scaled}; '
+                           'x4 candidates (the reference protocol)'}
+    frame = timed(history(32), FRAME, 32 * FRAME, 0)
+    out['c5'] = {'frame_append_tokens_per_s': FRAME / frame,
+                 'sample': 'one 64-token frame forward over a 2048-token packed history (the mean history of '
+                           f'a 64-frame request), {scaled}; one request on all host cores, the same rate for the '
+                           '64-request set'}
+    return out
+
+
 def bench_c4(device):
     """C4: candidate scoring over a 96-frame (6144-token) mixed 4/8/16 packed prefix with the
     random-init SmolLM2-360M-shape decoder: 32-token question, 4 x 24-token candidates."""
@@ -581,6 +642,15 @@ def main():
                                                  args.c5_sequential)
     if rank == 0 and 'c1' in configs:
         line['c1_cpu_reference_path'] = bench_c1()
+    if rank == 0 and model is not None and not args.no_cpu_baseline:
+        cpu = cpu_config_baselines(model)
+        meta = {'cores': cpu['cores'], 'kind': cpu['kind']}
+        if 'c2' in configs:
+            line['c2_pack_sweep']['cpu_baseline'] = dict(cpu['c2'], **meta)
+        if 'c4' in configs:
+            line['c4_candidate_scoring']['cpu_baseline'] = dict(cpu['c4'], **meta)
+        if 'c5' in configs:
+            line['c5_request_throughput']['cpu_baseline'] = dict(cpu['c5'], **meta)
     if rank == 0 and not args.no_cpu_baseline:
         line['cpu_baseline'] = cpu_baseline(args.cpu_seconds)
     if rank == 0:

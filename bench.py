@@ -60,7 +60,7 @@ def parse():
     ap.add_argument('--cpu-seconds', type=float, default=12.0, help='CPU-baseline sample budget')
     ap.add_argument('--e2e-steps', type=int, default=30)
     ap.add_argument('--no-cpu-baseline', action='store_true')
-    ap.add_argument('--configs', default='c1,c2,c4,c5',
+    ap.add_argument('--configs', default='c1,c2,c3,c4,c5',
                     help='extra BASELINE configurations reported in the same line (comma list, or "none")')
     ap.add_argument('--c5-requests', type=int, default=64, help='C5 requests in total, split across ranks')
     ap.add_argument('--c5-batch', type=int, default=8,
@@ -76,10 +76,11 @@ def parse():
     return args
 
 
-def frame_plan(seed):
-    frames = (PAST + FRAME - 1) // FRAME
+def frame_plan(seed, past=None):
+    past = PAST if past is None else past
+    frames = (past + FRAME - 1) // FRAME
     bits = random.Random(seed).choices(MIX[0], weights=MIX[1], k=frames)
-    sizes = [FRAME] * (frames - 1) + [PAST - FRAME * (frames - 1)]
+    sizes = [FRAME] * (frames - 1) + [past - FRAME * (frames - 1)]
     return list(zip(bits, sizes))
 
 
@@ -88,7 +89,7 @@ def attention_bytes(plan):
     metadata), the 5-byte token map entry per history token, Q and the output
     once, the native new K/V once."""
     hist = sum(2 * HEADS * n * ROW_BYTES[b] for b, n in plan)
-    maps = 5 * PAST
+    maps = 5 * sum(n for _, n in plan)
     q_out = 2 * NQ * HEADS * GROUP * DIM * 2
     new_kv = 2 * NQ * HEADS * DIM * 2
     return hist + maps + q_out + new_kv
@@ -140,26 +141,27 @@ class ClockSampler:
                 'reasons': sorted(reasons), 'samples': len(sm)}
 
 
-def build_cache(seed, device):
+def build_cache(seed, device, past=None, layers=None):
     from src.gpu_cache import GPUCache
+    layers = LAYERS if layers is None else layers
     gen = torch.Generator(device=device).manual_seed(seed)
     outliers = torch.randperm(DIM, generator=torch.Generator().manual_seed(seed))[:4].to(device)
-    plan = frame_plan(seed)
-    cache = GPUCache(None, layers=LAYERS, heads=HEADS, device=device)
+    plan = frame_plan(seed, past)
+    cache = GPUCache(None, layers=layers, heads=HEADS, device=device)
     for f, (bits, n) in enumerate(plan):
         cache.select(bits, f)
-        for layer in range(LAYERS):
+        for layer in range(layers):
             k = torch.randn(1, HEADS, n, DIM, generator=gen, device=device)
             k[..., outliers] *= 8
             v = torch.randn(1, HEADS, n, DIM, generator=gen, device=device)
             cache.append(k.bfloat16(), v.bfloat16(), layer)
     for b in (4, 8, 16):  # room for the timed frame appends without growth
         cache.reserve(b, cache.host_counts[b] + FRAME)
-    q = torch.randn(LAYERS, 1, HEADS * GROUP, NQ, DIM, generator=gen, device=device).bfloat16()
-    kn = torch.randn(LAYERS, 1, HEADS, NQ, DIM, generator=gen, device=device)
+    q = torch.randn(layers, 1, HEADS * GROUP, NQ, DIM, generator=gen, device=device).bfloat16()
+    kn = torch.randn(layers, 1, HEADS, NQ, DIM, generator=gen, device=device)
     kn[..., outliers] *= 8
     kn = kn.bfloat16()
-    vn = torch.randn(LAYERS, 1, HEADS, NQ, DIM, generator=gen, device=device).bfloat16()
+    vn = torch.randn(layers, 1, HEADS, NQ, DIM, generator=gen, device=device).bfloat16()
     cache.check()
     return cache, plan, q, kn, vn
 
@@ -247,6 +249,43 @@ def bench_c1(seconds=2.0):
         calls += 1
     return {'ms_per_call': 1e3 * (time.perf_counter() - t0) / calls, 'cores': os.cpu_count(), 'past': 1024,
             'what': 'reference CPU path (unpack + cat + SDPA), one layer, 64-token append'}
+
+
+def bench_c3_sweep(device, cases=((1024, 256), (4096, 64))):
+    """C3 at the shorter histories of the configuration (past 1024 and 4096; 8128 is the
+    headline): as many layers as keep the packed history above L2 (~180 MB), every
+    layer's call replayed from one CUDA graph."""
+    out = {}
+    for past, layers in cases:
+        cache, plan, q, kn, vn = build_cache(1100 + past, device, past=past, layers=layers)
+        outs = [None] * layers
+        stream = torch.cuda.Stream(device)
+
+        def sweep():
+            for layer in range(layers):
+                outs[layer] = cache.attend(q[layer], kn[layer], vn[layer], layer, past)
+
+        stream.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(stream):
+            sweep()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                sweep()
+            for _ in range(3):
+                graph.replay()
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record(stream)
+            for _ in range(20):
+                graph.replay()
+            end.record(stream)
+        torch.cuda.synchronize(device)
+        cache.check()
+        us = 1e3 * start.elapsed_time(end) / 20 / layers
+        nbytes = attention_bytes(plan)
+        out[str(past)] = {'us_per_layer_call': us, 'GB_per_s': nbytes / (us * 1e-6) / 1e9, 'layers': layers,
+                          'bytes_per_call': nbytes, 'working_set_MB': layers * nbytes // 2**20}
+        del graph, cache, q, kn, vn, outs
+    return out
 
 
 def bench_c2(device):
@@ -632,6 +671,8 @@ def main():
     configs = set() if args.configs == 'none' else set(args.configs.split(','))
     if 'c2' in configs:
         line['c2_pack_sweep'] = bench_c2(device)
+    if 'c3' in configs:
+        line['c3_past_sweep'] = bench_c3_sweep(device)
     model = None
     if 'c4' in configs or 'c5' in configs:
         c4, model = bench_c4(device)

@@ -334,6 +334,14 @@ def _pack_target(c, past, row, new_segment):
                         past, c.capacity, c.status.data_ptr())
 
 
+def _check_room(caches, layer, n):
+    """Every cache can take n more tokens on `layer` (checked for all before any is
+    claimed, so a batch that cannot proceed leaves every cache unchanged)."""
+    for c in caches:
+        if c.seen[layer] + n > c.capacity:
+            raise ValueError('GPU context limit exceeded')
+
+
 def _same_geometry(caches):
     if not caches:
         raise ValueError('no caches')
@@ -356,6 +364,7 @@ def append_many(caches, k, v, layer):
     if len({c.p16.data_ptr() for c in caches}) != b:
         # a cache listed twice, or forks of one cache (they write the same reserved rows)
         raise ValueError('batched appends need caches with their own pools')
+    _check_room(caches, layer, n)
     targets, claims = [], []
     for c in caches:
         past, n, row = c._claim(layer, n, fill_map=False)
@@ -442,6 +451,7 @@ class RequestBatch:
         current stream before whatever is launched next). Returns the pasts."""
         if len(self.caches) != self.count:
             raise ValueError('request batch has no caches bound (rebind before stepping)')
+        _check_room(self.caches, 0, self.n)
         if self._copied is not None:
             self._copied.synchronize()  # the previous step's copy has left the pinned buffer
         pasts = []

@@ -152,3 +152,16 @@ def test_hf_llama_forward_reaches_the_packed_attention():
     with pytest.raises(ValueError, match='requires CUDA'):
         model(torch.randint(0, 1000, (1, 64)), past_key_values=cache, use_cache=True)
     assert cache.get_mask_sizes(64, 0) == (64, 0) and cache.is_sliding == [False, False]
+
+
+def test_a_batch_over_the_context_limit_leaves_every_cache_unchanged():
+    from src.gpu_cache import _check_room
+    a = GPUCache(None, layers=2, device='cpu', max_tokens=256)
+    b = GPUCache(None, layers=2, device='cpu', max_tokens=128)
+    for c in (a, b):
+        c.select(4, 0)
+        c._claim_frame(64)
+    with pytest.raises(ValueError, match='context limit'):
+        _check_room([a, b], 0, 65)
+    assert a.seen == [64, 64] and b.seen == [64, 64] and len(a.plan) == len(b.plan) == 1
+    _check_room([a, b], 0, 64)

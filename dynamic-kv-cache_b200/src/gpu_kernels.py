@@ -14,6 +14,7 @@ reference's exception type) or RuntimeError (CUDA errors) on a non-zero status.
 There is no fallback: importing this module without the built library raises.
 """
 import ctypes
+import functools
 from pathlib import Path
 
 import torch
@@ -110,7 +111,14 @@ def _ptr(t):
     return None if t is None else t.data_ptr()
 
 
+_RAW_STREAM = getattr(torch._C, '_cuda_getCurrentRawStream', None)
+
+
 def _stream(t):
+    """Handle of the current CUDA stream of t's device (the raw query when torch has
+    it: a few hundred nanoseconds instead of a few microseconds per call)."""
+    if _RAW_STREAM is not None:
+        return _RAW_STREAM(t.device.index)
     return torch.cuda.current_stream(t.device).cuda_stream
 
 
@@ -131,7 +139,10 @@ def pack_rows(k, v, p4, m4, p8, m8, p16, layer, row_start, n, cap4, cap8, cap16,
                              cap4, cap8, cap16, heads, dim, bits, layers, _ptr(status), _stream(k)))
 
 
+@functools.lru_cache(maxsize=4096)
 def attention_workspace_bytes(past, nq, heads, group, dim=64):
+    """Workspace bytes of one packed_attention call of this shape (a pure function of
+    the shape: memoised, so the per-call path makes a single library call)."""
     return LIB.dkv_packed_attention_workspace(past, nq, heads, group, dim)
 
 
@@ -167,12 +178,13 @@ def packed_attention(q, knew, vnew, p4, m4, p8, m8, p16, rows, codes, out, layer
                      cap16, heads, group, dim, block_m, block_n, layers, status=None):
     q, knew, vnew = _rows_ready(q), _rows_ready(knew), _rows_ready(vnew)
     size = attention_workspace_bytes(past, nq, heads, group, dim)
-    workspace = _workspace(q.device, _stream(q), size) if size else None
+    stream = _stream(q)
+    workspace = _workspace(q.device, stream, size) if size else None
     _check(LIB.dkv_packed_attention(
         _ptr(q), _ptr(knew), _ptr(vnew), _ptr(p4), _ptr(m4), _ptr(p8), _ptr(m8), _ptr(p16), _ptr(rows),
         _ptr(codes), _ptr(out), q.stride(1), q.stride(2), knew.stride(1), knew.stride(2),
         vnew.stride(1), vnew.stride(2), layer, past, nq, cap4, cap8, cap16, heads, group, dim,
-        block_m, block_n, layers, _ptr(workspace), size, _ptr(status), _stream(q)))
+        block_m, block_n, layers, _ptr(workspace), size, _ptr(status), stream))
     return out
 
 
@@ -187,13 +199,14 @@ def packed_attention_batched(q, knew, vnew, p4, m4, p8, m8, p16, rows, codes, ou
         if x.shape[0] != chunks or x.stride(0) % 8:
             raise ValueError('batched attention operands need one leading chunk dimension of 16-byte steps')
     size = LIB.dkv_packed_attention_batched_workspace(past, nq, heads, group, dim, chunks)
-    workspace = _workspace(q.device, _stream(q), size) if size else None
+    stream = _stream(q)
+    workspace = _workspace(q.device, stream, size) if size else None
     _check(LIB.dkv_packed_attention_batched(
         _ptr(q), _ptr(knew), _ptr(vnew), _ptr(p4), _ptr(m4), _ptr(p8), _ptr(m8), _ptr(p16), _ptr(rows),
         _ptr(codes), _ptr(out), q.stride(1), q.stride(2), knew.stride(1), knew.stride(2), vnew.stride(1),
         vnew.stride(2), chunks, q.stride(0), knew.stride(0), vnew.stride(0), out.stride(0), layer, past, nq,
         cap4, cap8, cap16, heads, group, dim, block_m, block_n, layers, _ptr(workspace), size, _ptr(status),
-        _stream(q)))
+        stream))
     return out
 
 
@@ -227,11 +240,12 @@ def packed_attention_many(q, knew, vnew, histories, out, layer, nq, heads, group
     count = len(histories)
     table = (History * count)(*histories)
     size = LIB.dkv_packed_attention_many_workspace(max(h.past for h in histories), nq, heads, group, dim, count)
-    workspace = _workspace(q.device, _stream(q), size) if size else None
+    stream = _stream(q)
+    workspace = _workspace(q.device, stream, size) if size else None
     _check(LIB.dkv_packed_attention_many(
         _ptr(q), _ptr(knew), _ptr(vnew), ctypes.addressof(table), count, _ptr(out), q.stride(1), q.stride(2),
         knew.stride(1), knew.stride(2), vnew.stride(1), vnew.stride(2), q.stride(0), knew.stride(0),
-        vnew.stride(0), out.stride(0), layer, nq, heads, group, dim, layers, _ptr(workspace), size, _stream(q)))
+        vnew.stride(0), out.stride(0), layer, nq, heads, group, dim, layers, _ptr(workspace), size, stream))
     return out
 
 
@@ -257,11 +271,12 @@ def packed_attention_many_device(q, knew, vnew, histories_ptr, count, max_past, 
             raise ValueError('one history per request')
         _chunked(x, name)
     size = LIB.dkv_packed_attention_many_workspace(max_past, nq, heads, group, dim, count)
-    workspace = _workspace(q.device, _stream(q), size) if size else None
+    stream = _stream(q)
+    workspace = _workspace(q.device, stream, size) if size else None
     _check(LIB.dkv_packed_attention_many_device(
         _ptr(q), _ptr(knew), _ptr(vnew), histories_ptr, count, max_past, _ptr(out), q.stride(1), q.stride(2),
         knew.stride(1), knew.stride(2), vnew.stride(1), vnew.stride(2), q.stride(0), knew.stride(0),
-        vnew.stride(0), out.stride(0), layer, nq, heads, group, dim, layers, _ptr(workspace), size, _stream(q)))
+        vnew.stride(0), out.stride(0), layer, nq, heads, group, dim, layers, _ptr(workspace), size, stream))
     return out
 
 
@@ -271,12 +286,13 @@ def append_attention(q, knew, vnew, p4, m4, p8, m8, p16, rows, codes, out, layer
     """pack_rows (+ map_fill) and packed_attention of one frame in one launch."""
     q, knew, vnew = _rows_ready(q), _rows_ready(knew), _rows_ready(vnew)
     size = attention_workspace_bytes(past, nq, heads, group, dim)
-    workspace = _workspace(q.device, _stream(q), size) if size else None
+    stream = _stream(q)
+    workspace = _workspace(q.device, stream, size) if size else None
     _check(LIB.dkv_append_attention(
         _ptr(q), _ptr(knew), _ptr(vnew), _ptr(p4), _ptr(m4), _ptr(p8), _ptr(m8), _ptr(p16), _ptr(rows),
         _ptr(codes), _ptr(out), q.stride(1), q.stride(2), knew.stride(1), knew.stride(2), vnew.stride(1),
         vnew.stride(2), layer, past, nq, row_start, bits, int(fill_map), map_capacity, cap4, cap8, cap16, heads,
-        group, dim, block_m, block_n, layers, _ptr(workspace), size, _ptr(status), _stream(q)))
+        group, dim, block_m, block_n, layers, _ptr(workspace), size, _ptr(status), stream))
     return out
 
 
@@ -289,11 +305,12 @@ def append_attention_many_device(q, knew, vnew, targets_ptr, histories_ptr, coun
             raise ValueError('one history per request')
         _chunked(x, name)
     size = LIB.dkv_packed_attention_many_workspace(max_past, nq, heads, group, dim, count)
-    workspace = _workspace(q.device, _stream(q), size) if size else None
+    stream = _stream(q)
+    workspace = _workspace(q.device, stream, size) if size else None
     _check(LIB.dkv_append_attention_many_device(
         _ptr(q), _ptr(knew), _ptr(vnew), targets_ptr, histories_ptr, count, max_past, _ptr(out), q.stride(1),
         q.stride(2), knew.stride(1), knew.stride(2), vnew.stride(1), vnew.stride(2), q.stride(0), knew.stride(0),
-        vnew.stride(0), out.stride(0), layer, nq, heads, group, dim, layers, _ptr(workspace), size, _stream(q)))
+        vnew.stride(0), out.stride(0), layer, nq, heads, group, dim, layers, _ptr(workspace), size, stream))
     return out
 
 

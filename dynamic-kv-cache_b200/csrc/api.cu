@@ -128,7 +128,7 @@ int32_t dkv_packed_attention_launches(int32_t past, int32_t nq, int32_t heads, i
   const dkv::AttnPlan p = dkv::make_plan(past, nq, heads, group);
   if (p.splits == 1) return 1;
   bool fused = false;
-  if (p.tc && dkv::attention_tc_merges_in_kernel(p, heads, &fused) != cudaSuccess) return -1;
+  if (dkv::attention_tc_merges_in_kernel(p, heads, &fused) != cudaSuccess) return -1;
   return fused ? 1 : 2;
 }
 
@@ -169,21 +169,18 @@ int launch_planned(dkv::AttnArgs& a, const dkv::AttnPlan& p, const void* q, cons
   }
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int zdim = heads * chunks;  // grid z: chunk * heads + KV head
-  if (pack != nullptr) {  // append + attend: the tensor-core kernel packs too, else a pack launch first
-    if (p.tc && pack_on_device) {
+  if (pack != nullptr) {  // append + attend: the attention kernel packs the frame too
+    if (pack_on_device) {
       a.pack_mode = 2;
       a.pack_table = pack;
-    } else if (p.tc && chunks == 1) {
+    } else if (chunks == 1) {
       a.pack_mode = 1;
       a.pack = *pack;
     } else {
-      const cudaError_t e = dkv::launch_pack_many(knew, vnew, pack, pack_on_device, chunks, kh, kt, vh, vt, kc, vc,
-                                                  layer, nq, heads, st);
-      if (e != cudaSuccess) return cuda_status(e, "pack launch");
+      return fail(DKV_EINVAL, "a pack destination by value serves one request");
     }
   }
-  cudaError_t e = p.tc ? dkv::launch_attention_tc(a, zdim, st, table, device_table)
-                       : dkv::launch_attention_split(a, zdim, st, table, device_table);
+  cudaError_t e = dkv::launch_attention_tc(a, zdim, st, table, device_table);
   if (e == cudaSuccess && p.splits > 1 && !a.fused) e = dkv::launch_attention_combine(a, zdim, st);
   return cuda_status(e, "packed_attention launch");
 }

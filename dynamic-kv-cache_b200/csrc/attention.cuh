@@ -6,9 +6,7 @@
 namespace dkv {
 
 constexpr int kBN = 64;                 // keys per history tile
-constexpr int kMaxCtaRows = 192;        // flattened (query, head) rows per CTA, CUDA-core path
-constexpr int kTcCtaRows = 256;         // rows per CTA on the tensor-core path (2 x M=128)
-constexpr int kTcMinRows = 49;          // group*nq from which the tensor-core path is used
+constexpr int kTcCtaRows = 256;         // stacked (query, head) rows per CTA (2 x M=128)
 constexpr int kTargetCtas = 148;        // one wave on a B200 (148 SMs)
 // D^-0.5 * log2(e): the reference scales scores by D^-0.5 (src/gpu_kernels.py:95)
 // and uses exp; the kernels work in the exp2 domain with the factor folded in.
@@ -23,10 +21,9 @@ constexpr size_t kSyncBytes = 2 * kSyncGroups * sizeof(uint32_t);
 // Work decomposition of one attention call. Deterministic in (past, nq, heads,
 // group): no dependence on the device, so results are bit-identical across GPUs.
 struct AttnPlan {
-  int tc;        // 1: tcgen05 tensor-core kernel, 0: mma.sync split kernel
   int mrows;     // group * nq flattened rows per KV head (row r = query r/G, head r%G)
   int mblocks;   // row blocks per KV head
-  int cta_rows;  // rows per block (multiple of 16; 256 on the tensor-core path)
+  int cta_rows;  // rows per block (kTcCtaRows)
   int splits;    // history splits per (head, row block)
   int chunk;     // keys per split, multiple of kBN
   size_t ws_o_bytes, ws_ml_bytes;
@@ -48,15 +45,8 @@ inline AttnPlan make_plan(int past, int nq, int heads, int group, int chunks = 1
   heads *= chunks;
   AttnPlan p{};
   p.mrows = group * nq;
-  p.tc = p.mrows >= kTcMinRows;
-  if (p.tc) {
-    p.cta_rows = kTcCtaRows;
-    p.mblocks = (p.mrows + kTcCtaRows - 1) / kTcCtaRows;
-  } else {
-    p.mblocks = (p.mrows + kMaxCtaRows - 1) / kMaxCtaRows;
-    const int per_block = (p.mrows + p.mblocks - 1) / p.mblocks;
-    p.cta_rows = ((per_block + 15) / 16) * 16;
-  }
+  p.cta_rows = kTcCtaRows;
+  p.mblocks = (p.mrows + kTcCtaRows - 1) / kTcCtaRows;
   const int total = past + nq;
   const int tiles = (total + kBN - 1) / kBN;
   int target = kTargetCtas / (heads * p.mblocks);
@@ -211,8 +201,6 @@ __device__ __forceinline__ float merge_row_weights(Load load, int splits, float*
 // `table` (may be null): per-chunk histories of a call over several requests.
 // Per-chunk histories of a call over several requests: `table` (by value) or
 // `device_table` (device memory); both null: every chunk reads a.hist.
-cudaError_t launch_attention_split(const AttnArgs& a, int heads, cudaStream_t stream,
-                                   const HistoryTable* table = nullptr, const History* device_table = nullptr);
 // Sets a.fused when every CTA of the grid can be resident at once (one CTA per SM):
 // the split merge then runs inside the kernel and no combine launch follows.
 cudaError_t launch_attention_tc(AttnArgs& a, int heads, cudaStream_t stream, const HistoryTable* table = nullptr,

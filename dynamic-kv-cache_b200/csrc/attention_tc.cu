@@ -1123,7 +1123,7 @@ bool merge_in_kernel_allowed() {
 bool attention_tc_fused(const AttnPlan& p, int heads, int dev) {
   // in-kernel merge only when no CTA of a group can wait for one that is not yet resident
   const long long grid = static_cast<long long>(p.splits) * p.mblocks * heads;
-  return p.tc && p.splits > 1 && heads * p.mblocks <= kSyncGroups && grid <= g_resident[dev] &&
+  return p.splits > 1 && heads * p.mblocks <= kSyncGroups && grid <= g_resident[dev] &&
          merge_in_kernel_allowed();
 }
 
@@ -1140,7 +1140,6 @@ cudaError_t launch_attention_tc(AttnArgs& a, int heads, cudaStream_t stream, con
   cudaError_t e = configure(dev);
   if (e != cudaSuccess) return e;
   AttnPlan p{};
-  p.tc = 1;
   p.splits = a.splits;
   p.mblocks = a.mblocks;
   a.fused = a.sync != nullptr && attention_tc_fused(p, heads, dev);

@@ -131,8 +131,8 @@ class GPUCache(DynamicCache):
         return past
 
     def append_attend(self, q, k, v, layer):
-        """append() then attend() of one frame in one call (one launch on the
-        tensor-core path): returns [1, n, query_heads, dim], bit-identical to the
+        """append() then attend() of one frame in one call (one kernel launch):
+        returns [1, n, query_heads, dim], bit-identical to the
         two calls. The reference's attention forward makes the two calls back to
         back (src/gpu_cache.py:172-173)."""
         if k.shape[0] != 1 or k.shape[-1] != self.dim or k.device.type != 'cuda':

@@ -302,9 +302,8 @@ int dkv_packed_attention_many_device(const void* q, const void* knew, const void
  * [row_start, row_start + nq) of the `bits` pool exactly as dkv_pack_rows does
  * (with fill_map, also the token-map update of dkv_map_fill at [past, past + nq)),
  * and computes dkv_packed_attention over the `past` history tokens plus the new
- * rows read natively. On the tensor-core path (group * nq >= 49) one kernel does
- * both: its blocks pack their share of the new rows while they wait for the
- * other history splits. Otherwise a pack launch precedes the attention.
+ * rows read natively. One kernel does both: its blocks pack their share of the
+ * new rows while they wait for the other history splits.
  * Results are bit-identical to dkv_pack_rows (+ dkv_map_fill) followed by
  * dkv_packed_attention; same workspace contract as dkv_packed_attention.
  */

@@ -1,7 +1,7 @@
 """Append + attend in one call (dkv_append_attention): the output, the pools and
 the token maps must be bit-identical to pack_rows (+ map_fill) followed by
-packed_attention, on the tensor-core path (one launch: the attention blocks pack
-the frame) and on the short-query path (pack launch, then attention)."""
+packed_attention (one launch: the attention blocks pack the frame), from decode-
+shaped calls (1 query) to two row blocks per KV head."""
 import os
 import subprocess
 import sys

@@ -65,7 +65,7 @@ def _noalloc(fn, lib, cache, q, kn, vn, past):
 def test_noalloc_entry_point_matches_workspace_entry_point_on_two_calls(cuda):
     from src import gpu_kernels as K
     fn = _bind(K.LIB)
-    # (8128 past, 64 queries): tensor-core kernel, 26 splits; (4096, 5): mma.sync kernel
+    # (8128 past, 64 queries): 26 splits, register merge; (4096, 5): 15 stacked rows
     cases = [(8128, 64, 11), (4096, 5, 12)]
     built = [_case(*c) for c in cases]
     assert all(K.attention_workspace_bytes(p, n, 5, 3) > 0 for p, n, _ in cases)  # both use scratch

@@ -15,8 +15,12 @@ Printed (rank 0, one JSON line):
   value      packed-KV attention HBM GB/s, algorithmic bytes of all ranks / max time
              (device-resident inputs; the 32-layer sweep replayed as a CUDA graph)
   e2e        same metric through the public API (GPUCache.attend) with pinned host
-             buffers: per layer H2D of q/k/v and D2H of the output inside the timing
+             buffers: per step one H2D copy of every layer's q, k and v and one D2H
+             copy of the outputs inside the timing
+  decode_us_per_layer_call   1 query after the same history, per layer call
   frame_append_tokens_per_s  pack + attend of a 64-token frame on all 32 layers (one fused launch each)
+  c1..c5     the other BASELINE configurations (C3 also at past 1024 / 4096), each with
+             a CPU baseline of the oracle port on a bounded, stated sample
   roofline   dominant op (attention) vs measured HBM peak; roofline_tensor vs bf16
   cpu_baseline  the reference CPU path (dequantise + torch SDPA, oracle port) on a
              bounded sample of the same workload, all host cores
@@ -567,6 +571,29 @@ def main():
     value = world * LAYERS * bytes_call * args.steps / (ms_total * 1e-3) / 1e9
     us_call = 1e3 * ms_step / LAYERS
 
+    # ---- decode-shaped calls: 1 query after the same history, 32 layers, graph replay ----
+    dq1, dk1, dv1 = q[:, :, :, :1].contiguous(), kn[:, :, :, :1].contiguous(), vn[:, :, :, :1].contiguous()
+    douts = [None] * LAYERS
+
+    def decode_sweep():
+        for layer in range(LAYERS):
+            douts[layer] = cache.attend(dq1[layer], dk1[layer], dv1[layer], layer, PAST)
+
+    with torch.cuda.stream(stream):
+        decode_sweep()
+        dgraph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(dgraph, stream=stream):
+            decode_sweep()
+        for _ in range(args.warmup):
+            dgraph.replay()
+        start.record(stream)
+        for _ in range(20):
+            dgraph.replay()
+        end.record(stream)
+    torch.cuda.synchronize(device)
+    decode_us = 1e3 * start.elapsed_time(end) / 20 / LAYERS
+    del dgraph
+
     # ---- frame append (fused pack + attend on a fork, 32 layers), captured and replayed ----
     branch = cache.fork()
     branch.select(16)
@@ -653,6 +680,7 @@ def main():
                          '(larger than L2 at the default 32 layers: no flush needed)',
                    'requests': f'one independent request per rank (seed 1000+rank)', 'parallelism': f'dp{world}'},
         'us_per_layer_call': us_call,
+        'decode_us_per_layer_call': decode_us,
         'frame_append_tokens_per_s': fa_tokens_s,
         'frame_append_ms_per_frame': fa_ms_step,
         'e2e': {'value': e2e_value, 'unit': 'GB/s', 'h2d_bytes_per_step': h2d, 'd2h_bytes_per_step': d2h,

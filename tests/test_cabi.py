@@ -130,3 +130,39 @@ def test_attention_many_rejects_bad_arguments_on_host():
     rc = K.LIB.dkv_pack_rows_many_device(0x1000, 0x2000, 0x10008, 2, 64 * 64, 64, 64 * 64, 64, 5 * 64 * 64,
                                          5 * 64 * 64, 0, 64, 5, 64, 1, None)
     assert rc == K.DKV_EINVAL and 'aligned' in K.LIB.dkv_last_error().decode()
+
+
+def _append_args(**over):
+    # Fake, 16-byte aligned addresses: every case below fails host validation first.
+    a = dict(q=0x1000, knew=0x2000, vnew=0x3000, p4=0x4000, m4=0x5000, p8=0x6000, m8=0x7000, p16=0x8000,
+             rows=0x9000, codes=0xA000, out=0xB000, qh=64 * 64, qt=64, kh=64 * 64, kt=64, vh=64 * 64, vt=64,
+             layer=0, past=128, nq=64, row_start=0, bits=4, fill_map=1, map_capacity=4096, cap4=256, cap8=256,
+             cap16=256, heads=5, group=3, dim=64, block_m=16, block_n=64, layers=1, workspace=None, ws=0,
+             status=None, stream=None)
+    a.update(over)
+    return list(a.values())
+
+
+@pytest.mark.parametrize('over,code,text', [
+    (dict(bits=5), 1, 'bit widths'),
+    (dict(row_start=200), 2, 'capacity'),
+    (dict(rows=None), 1, 'null token map'),
+    (dict(map_capacity=150), 2, 'context limit'),
+    (dict(dim=128), 1, 'head_dim=64'),
+    (dict(p16=None), 1, 'null pool'),
+])
+def test_append_attention_rejects_bad_arguments_on_host(over, code, text):
+    from src import gpu_kernels as K
+    rc = K.LIB.dkv_append_attention(*_append_args(**over))
+    assert rc == code
+    assert text in K.LIB.dkv_last_error().decode()
+
+
+def test_append_attention_many_device_rejects_unaligned_tables():
+    from src import gpu_kernels as K
+    rest = [0xB000, 64 * 64, 64, 64 * 64, 64, 64 * 64, 64, 15 * 64 * 64, 5 * 64 * 64, 5 * 64 * 64, 15 * 64 * 64,
+            0, 64, 5, 3, 64, 1, None, 0, None]
+    rc = K.LIB.dkv_append_attention_many_device(0x1000, 0x2000, 0x3000, 0x10008, 0x20000, 2, 100, *rest)
+    assert rc == K.DKV_EINVAL and 'aligned' in K.LIB.dkv_last_error().decode()
+    rc = K.LIB.dkv_append_attention_many_device(0x1000, 0x2000, 0x3000, 0x10000, 0x20000, 0, 100, *rest)
+    assert rc == K.DKV_EINVAL and 'request count' in K.LIB.dkv_last_error().decode()

@@ -418,6 +418,7 @@ def bench_c4(device):
     cache = model.ingest(embeds, bits_for('dynamic', 96, seed=4), 'dynamic', qa_reserve=64)
     model.answer(question, cands, cache)
     model.answer(question, cands, cache, batched=True)
+    model.answer(question, cands, cache, graph=True)  # captures the candidate step once
     torch.cuda.synchronize(device)
     reps, t0 = 5, time.perf_counter()
     for _ in range(reps):
@@ -426,14 +427,21 @@ def bench_c4(device):
     ms = 1e3 * (time.perf_counter() - t0) / reps
     t0 = time.perf_counter()
     for _ in range(reps):
+        graphed = model.answer(question, cands, cache, graph=True)
+    torch.cuda.synchronize(device)
+    ms_graph = 1e3 * (time.perf_counter() - t0) / reps
+    t0 = time.perf_counter()
+    for _ in range(reps):
         batched = model.answer(question, cands, cache, batched=True)
     torch.cuda.synchronize(device)
     ms_batched = 1e3 * (time.perf_counter() - t0) / reps
     return {'ms_per_4_candidates': ms, 'prefix_tokens': cache.seen[0],
             'scores_mean_ll': ans['scores'], 'summed_ll': ans['summed'],
             'ms_per_4_candidates_batched': ms_batched, 'batched_scores_mean_ll': batched['scores'],
-            'note': 'wall time of StreamingModel.answer, eager: the reference protocol (4 forks x question + '
-                    'candidate) and batched (question once, 4 candidates in one forward)'}, model
+            'ms_per_4_candidates_graph': ms_graph, 'graph_scores_mean_ll': graphed['scores'],
+            'note': 'wall time of StreamingModel.answer: the reference protocol (4 forks x question + candidate) '
+                    'eager and with each candidate forward replayed from a captured CUDA graph, and batched '
+                    '(question once, 4 candidates in one eager forward)'}, model
 
 
 def bench_c5(model, device, rank, world, total, dist, batch, sequential):
@@ -454,7 +462,7 @@ def bench_c5(model, device, rank, world, total, dist, batch, sequential):
     warm = mine[:batch]  # captures the frame-step graph and loads every kernel once
     model.answer_many([reqs[r][1] for r in warm], [reqs[r][2] for r in warm],
                       model.ingest_many([reqs[r][0] for r in warm], [bits[r] for r in warm], 'dynamic',
-                                        qa_reserve=64, graph=True))
+                                        qa_reserve=64, graph=True), graph=True)
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize(device)
@@ -465,7 +473,7 @@ def bench_c5(model, device, rank, world, total, dist, batch, sequential):
         caches = model.ingest_many([reqs[r][0] for r in ids], [bits[r] for r in ids], 'dynamic', qa_reserve=64,
                                    graph=True)
         scores += [a['scores'] for a in model.answer_many([reqs[r][1] for r in ids], [reqs[r][2] for r in ids],
-                                                          caches)]
+                                                          caches, graph=True)]
         del caches
     torch.cuda.synchronize(device)
     secs = torch.tensor([time.perf_counter() - t0], device=device)
@@ -498,8 +506,9 @@ def bench_c5(model, device, rank, world, total, dist, batch, sequential):
                            'frame_append_tokens_per_s': seq * world * 64 * 64 / max(float(seq_secs.item()), 1e-9),
                            'max_abs_score_diff_vs_batched': float(diff.item())},
             'note': 'wall time of ingest + scoring with inputs already on the device (one warm-up batch first); '
-                    'batched: requests stepped together, each frame step one replay of a captured CUDA graph '
-                    '(FrameGraph: one append+attention launch per layer for the whole batch), scoring eager; '
+                    'batched: requests stepped together, each frame step and each candidate step one replay of '
+                    'a captured CUDA graph (FrameGraph: one append+attention launch per layer for the whole '
+                    'batch); '
                     'sequential: the reference protocol, one request at a time, eager; scores gathered with NCCL '
                     'all_gather'}
 

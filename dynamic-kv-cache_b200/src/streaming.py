@@ -46,15 +46,15 @@ class StreamingModel:
         self.model = Decoder(cfg, device=device, seed=seed)
         gen = torch.Generator().manual_seed(seed + 1)
         self.prefix_ids = torch.randint(0, cfg.vocab, (1, prefix_tokens), generator=gen).to(self.device)
-        self._frame_graphs = {}  # (requests, frame tokens) -> FrameGraph, captured once and rebound
+        self._frame_graphs = {}  # (requests, tokens, logits) -> FrameGraph, captured once and rebound
 
-    def frame_graph(self, caches, n):
-        """The FrameGraph for len(caches) requests of n-token frames, captured on first
-        use and rebound to `caches` afterwards."""
-        key = (len(caches), n)
+    def frame_graph(self, caches, n, logits=0):
+        """The FrameGraph for len(caches) requests of n-token steps returning `logits`
+        positions, captured on first use and rebound to `caches` afterwards."""
+        key = (len(caches), n, logits)
         fg = self._frame_graphs.get(key)
         if fg is None:
-            fg = self._frame_graphs[key] = FrameGraph(self.model, caches, n)
+            fg = self._frame_graphs[key] = FrameGraph(self.model, caches, n, logits=logits)
         else:
             fg.rebind(caches)
         return fg
@@ -88,20 +88,28 @@ class StreamingModel:
         return cache
 
     @torch.inference_mode()
-    def answer(self, question_ids, candidate_ids, cache, batched=False):
+    def answer(self, question_ids, candidate_ids, cache, batched=False, graph=False):
         """Candidate protocol (src/streaming.py:209-225): per candidate, a fork of
         the cache sees question + candidate; the score is the mean log-likelihood
         of the candidate tokens. Returns scores (mean), summed log-likelihoods and
         the argmax. batched=True (equal-length candidates; not in the reference)
         appends the question to one fork once and runs every candidate in one
-        forward over it: the same likelihoods up to floating-point order."""
+        forward over it: the same likelihoods up to floating-point order.
+        graph=True (GPUCache; not in the reference) replays each candidate's
+        forward from one captured CUDA graph (FrameGraph) instead of launching it."""
         if batched and len({c.shape[1] for c in candidate_ids}) == 1:
             return self._answer_batched(question_ids, candidate_ids, cache)
+        graph = graph and isinstance(cache, GPUCache)
         means, sums = [], []
         for answer_ids in candidate_ids:
             ids = torch.cat((question_ids, answer_ids), dim=1)
             fork = cache.fork()
-            logits = self.model(fork, ids=ids, logits=answer_ids.shape[1] + 1)
+            if graph:
+                fg = self.frame_graph([fork], ids.shape[1], answer_ids.shape[1] + 1)
+                logits = fg.step(ids=ids)
+                fg.batch.release()
+            else:
+                logits = self.model(fork, ids=ids, logits=answer_ids.shape[1] + 1)
             ll = logits[0, :-1].log_softmax(-1).gather(1, answer_ids[0][:, None])[:, 0]
             means.append(ll.mean())
             sums.append(ll.sum())
@@ -147,11 +155,12 @@ class StreamingModel:
         return caches
 
     @torch.inference_mode()
-    def answer_many(self, questions, candidates, caches):
+    def answer_many(self, questions, candidates, caches, graph=False):
         """answer() (the reference's candidate protocol) for B requests at once:
         candidate j of every request runs on a fork of that request's cache, the B
         forks in one batched forward. questions[r] [1, q], candidates[r] a list of
         [1, c] ids; every request has the same question and candidate lengths.
+        graph=True replays each candidate step from one captured CUDA graph.
         Returns one answer() dict per request."""
         b = len(caches)
         if len(questions) != b or len(candidates) != b or len({len(c) for c in candidates}) != 1:
@@ -164,7 +173,12 @@ class StreamingModel:
             answers = [c[j] for c in candidates]
             ids = torch.cat([torch.cat((q, a), dim=1) for q, a in zip(questions, answers)], dim=0)  # [B, q + c]
             forks = [cache.fork() for cache in caches]
-            logits = self.model.forward_many(forks, ids=ids, logits=answers[0].shape[1] + 1)
+            if graph:
+                fg = self.frame_graph(forks, ids.shape[1], answers[0].shape[1] + 1)
+                logits = fg.step(ids=ids)
+                fg.batch.release()
+            else:
+                logits = self.model.forward_many(forks, ids=ids, logits=answers[0].shape[1] + 1)
             target = torch.cat(answers, dim=0)                                                  # [B, c]
             ll = logits[:, :-1].log_softmax(-1).gather(2, target[..., None])[..., 0]           # [B, c]
             for r in range(b):

@@ -290,12 +290,12 @@ def test_frame_graph_is_reused_for_the_next_batch(cuda):
                                candidate_tokens=6, device='cuda') for s in seeds] for seeds in ((11, 12), (13, 14))]
     bits = [[bits_for('dynamic', 4, seed=s) for s in seeds] for seeds in ((11, 12), (13, 14))]
     model.ingest_many([r[0] for r in sets[0]], bits[0], 'dynamic', qa_reserve=64, graph=True)
-    graph = model._frame_graphs[(2, 64)].graph
+    graph = model._frame_graphs[(2, 64, 0)].graph
     graphed = model.ingest_many([r[0] for r in sets[1]], bits[1], 'dynamic', qa_reserve=64, graph=True)
-    assert model._frame_graphs[(2, 64)].graph is graph  # captured once
-    assert model._frame_graphs[(2, 64)].batch.caches == []  # finished caches are not kept alive
+    assert model._frame_graphs[(2, 64, 0)].graph is graph  # captured once
+    assert model._frame_graphs[(2, 64, 0)].batch.caches == []  # finished caches are not kept alive
     with pytest.raises(ValueError, match='no caches bound'):
-        model._frame_graphs[(2, 64)].step(embeds=torch.zeros(2, 64, TINY.hidden, dtype=torch.bfloat16,
+        model._frame_graphs[(2, 64, 0)].step(embeds=torch.zeros(2, 64, TINY.hidden, dtype=torch.bfloat16,
                                                                 device='cuda'))
     eager = model.ingest_many([r[0] for r in sets[1]], bits[1], 'dynamic', qa_reserve=64)
     got = model.answer_many([r[1] for r in sets[1]], [r[2] for r in sets[1]], graphed)
@@ -306,3 +306,30 @@ def test_frame_graph_is_reused_for_the_next_batch(cuda):
         for x, y in zip(g.materialize(0), e.materialize(0)):
             assert torch.equal(x, y)
         assert max(abs(p - q) for p, q in zip(a['scores'], b['scores'])) < 2e-2
+
+
+@pytest.mark.parametrize('mode', ['fused16', 'dynamic'])
+def test_graph_replayed_scoring_matches_eager_scoring(cuda, mode):
+    """The reference protocol with each candidate's forward replayed from a captured
+    graph scores like the eager protocol and the oracle decoder, for one request and
+    for a batch of requests; a second run through the cached graphs repeats it."""
+    model = StreamingModel(TINY, device='cuda', seed=9)
+    reqs = [synthetic_request(TINY, seed=s, frames=4, frame_tokens=64, question_tokens=12, candidates=3,
+                              candidate_tokens=6, device='cuda') for s in (21, 22)]
+    bits = [bits_for(mode, 4, seed=s) for s in (21, 22)]
+    caches = model.ingest_many([r[0] for r in reqs], bits, mode, qa_reserve=64)
+    oracle = OracleDecoder(TINY, decoder_params(model.model))
+    for r, (embeds, question, cands) in enumerate(reqs):
+        eager = model.answer(question, cands, caches[r])
+        graphed = model.answer(question, cands, caches[r], graph=True)
+        again = model.answer(question, cands, caches[r], graph=True)
+        means, _ = oracle.request(model.prefix_ids, embeds, bits[r], question, cands)
+        assert max(abs(a - b) for a, b in zip(graphed['scores'], eager['scores'])) < 2e-2
+        assert max(abs(a - b) for a, b in zip(graphed['scores'], means)) < 2e-2
+        assert graphed['scores'] == again['scores']
+        caches[r].check()
+    many = model.answer_many([r[1] for r in reqs], [r[2] for r in reqs], caches, graph=True)
+    eager_many = model.answer_many([r[1] for r in reqs], [r[2] for r in reqs], caches)
+    for a, b in zip(many, eager_many):
+        assert max(abs(x - y) for x, y in zip(a['scores'], b['scores'])) < 2e-2
+    assert all(c.seen == caches[0].seen for c in caches)  # scoring never moves the video caches

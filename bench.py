@@ -444,6 +444,42 @@ def bench_c4(device):
                     '(question once, 4 candidates in one eager forward)'}, model
 
 
+def rank_requests(total, world, rank):
+    """Request ids of one rank: a contiguous slice of `total` // `world`."""
+    per = total // world
+    return list(range(rank * per, (rank + 1) * per))
+
+
+def rank_batches(total, world, rank, batch):
+    """The request batches one rank steps together: fixed-size slices of its requests,
+    so whenever `batch` divides total // world every GPU count forms the same batches
+    (and, with deterministic kernels, the same scores)."""
+    mine = rank_requests(total, world, rank)
+    return [mine[s:s + batch] for s in range(0, len(mine), batch)]
+
+
+def max_over_ranks(values, dist):
+    """Element-wise max over ranks of a 1-D tensor (the job's time is its slowest rank's)."""
+    if dist is not None:
+        dist.all_reduce(values, op=dist.ReduceOp.MAX)
+    return values
+
+
+def gather_scores(local, dist, world):
+    """Every rank's score rows, in rank order (one all_gather of a few KiB)."""
+    if dist is None:
+        return local
+    gathered = [torch.empty_like(local) for _ in range(world)]
+    dist.all_gather(gathered, local)
+    return torch.cat(gathered)
+
+
+def scores_digest(scores):
+    """SHA-256 of fp32 score rows: equal digests = bit-identical scores."""
+    import hashlib
+    return hashlib.sha256(scores.detach().float().cpu().contiguous().numpy().tobytes()).hexdigest()
+
+
 def bench_c5(model, device, rank, world, total, dist, batch, sequential):
     """C5: `total` independent requests (64 frames x 64 tokens, dynamic 4/8/16, seed = request
     id, then 4-candidate scoring) split across ranks; on each rank the requests are stepped
@@ -451,10 +487,9 @@ def bench_c5(model, device, rank, world, total, dist, batch, sequential):
     pack and one attention launch per layer for the whole batch). Scores gathered with NCCL.
     The first `sequential` requests of each rank are also run one at a time through the
     reference's per-request protocol, timed separately, and their scores compared."""
-    import hashlib
     from src.streaming import bits_for, synthetic_request
     per = total // world
-    mine = list(range(rank * per, (rank + 1) * per))
+    mine = rank_requests(total, world, rank)
     # inputs (frame embeddings as a vision tower would hand them over, question and
     # candidates) are made on the device before the clock starts
     reqs = {r: synthetic_request(model.cfg, seed=r, frames=64, device=device) for r in mine}
@@ -468,8 +503,7 @@ def bench_c5(model, device, rank, world, total, dist, batch, sequential):
     torch.cuda.synchronize(device)
     t0 = time.perf_counter()
     scores = []
-    for s in range(0, per, batch):
-        ids = mine[s:s + batch]
+    for ids in rank_batches(total, world, rank, batch):
         caches = model.ingest_many([reqs[r][0] for r in ids], [bits[r] for r in ids], 'dynamic', qa_reserve=64,
                                    graph=True)
         scores += [a['scores'] for a in model.answer_many([reqs[r][1] for r in ids], [reqs[r][2] for r in ids],
@@ -490,18 +524,12 @@ def bench_c5(model, device, rank, world, total, dist, batch, sequential):
     diff = torch.tensor([max((abs(a - b) for x, y in zip(seq_scores, scores) for a, b in zip(x, y)), default=0.0)],
                         device=device)
     local = torch.tensor(scores, dtype=torch.float32, device=device)
-    if dist is not None:
-        dist.all_reduce(secs, op=dist.ReduceOp.MAX)
-        dist.all_reduce(seq_secs, op=dist.ReduceOp.MAX)
-        dist.all_reduce(diff, op=dist.ReduceOp.MAX)
-        gathered = [torch.empty_like(local) for _ in range(world)]
-        dist.all_gather(gathered, local)
-        local = torch.cat(gathered)
-    all_scores = local.cpu().numpy()
+    secs, seq_secs, diff = max_over_ranks(torch.cat((secs, seq_secs, diff)), dist).split(1)
+    all_scores = gather_scores(local, dist, world)
     return {'frame_append_tokens_per_s': per * world * 64 * 64 / float(secs.item()),
             'requests': per * world, 'seconds': float(secs.item()), 'batch_per_gpu': batch,
             'scaling': 'strong (fixed request set)',
-            'scores_sha256': hashlib.sha256(all_scores.tobytes()).hexdigest(),
+            'scores_sha256': scores_digest(all_scores),
             'sequential': {'requests_per_gpu': seq, 'seconds': float(seq_secs.item()),
                            'frame_append_tokens_per_s': seq * world * 64 * 64 / max(float(seq_secs.item()), 1e-9),
                            'max_abs_score_diff_vs_batched': float(diff.item())},

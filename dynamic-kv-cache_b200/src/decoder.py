@@ -118,7 +118,6 @@ class Decoder(torch.nn.Module):
         return cos.view(b, n, 1, -1), sin.view(b, n, 1, -1)
 
     def attention(self, x, layer, cache, cos, sin):
-        c = self.cfg
         n = x.shape[1]
         q, k, v = self.project_qkv(x, layer, cos, sin)
         if isinstance(cache, GPUCache):
@@ -134,7 +133,6 @@ class Decoder(torch.nn.Module):
         """Attention of B token chunks x [B, n, hidden] side by side over the cache's
         history: each chunk sees the history and its own earlier tokens; nothing is
         appended (the packed path runs one batched kernel call per layer)."""
-        c = self.cfg
         b, n = x.shape[0], x.shape[1]
         q, k, v = self.project_qkv(x, layer, cos, sin)
         past = cache.get_seq_length(layer)

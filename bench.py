@@ -419,6 +419,7 @@ def bench_c4(device):
     model.answer(question, cands, cache)
     model.answer(question, cands, cache, batched=True)
     model.answer(question, cands, cache, graph=True)  # captures the candidate step once
+    model.answer(question, cands, cache, batched=True, graph=True)
     torch.cuda.synchronize(device)
     reps, t0 = 5, time.perf_counter()
     for _ in range(reps):
@@ -432,6 +433,11 @@ def bench_c4(device):
     ms_graph = 1e3 * (time.perf_counter() - t0) / reps
     t0 = time.perf_counter()
     for _ in range(reps):
+        batched_graph = model.answer(question, cands, cache, batched=True, graph=True)
+    torch.cuda.synchronize(device)
+    ms_batched_graph = 1e3 * (time.perf_counter() - t0) / reps
+    t0 = time.perf_counter()
+    for _ in range(reps):
         batched = model.answer(question, cands, cache, batched=True)
     torch.cuda.synchronize(device)
     ms_batched = 1e3 * (time.perf_counter() - t0) / reps
@@ -439,9 +445,11 @@ def bench_c4(device):
             'scores_mean_ll': ans['scores'], 'summed_ll': ans['summed'],
             'ms_per_4_candidates_batched': ms_batched, 'batched_scores_mean_ll': batched['scores'],
             'ms_per_4_candidates_graph': ms_graph, 'graph_scores_mean_ll': graphed['scores'],
+            'ms_per_4_candidates_batched_graph': ms_batched_graph,
+            'batched_graph_scores_mean_ll': batched_graph['scores'],
             'note': 'wall time of StreamingModel.answer: the reference protocol (4 forks x question + candidate) '
                     'eager and with each candidate forward replayed from a captured CUDA graph, and batched '
-                    '(question once, 4 candidates in one eager forward)'}, model
+                    '(question once, 4 candidates in one forward) eager and graph-replayed'}, model
 
 
 def rank_requests(total, world, rank):

@@ -189,8 +189,13 @@ class Decoder(torch.nn.Module):
         for layer in range(c.layers):
             q, k, v = self.project_qkv(self.rms(x, self.norm_attn[layer]), layer, cos, sin)
             out = torch.empty((b, n, c.q_heads, c.head_dim), dtype=x.dtype, device=x.device)
-            K.append_attention_many_device(q, k, v, batch.targets_ptr, batch.histories_ptr, b, batch.max_past, out,
-                                           layer, n, c.kv_heads, c.q_heads // c.kv_heads, c.head_dim, c.layers)
+            if batch.append:
+                K.append_attention_many_device(q, k, v, batch.targets_ptr, batch.histories_ptr, b, batch.max_past,
+                                               out, layer, n, c.kv_heads, c.q_heads // c.kv_heads, c.head_dim,
+                                               c.layers)
+            else:
+                K.packed_attention_many_device(q, k, v, batch.histories_ptr, b, batch.max_past, out, layer, n,
+                                               c.kv_heads, c.q_heads // c.kv_heads, c.head_dim, c.layers)
             x = x + F.linear(out.reshape(b, n, -1), self.o[layer])
             h = self.rms(x, self.norm_mlp[layer])
             gate, up = F.linear(h, self.gate_up[layer]).chunk(2, dim=-1)
@@ -242,11 +247,13 @@ class FrameGraph:
     the warm-up); the graph of the whole decoder step is then captured once and
     every later step is: host bookkeeping + one descriptor copy (RequestBatch),
     one input copy, one graph replay. Steps must keep the frame length n; the
-    caches' precision may change per step (select() before step())."""
+    caches' precision may change per step (select() before step()). With
+    append=False the steps attend over the caches' histories without appending
+    (query chunks side by side, e.g. candidates over one fork)."""
 
-    def __init__(self, model, caches, n, logits=0, max_past=None):
+    def __init__(self, model, caches, n, logits=0, max_past=None, append=True):
         self.model, self.n, self.logits = model, n, logits
-        self.batch = RequestBatch(caches, n, max_past)
+        self.batch = RequestBatch(caches, n, max_past, append)
         dev = self.batch.device
         self.x = torch.empty((len(caches), n, model.cfg.hidden), dtype=model.embed.dtype, device=dev)
         self.stream = torch.cuda.Stream(dev)

@@ -404,12 +404,16 @@ class RequestBatch:
     GPUCache.append makes on each layer, pool growth included) and refreshes the
     buffer with one stream-ordered copy from pinned memory. A graph captured over
     the kernels therefore replays correctly step after step. The histories are
-    planned for at most `max_past` tokens (default: the caches' capacity)."""
+    planned for at most `max_past` tokens (default: the caches' capacity). With
+    append=False the steps attend without appending (query chunks side by side over
+    their caches' histories, e.g. candidates over one fork): no claims, and one
+    cache may appear several times."""
 
-    def __init__(self, caches, n, max_past=None):
+    def __init__(self, caches, n, max_past=None, append=True):
         first = _same_geometry(caches)
-        if len({c.p16.data_ptr() for c in caches}) != len(caches):
+        if append and len({c.p16.data_ptr() for c in caches}) != len(caches):
             raise ValueError('batched appends need caches with their own pools')
+        self.append = append
         self.caches, self.n, self.count = list(caches), n, len(caches)
         self.layers, self.heads, self.dim, self.device = first.layers, first.heads, first.dim, first.device
         self.max_past = max(c.capacity for c in caches) if max_past is None else max_past
@@ -441,23 +445,30 @@ class RequestBatch:
         if len(caches) != self.count or (first.layers, first.heads, first.dim, first.device) != \
                 (self.layers, self.heads, self.dim, self.device):
             raise ValueError('rebinding needs as many caches of the same geometry')
-        if len({c.p16.data_ptr() for c in caches}) != len(caches):
+        if self.append and len({c.p16.data_ptr() for c in caches}) != len(caches):
             raise ValueError('batched appends need caches with their own pools')
         self.caches = list(caches)
 
     def prepare(self):
         """Claims the next n-token frame of every cache at its selected precision on
-        all layers and writes the step's descriptors to the device (ordered on the
-        current stream before whatever is launched next). Returns the pasts."""
+        all layers (append=False: takes each cache's history as it is) and writes the
+        step's descriptors to the device (ordered on the current stream before
+        whatever is launched next). Returns the pasts."""
         if len(self.caches) != self.count:
             raise ValueError('request batch has no caches bound (rebind before stepping)')
-        _check_room(self.caches, 0, self.n)
+        if self.append:
+            _check_room(self.caches, 0, self.n)
         if self._copied is not None:
             self._copied.synchronize()  # the previous step's copy has left the pinned buffer
         pasts = []
         for r, c in enumerate(self.caches):
-            past, row = c._claim_frame(self.n)
-            self._targets[r] = _pack_target(c, past, row, c.online)
+            if self.append:
+                past, row = c._claim_frame(self.n)
+                self._targets[r] = _pack_target(c, past, row, c.online)
+            else:
+                past = c.seen[0]
+                if any(x != past for x in c.seen):
+                    raise ValueError('GPU cache layers disagree about the history length')
             self._hists[r] = _history(c, past)
             self._positions[r] = self._ramp + past
             pasts.append(past)

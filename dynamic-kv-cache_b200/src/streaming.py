@@ -46,15 +46,15 @@ class StreamingModel:
         self.model = Decoder(cfg, device=device, seed=seed)
         gen = torch.Generator().manual_seed(seed + 1)
         self.prefix_ids = torch.randint(0, cfg.vocab, (1, prefix_tokens), generator=gen).to(self.device)
-        self._frame_graphs = {}  # (requests, tokens, logits) -> FrameGraph, captured once and rebound
+        self._frame_graphs = {}  # (requests, tokens, logits, append) -> FrameGraph, captured once and rebound
 
-    def frame_graph(self, caches, n, logits=0):
+    def frame_graph(self, caches, n, logits=0, append=True):
         """The FrameGraph for len(caches) requests of n-token steps returning `logits`
         positions, captured on first use and rebound to `caches` afterwards."""
-        key = (len(caches), n, logits)
+        key = (len(caches), n, logits, append)
         fg = self._frame_graphs.get(key)
         if fg is None:
-            fg = self._frame_graphs[key] = FrameGraph(self.model, caches, n, logits=logits)
+            fg = self._frame_graphs[key] = FrameGraph(self.model, caches, n, logits=logits, append=append)
         else:
             fg.rebind(caches)
         return fg
@@ -98,7 +98,7 @@ class StreamingModel:
         graph=True (GPUCache; not in the reference) replays each candidate's
         forward from one captured CUDA graph (FrameGraph) instead of launching it."""
         if batched and len({c.shape[1] for c in candidate_ids}) == 1:
-            return self._answer_batched(question_ids, candidate_ids, cache)
+            return self._answer_batched(question_ids, candidate_ids, cache, graph and isinstance(cache, GPUCache))
         graph = graph and isinstance(cache, GPUCache)
         means, sums = [], []
         for answer_ids in candidate_ids:
@@ -191,11 +191,19 @@ class StreamingModel:
                             prediction=max(range(len(values)), key=values.__getitem__)))
         return out
 
-    def _answer_batched(self, question_ids, candidate_ids, cache):
+    def _answer_batched(self, question_ids, candidate_ids, cache, graph=False):
         fork = cache.fork()
-        first = self.model(fork, ids=question_ids, logits=1)[0, -1].log_softmax(-1)  # predicts token 0
         ids = torch.cat(candidate_ids, dim=0)                                         # [B, n]
-        rest = self.model.forward_chunks(fork, ids, logits=ids.shape[1])[:, :-1].log_softmax(-1)
+        if graph:  # the question appended by one graph replay, the candidates attended by another
+            fg = self.frame_graph([fork], question_ids.shape[1], 1)
+            first = fg.step(ids=question_ids)[0, -1].log_softmax(-1)                  # predicts token 0
+            fg.batch.release()
+            fg = self.frame_graph([fork] * ids.shape[0], ids.shape[1], ids.shape[1], append=False)
+            rest = fg.step(ids=ids)[:, :-1].log_softmax(-1)
+            fg.batch.release()
+        else:
+            first = self.model(fork, ids=question_ids, logits=1)[0, -1].log_softmax(-1)  # predicts token 0
+            rest = self.model.forward_chunks(fork, ids, logits=ids.shape[1])[:, :-1].log_softmax(-1)
         ll = torch.cat((first[ids[:, :1]], rest.gather(2, ids[:, 1:, None])[..., 0]), dim=1)  # [B, n]
         means, sums = ll.mean(1), ll.sum(1)
         values = means.tolist()

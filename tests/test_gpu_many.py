@@ -290,12 +290,12 @@ def test_frame_graph_is_reused_for_the_next_batch(cuda):
                                candidate_tokens=6, device='cuda') for s in seeds] for seeds in ((11, 12), (13, 14))]
     bits = [[bits_for('dynamic', 4, seed=s) for s in seeds] for seeds in ((11, 12), (13, 14))]
     model.ingest_many([r[0] for r in sets[0]], bits[0], 'dynamic', qa_reserve=64, graph=True)
-    graph = model._frame_graphs[(2, 64, 0)].graph
+    graph = model._frame_graphs[(2, 64, 0, True)].graph
     graphed = model.ingest_many([r[0] for r in sets[1]], bits[1], 'dynamic', qa_reserve=64, graph=True)
-    assert model._frame_graphs[(2, 64, 0)].graph is graph  # captured once
-    assert model._frame_graphs[(2, 64, 0)].batch.caches == []  # finished caches are not kept alive
+    assert model._frame_graphs[(2, 64, 0, True)].graph is graph  # captured once
+    assert model._frame_graphs[(2, 64, 0, True)].batch.caches == []  # finished caches are not kept alive
     with pytest.raises(ValueError, match='no caches bound'):
-        model._frame_graphs[(2, 64, 0)].step(embeds=torch.zeros(2, 64, TINY.hidden, dtype=torch.bfloat16,
+        model._frame_graphs[(2, 64, 0, True)].step(embeds=torch.zeros(2, 64, TINY.hidden, dtype=torch.bfloat16,
                                                                 device='cuda'))
     eager = model.ingest_many([r[0] for r in sets[1]], bits[1], 'dynamic', qa_reserve=64)
     got = model.answer_many([r[1] for r in sets[1]], [r[2] for r in sets[1]], graphed)
@@ -333,3 +333,24 @@ def test_graph_replayed_scoring_matches_eager_scoring(cuda, mode):
     for a, b in zip(many, eager_many):
         assert max(abs(x - y) for x, y in zip(a['scores'], b['scores'])) < 2e-2
     assert all(c.seen == caches[0].seen for c in caches)  # scoring never moves the video caches
+
+
+@pytest.mark.parametrize('mode', ['fused16', 'dynamic'])
+def test_graph_replayed_batched_scoring_matches_eager(cuda, mode):
+    """Batched scoring (question once, candidates side by side over one fork) with
+    both steps replayed from captured graphs, the candidates' without appending."""
+    model = StreamingModel(TINY, device='cuda', seed=13)
+    embeds, question, cands = synthetic_request(TINY, seed=31, frames=4, frame_tokens=64, question_tokens=12,
+                                                candidates=4, candidate_tokens=6, device='cuda')
+    bits = bits_for(mode, 4, seed=31)
+    cache = model.ingest(embeds, bits, mode, qa_reserve=64)
+    eager = model.answer(question, cands, cache, batched=True)
+    graphed = model.answer(question, cands, cache, batched=True, graph=True)
+    again = model.answer(question, cands, cache, batched=True, graph=True)
+    means, _ = OracleDecoder(TINY, decoder_params(model.model)).request(model.prefix_ids, embeds, bits, question,
+                                                                        cands)
+    assert max(abs(a - b) for a, b in zip(graphed['scores'], eager['scores'])) < 2e-2
+    assert max(abs(a - b) for a, b in zip(graphed['scores'], means)) < 2e-2
+    assert graphed['scores'] == again['scores']
+    cache.check()
+    assert cache.seen == [model.prefix_ids.shape[1] + 4 * 64] * TINY.layers

@@ -1,6 +1,7 @@
 // Tensor-core (tcgen05 + TMEM) causal GQA attention over packed mixed-precision
-// history, sm_100a. Used when the stacked query rows (group * nq) form a real
-// dense contraction (frame appends, candidate scoring).
+// history, sm_100a: every attention call, from a one-token decode step (3 stacked
+// rows, padded into the M=128 tile) to frames and candidate chunks of two row
+// blocks per KV head.
 //
 // Semantics are those of the reference kernel packed_attention
 // (src/gpu_kernels.py:71-105): dequantised history rounded to bf16 (:93-94), the
@@ -8,14 +9,15 @@
 // online softmax (:98-103), p rounded to bf16 before P.V (:102), fp32 accumulation.
 //
 // One CTA per (KV head, block of up to 256 stacked rows, history split), 16 warps
-// in five roles, connected only by mbarriers:
-//   warps 10-11 loaders (even / odd tiles): token maps of tile i+6 arrive by TMA
-//               bulk copy; for tile i+4
-//               the warp splits the 64 tokens into runs of consecutive pool rows of
-//               one precision and streams each run (codes, and the offset/scale
-//               pairs) into a 4-deep raw ring with one TMA bulk copy per run;
-//   warps 12-15 converters: dequantise a raw tile in registers into bf16 K and V
-//               tiles (64 keys) of a 3-stage ring, 128B-swizzled for the tensor core;
+// in five roles, connected only by mbarriers (warp w runs on sub-partition w % 4):
+//   warps 12-13 loaders (even / odd tiles): token maps of tile i+6 arrive by TMA
+//               bulk copy; for tile i+4 the warp splits the 64 tokens into runs of
+//               consecutive pool rows of one precision and streams each run (codes,
+//               and the offset/scale pairs) into a 4-deep raw ring with one TMA bulk
+//               copy per run;
+//   warps 10, 11, 14, 15 converters: dequantise a raw tile in registers into bf16
+//               K and V tiles (64 keys) of a 3-stage ring, 128B-swizzled for the
+//               tensor core;
 //   warp 8      S issuer (one thread): S = Q K^T into TMEM, double-buffered, with Q
 //               held in TMEM; an S buffer is reused as soon as the softmax has read it;
 //   warp 9      PV issuer (one thread): O += P V into TMEM with P read from TMEM;
@@ -28,15 +30,22 @@
 // converters' and TMA's shared-memory traffic.
 // The running max is only moved when a tile's max exceeds it by more than 2^8
 // (p <= 256, exact after the final O / l division). Partial (max, sum, O) per
-// split go to the workspace and are merged by the deterministic combine kernel.
-// Every mbarrier wait is bounded: a stalled pipeline reports DKV_ETIMEOUT in the
-// status word and the CTA exits after its MMAs drain and TMEM is freed.
+// split go to the workspace. Every mbarrier wait is bounded: a stalled pipeline
+// reports DKV_ETIMEOUT in the status word and the CTA exits after its MMAs drain
+// and TMEM is freed.
 //
 // When the whole grid is resident at once (one CTA per SM, at most 148 CTAs), the
 // splits are merged in the same launch: each CTA publishes its partial, counts
 // itself in on its group's arrival counter and, once all splits of the group are
 // in, merges an equal slice of the group's rows from every split's partial. The
 // wait is bounded; the last CTA to leave resets the counters for the next call.
+// Otherwise the combine kernel merges them, with the same arithmetic.
+// A call that appends (append + attend in one launch) also packs the new rows:
+// the CTAs of a (chunk, KV head) share them, each packing its share while it
+// waits for its group.
+// A query chunk's history comes from the call itself, from a by-value table of
+// requests in the kernel parameters, or from a table in device memory (graph
+// replay): three instantiations of the same kernel.
 #include <cstdlib>
 #include <cstring>
 
@@ -426,7 +435,7 @@ attention_tc_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ 
     }
     __syncwarp();
   } else if (warp == kPVWarp) {
-    // ================= [O | l] += P [V | 1] issuer =================
+    // ================= O += P V issuer =================
     if (lane == 0 && ntiles > 0) {
       bool ok = true;
       for (int i = 0; i < ntiles && ok; ++i) {

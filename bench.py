@@ -747,10 +747,12 @@ def main():
     if 'c3' in configs:
         line['c3_past_sweep'] = bench_c3_sweep(device)
     model = None
-    if 'c4' in configs or 'c5' in configs:
-        c4, model = bench_c4(device)
-        if 'c4' in configs:
-            line['c4_candidate_scoring'] = c4
+    if 'c4' in configs:
+        line['c4_candidate_scoring'], model = bench_c4(device)
+    elif 'c5' in configs:
+        from src.decoder import SMOLLM2_360M
+        from src.streaming import StreamingModel
+        model = StreamingModel(SMOLLM2_360M, device=device, seed=0)
     if 'c5' in configs:
         line['c5_request_throughput'] = bench_c5(model, device, rank, world, args.c5_requests, dist, args.c5_batch,
                                                  args.c5_sequential)

@@ -17,6 +17,10 @@ cudaError_t launch_reconstruct(const Pools& P, const int32_t* rows, const uint8_
                                int layer, int n, int32_t* status, cudaStream_t stream);
 cudaError_t launch_map_fill(int32_t* rows, uint8_t* codes, int64_t start, int n, int64_t row, int bits,
                             cudaStream_t stream);
+cudaError_t launch_rotary(const void* x, const float* cos_t, const float* sin_t, void* out, int64_t xb, int64_t xt,
+                          int64_t cb, int b, int n, int heads, cudaStream_t stream);
+cudaError_t launch_silu_mul(const void* gate, const void* up, void* out, int64_t gs, int64_t us, int64_t rows,
+                            int width, cudaStream_t stream);
 cudaError_t launch_pack_many(const void* k, const void* v, const dkv_pack_target* targets, bool on_device, int count,
                              int64_t kh, int64_t kt, int64_t vh, int64_t vt, int64_t kc, int64_t vc, int layer, int n,
                              int heads, cudaStream_t stream);
@@ -457,6 +461,35 @@ int dkv_map_fill(int32_t* rows, uint8_t* codes, int64_t start, int32_t n, int64_
   if (n == 0) return ok();
   return cuda_status(dkv::launch_map_fill(rows, codes, start, n, row, bits, static_cast<cudaStream_t>(stream)),
                      "map_fill launch");
+}
+
+int dkv_rotary(const void* x, const float* cos_t, const float* sin_t, void* out, int64_t xb, int64_t xt,
+               int64_t cb, int32_t b, int32_t n, int32_t heads, int32_t dim, void* stream) {
+  if (dim != dkv::kDim) return fail(DKV_EINVAL, "GPU kernel currently supports head_dim=64");
+  if (b < 0 || n < 0 || heads <= 0) return fail(DKV_EINVAL, "rotary: negative sizes or no heads");
+  if (static_cast<int64_t>(b) * n == 0) return ok();
+  if (!x || !cos_t || !sin_t || !out) return fail(DKV_EINVAL, "rotary: null pointer");
+  if (!aligned16(x) || !aligned16(out) || !aligned16(cos_t) || !aligned16(sin_t))
+    return fail(DKV_EINVAL, "rotary: tensors must be 16-byte aligned");
+  if (xb < 0 || xt < static_cast<int64_t>(heads) * dim || xb % 8 || xt % 8)
+    return fail(DKV_EINVAL, "rotary: token strides must hold the heads and be multiples of 8 elements");
+  if (cb < 0 || cb % 4) return fail(DKV_EINVAL, "rotary: table batch stride must be a multiple of 4");
+  return cuda_status(dkv::launch_rotary(x, cos_t, sin_t, out, xb, xt, cb, b, n, heads,
+                                        static_cast<cudaStream_t>(stream)),
+                     "rotary launch");
+}
+
+int dkv_silu_mul(const void* gate, const void* up, void* out, int64_t gs, int64_t us, int64_t rows, int32_t width,
+                 void* stream) {
+  if (rows < 0 || width <= 0 || width % 8) return fail(DKV_EINVAL, "silu_mul: width must be a positive multiple of 8");
+  if (rows == 0) return ok();
+  if (!gate || !up || !out) return fail(DKV_EINVAL, "silu_mul: null pointer");
+  if (!aligned16(gate) || !aligned16(up) || !aligned16(out))
+    return fail(DKV_EINVAL, "silu_mul: tensors must be 16-byte aligned");
+  if (gs < width || us < width || gs % 8 || us % 8)
+    return fail(DKV_EINVAL, "silu_mul: row strides must hold a row and be multiples of 8 elements");
+  return cuda_status(dkv::launch_silu_mul(gate, up, out, gs, us, rows, width, static_cast<cudaStream_t>(stream)),
+                     "silu_mul launch");
 }
 
 }  // extern "C"

@@ -106,7 +106,10 @@ class Decoder(torch.nn.Module):
         c = self.cfg
         b, n = x.shape[0], x.shape[1]
         h = F.linear(x, self.qkv[layer]).view(b, n, c.q_heads + 2 * c.kv_heads, c.head_dim)
-        qk = apply_rope(h[:, :, :c.q_heads + c.kv_heads], cos, sin)
+        if h.is_cuda:  # one launch, bit-identical to apply_rope
+            qk = K.rotary(h, cos, sin, c.q_heads + c.kv_heads)
+        else:  # the native-cache decoder on the CPU
+            qk = apply_rope(h[:, :, :c.q_heads + c.kv_heads], cos, sin)
         q = qk[:, :, :c.q_heads].transpose(1, 2)
         k = qk[:, :, c.q_heads:].transpose(1, 2)
         v = h[:, :, c.q_heads + c.kv_heads:].transpose(1, 2)

@@ -81,6 +81,8 @@ def _load():
         'dkv_append_attention': ([P, P, P, P, P, P, P, P, P, P, P, I64, I64, I64, I64, I64, I64, I32, I32, I32, I64,
                                   I32, I32, I64, I64, I64, I64, I32, I32, I32, I32, I32, I32, P, SZ, P, P],
                                  ctypes.c_int),
+        'dkv_rotary': ([P, P, P, P, I64, I64, I64, I32, I32, I32, I32, P], ctypes.c_int),
+        'dkv_silu_mul': ([P, P, P, I64, I64, I64, I32, P], ctypes.c_int),
         'dkv_append_attention_many_device': ([P, P, P, P, P, I32, I32, P, I64, I64, I64, I64, I64, I64, I64, I64, I64,
                                               I64, I32, I32, I32, I32, I32, I32, P, SZ, P], ctypes.c_int),
     }
@@ -95,7 +97,8 @@ EXPORTS = ('dkv_version', 'dkv_last_error', 'dkv_pack_rows', 'dkv_packed_attenti
            'dkv_packed_attention_workspace', 'dkv_packed_attention_launches', 'dkv_packed_attention_batched',
            'dkv_packed_attention_batched_workspace', 'dkv_reconstruct', 'dkv_map_fill', 'dkv_pack_rows_many',
            'dkv_packed_attention_many', 'dkv_packed_attention_many_workspace', 'dkv_pack_rows_many_device',
-           'dkv_packed_attention_many_device', 'dkv_append_attention', 'dkv_append_attention_many_device')
+           'dkv_packed_attention_many_device', 'dkv_append_attention', 'dkv_append_attention_many_device',
+           'dkv_rotary', 'dkv_silu_mul')
 
 
 def _check(rc):
@@ -324,6 +327,46 @@ def reconstruct(p4, m4, p8, m8, p16, rows, codes, out, layer, n, cap4, cap8, cap
 
 def map_fill(rows, codes, start, n, row, bits, capacity):
     _check(LIB.dkv_map_fill(_ptr(rows), _ptr(codes), start, n, row, bits, capacity, _stream(rows)))
+
+
+def rotary(x, cos, sin, heads):
+    """Rotate-half rotary embedding of the first `heads` heads of x (bf16 [b, n, >= heads,
+    64], heads contiguous) with fp32 tables cos / sin [b or 1, n, 1 or absent, 64]: one
+    launch, bit-identical to the fp32 PyTorch form (x.float() * cos + rotate_half(x) * sin,
+    rounded to bf16). Returns bf16 [b, n, heads, 64], contiguous."""
+    if x.dtype != torch.bfloat16 or cos.dtype != torch.float32 or sin.dtype != torch.float32:
+        raise ValueError('rotary takes bf16 activations and fp32 cos / sin tables')
+    b, n, dim = x.shape[0], x.shape[1], x.shape[-1]
+    if x.stride(-1) != 1 or x.stride(-2) != dim or x.stride(1) % 8 or x.stride(0) % 8 or x.data_ptr() % 16:
+        x = x.contiguous()
+    cos, sin = cos.reshape(cos.shape[0], n, dim), sin.reshape(sin.shape[0], n, dim)
+    if cos.shape[0] not in (1, b) or sin.shape != cos.shape:
+        raise ValueError('rotary tables must have 1 or b rows of n positions')
+    cos, sin = cos.contiguous(), sin.contiguous()
+    out = torch.empty((b, n, heads, dim), dtype=torch.bfloat16, device=x.device)
+    cb = n * dim if cos.shape[0] > 1 else 0
+    _check(LIB.dkv_rotary(_ptr(x), _ptr(cos), _ptr(sin), _ptr(out), x.stride(0), x.stride(1), cb, b, n, heads, dim,
+                          _stream(x)))
+    return out
+
+
+def silu_mul(gate, up):
+    """silu(gate) * up for bf16 gate / up of one shape [..., width] (rows with a common
+    stride, e.g. the two halves of a joined gate/up projection): one launch,
+    bit-identical to torch.nn.functional.silu(gate) * up. Returns a contiguous bf16
+    tensor of that shape."""
+    if gate.dtype != torch.bfloat16 or up.dtype != torch.bfloat16 or gate.shape != up.shape:
+        raise ValueError('silu_mul takes bf16 gate and up of one shape')
+    width = gate.shape[-1]
+    g, u = gate.reshape(-1, width), up.reshape(-1, width)
+    if g.stride(-1) != 1 or g.stride(0) % 8 or g.data_ptr() % 16:
+        g = g.contiguous()
+    if u.stride(-1) != 1 or u.stride(0) % 8 or u.data_ptr() % 16:
+        u = u.contiguous()
+    out = torch.empty(gate.shape, dtype=torch.bfloat16, device=gate.device)
+    _check(LIB.dkv_silu_mul(_ptr(g), _ptr(u), _ptr(out), g.stride(0), u.stride(0), g.shape[0], width,
+                            _stream(gate)))
+    return out
 
 
 def raise_for_status(status):

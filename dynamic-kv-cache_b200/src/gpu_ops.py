@@ -2,13 +2,17 @@
 
 The reference joins the QKV and gate/up projection weights into single GEMMs
 and runs RMSNorm / SiLU*up as prebuilt PyTorch CUDA ops (src/gpu_ops.py:9-48).
-These are library GEMMs and pointwise ops, not part of the packed-KV kernels,
-so they stay on PyTorch here too; the API and the weight-joining invariants
-(bit-identical parameter views over one joined tensor) are the same.
+The GEMMs and the RMSNorm stay on PyTorch here; SiLU*up on CUDA bf16 tensors is
+one libdkv launch (dkv_silu_mul, bit-identical to the two PyTorch ops it
+replaces), and other dtypes / devices keep the reference's PyTorch form. The API
+and the weight-joining invariants (bit-identical parameter views over one joined
+tensor) are the same.
 """
 import types
 
 import torch
+
+from . import gpu_kernels as K
 
 
 def cuda_rms(x, weight, eps):
@@ -17,7 +21,10 @@ def cuda_rms(x, weight, eps):
 
 
 def activation_product(gate, up):
-    """silu(gate) * up (src/gpu_ops.py:14-17)."""
+    """silu(gate) * up (src/gpu_ops.py:14-17): one dkv_silu_mul launch for CUDA bf16
+    tensors, the reference's PyTorch form otherwise."""
+    if gate.is_cuda and gate.dtype == torch.bfloat16 and up.dtype == torch.bfloat16 and gate.shape == up.shape:
+        return K.silu_mul(gate, up)
     return torch.nn.functional.silu(gate) * up
 
 

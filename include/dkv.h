@@ -355,6 +355,31 @@ int dkv_reconstruct(const void* p4, const void* m4, const void* p8,
 int dkv_map_fill(int32_t* rows, uint8_t* codes, int64_t start, int32_t n,
                  int64_t row, int32_t bits, int64_t capacity, void* stream);
 
+/*
+ * Rotate-half rotary embedding of the first `heads` heads of each token, one
+ * launch (the reference applies HF apply_rotary_pos_emb to q and k before
+ * append / attend, src/gpu_cache.py:170; this is its fp32 form, as in the
+ * streaming decoder). x: bf16 [b, n, >= heads, dim], token strides (xb, xt)
+ * in elements, heads contiguous; cos / sin: fp32 [b or 1, n, dim] with batch
+ * stride cb (0 broadcasts one table over b) and token stride dim; out: bf16
+ * [b, n, heads, dim], contiguous. For i < dim/2, with h = dim/2:
+ *   out[i]     = bf16(x[i] cos[i]         - x[i + h] sin[i])
+ *   out[i + h] = bf16(x[i + h] cos[i + h] + x[i] sin[i + h])
+ * each product and the sum one fp32 operation rounded to nearest.
+ */
+int dkv_rotary(const void* x, const float* cos_t, const float* sin_t, void* out,
+               int64_t xb, int64_t xt, int64_t cb, int32_t b, int32_t n,
+               int32_t heads, int32_t dim, void* stream);
+
+/*
+ * silu(gate) * up over `rows` rows of `width` elements (activation_product,
+ * src/gpu_ops.py:14-17), one launch: silu = gate / (1 + exp(-gate)) in fp32
+ * rounded to bf16, then the product in fp32 rounded to bf16. gate / up: bf16
+ * with row strides gs / us (elements); out: bf16 [rows, width], contiguous.
+ */
+int dkv_silu_mul(const void* gate, const void* up, void* out, int64_t gs, int64_t us,
+                 int64_t rows, int32_t width, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

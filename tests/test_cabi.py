@@ -166,3 +166,40 @@ def test_append_attention_many_device_rejects_unaligned_tables():
     assert rc == K.DKV_EINVAL and 'aligned' in K.LIB.dkv_last_error().decode()
     rc = K.LIB.dkv_append_attention_many_device(0x1000, 0x2000, 0x3000, 0x10000, 0x20000, 0, 100, *rest)
     assert rc == K.DKV_EINVAL and 'request count' in K.LIB.dkv_last_error().decode()
+
+
+@pytest.mark.parametrize('over,text', [
+    (dict(dim=32), 'head_dim=64'),
+    (dict(heads=0), 'no heads'),
+    (dict(x=0x1008), 'aligned'),
+    (dict(xt=20 * 64 - 8), 'token strides'),
+    (dict(xb=12), 'token strides'),
+    (dict(cb=6), 'batch stride'),
+    (dict(cos=None), 'null pointer'),
+])
+def test_rotary_rejects_bad_arguments_on_host(over, text):
+    from src import gpu_kernels as K
+    a = dict(x=0x1000, cos=0x2000, sin=0x3000, out=0x4000, xb=64 * 25 * 8, xt=25 * 64, cb=8 * 64, b=2, n=8,
+             heads=20, dim=64, stream=None)
+    a.update(over)
+    assert K.LIB.dkv_rotary(*a.values()) == K.DKV_EINVAL
+    assert text in K.LIB.dkv_last_error().decode()
+    a.update(b=0)  # an empty call is a no-op once the shape checks pass
+    if 'dim' not in over and 'heads' not in over:
+        assert K.LIB.dkv_rotary(*a.values()) == K.DKV_OK
+
+
+@pytest.mark.parametrize('over,text', [
+    (dict(width=12), 'multiple of 8'),
+    (dict(width=0), 'multiple of 8'),
+    (dict(up=0x2004), 'aligned'),
+    (dict(gs=2552), 'row strides'),
+    (dict(us=5124), 'row strides'),
+    (dict(out=None), 'null pointer'),
+])
+def test_silu_mul_rejects_bad_arguments_on_host(over, text):
+    from src import gpu_kernels as K
+    a = dict(gate=0x1000, up=0x2000, out=0x3000, gs=5120, us=5120, rows=7, width=2560, stream=None)
+    a.update(over)
+    assert K.LIB.dkv_silu_mul(*a.values()) == K.DKV_EINVAL
+    assert text in K.LIB.dkv_last_error().decode()

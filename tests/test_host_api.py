@@ -165,3 +165,30 @@ def test_a_batch_over_the_context_limit_leaves_every_cache_unchanged():
         _check_room([a, b], 0, 65)
     assert a.seen == [64, 64] and b.seen == [64, 64] and len(a.plan) == len(b.plan) == 1
     _check_room([a, b], 0, 64)
+
+
+def test_install_fused_ops_joins_weights_and_keeps_the_forward():
+    """install_fused_ops (src/gpu_ops.py:19-48): the QKV and gate/up weights become
+    views of one joined tensor each (same values, no second copy), and the fused
+    RMSNorm / MLP forwards give the original forwards' results (CPU, fp32: the
+    reference's PyTorch form of the ops)."""
+    from src.gpu_ops import install_fused_ops
+    model = _tiny_llama().float()
+    ids = torch.randint(0, 1000, (1, 17))
+    with torch.no_grad():
+        expected = model(ids).logits
+    before = {n: p.detach().clone() for n, p in model.named_parameters()}
+    state = {'enabled': True}
+    install_fused_ops(model.model, state)
+    for name, p in model.named_parameters():
+        assert torch.equal(p, before[name]), name
+    attn, mlp = model.model.layers[0].self_attn, model.model.layers[0].mlp
+    assert attn.q_proj.weight.data_ptr() == attn._qkv_weight.data_ptr()
+    assert attn.v_proj.weight.data_ptr() == attn._qkv_weight[-attn.v_proj.out_features:].data_ptr()
+    assert mlp.up_proj.weight.data_ptr() == mlp._gate_up_weight[mlp.gate_proj.out_features:].data_ptr()
+    with torch.no_grad():
+        fused = model(ids).logits
+        state['enabled'] = False
+        original = model(ids).logits
+    assert torch.allclose(fused, expected, atol=1e-4, rtol=1e-4)
+    assert torch.equal(original, expected)

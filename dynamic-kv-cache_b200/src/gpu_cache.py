@@ -342,6 +342,23 @@ def _check_room(caches, layer, n):
             raise ValueError('GPU context limit exceeded')
 
 
+def _claim_all(caches, claim):
+    """claim(c) for every cache, all or nothing: if one raises (a frame that does not
+    match an offline plan, layers out of step), the caches claimed before it get their
+    host bookkeeping back, so the batch leaves every cache as it was. Pools grown on
+    the way stay grown (their rows are unchanged)."""
+    saved, out = [], []
+    try:
+        for c in caches:
+            saved.append((c, c.seen.copy(), c.cursors.copy(), c.plan.copy(), c.host_counts.copy()))
+            out.append(claim(c))
+    except Exception:
+        for c, seen, cursors, plan, counts in saved:
+            c.seen, c.cursors, c.plan, c.host_counts = seen, cursors, plan, counts
+        raise
+    return out
+
+
 def _same_geometry(caches):
     if not caches:
         raise ValueError('no caches')
@@ -365,11 +382,9 @@ def append_many(caches, k, v, layer):
         # a cache listed twice, or forks of one cache (they write the same reserved rows)
         raise ValueError('batched appends need caches with their own pools')
     _check_room(caches, layer, n)
-    targets, claims = [], []
-    for c in caches:
-        past, n, row = c._claim(layer, n, fill_map=False)
-        claims.append(past)
-        targets.append(_pack_target(c, past, row, c.online and layer == 0))
+    claimed = _claim_all(caches, lambda c: c._claim(layer, n, fill_map=False))
+    claims = [past for past, _, _ in claimed]
+    targets = [_pack_target(c, past, row, c.online and layer == 0) for c, (past, _, row) in zip(caches, claimed)]
     for s in range(0, b, K.MAX_REQUESTS):
         e = min(s + K.MAX_REQUESTS, b)
         K.pack_rows_many(k[s:e], v[s:e], targets[s:e], layer, n, first.heads, first.dim, first.layers)
@@ -460,15 +475,16 @@ class RequestBatch:
             _check_room(self.caches, 0, self.n)
         if self._copied is not None:
             self._copied.synchronize()  # the previous step's copy has left the pinned buffer
+        if self.append:
+            claimed = _claim_all(self.caches, lambda c: c._claim_frame(self.n))
+        else:
+            claimed = [(c.seen[0], None) for c in self.caches]
+            if any(x != c.seen[0] for c in self.caches for x in c.seen):
+                raise ValueError('GPU cache layers disagree about the history length')
         pasts = []
-        for r, c in enumerate(self.caches):
+        for r, (c, (past, row)) in enumerate(zip(self.caches, claimed)):
             if self.append:
-                past, row = c._claim_frame(self.n)
                 self._targets[r] = _pack_target(c, past, row, c.online)
-            else:
-                past = c.seen[0]
-                if any(x != past for x in c.seen):
-                    raise ValueError('GPU cache layers disagree about the history length')
             self._hists[r] = _history(c, past)
             self._positions[r] = self._ramp + past
             pasts.append(past)

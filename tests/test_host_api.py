@@ -192,3 +192,23 @@ def test_install_fused_ops_joins_weights_and_keeps_the_forward():
         original = model(ids).logits
     assert torch.allclose(fused, expected, atol=1e-4, rtol=1e-4)
     assert torch.equal(original, expected)
+
+
+def test_a_batch_claim_that_fails_leaves_every_cache_unchanged():
+    """Batched appends claim all caches or none: a cache whose offline plan does
+    not match the frame undoes the claims already made for the others."""
+    from src.gpu_cache import _claim_all
+    a = GPUCache(None, layers=2, device='cpu', max_tokens=512)
+    b = GPUCache(None, layers=2, device='cpu', max_tokens=512)
+    bad = GPUCache([(16, 64)], layers=2, device='cpu')
+    for c in (a, b, bad):
+        c.select(4, 0)
+    with pytest.raises(ValueError, match='does not match plan'):
+        _claim_all([a, b, bad], lambda c: c._claim_frame(64))
+    for c in (a, b):
+        assert c.seen == [0, 0] and c.plan == [] and c.host_counts == {4: 0, 8: 0, 16: 0}
+    assert bad.seen == [0, 0] and bad.cursors == [0, 0]
+    bad.select(16, 0)
+    claimed = _claim_all([a, b, bad], lambda c: c._claim_frame(64))
+    assert claimed == [(0, 0), (0, 0), (0, 0)]
+    assert a.seen == b.seen == bad.seen == [64, 64] and a.plan == [(0, 64, 4, 0)] and a.host_counts[4] == 64

@@ -212,3 +212,22 @@ def test_a_batch_claim_that_fails_leaves_every_cache_unchanged():
     claimed = _claim_all([a, b, bad], lambda c: c._claim_frame(64))
     assert claimed == [(0, 0), (0, 0), (0, 0)]
     assert a.seen == b.seen == bad.seen == [64, 64] and a.plan == [(0, 64, 4, 0)] and a.host_counts[4] == 64
+
+
+def test_request_descriptors_carry_the_cache_state():
+    """The per-request descriptors the batched kernels read (dkv_history,
+    dkv_pack_target) hold the cache's own pools, maps, capacities and lengths."""
+    from src.gpu_cache import _history, _pack_target
+    c = GPUCache(None, layers=2, device='cpu', max_tokens=512)
+    c.select(8, 0)
+    past, row = c._claim_frame(64)
+    h = _history(c, past)
+    assert (h.p4, h.m4, h.p8, h.m8, h.p16) == tuple(t.data_ptr() for t in c._pools())
+    assert (h.rows, h.codes) == (c.rows.data_ptr(), c.codes.data_ptr())
+    assert (h.cap4, h.cap8, h.cap16, h.past, h.capacity) == (c.caps[4], c.caps[8], c.caps[16], 0, 512)
+    assert h.status == c.status.data_ptr()
+    t = _pack_target(c, past, row, True)
+    assert (t.bits, t.row_start, t.map_start, t.map_capacity) == (8, 0, 0, 512)
+    assert (t.map_rows, t.map_codes) == (c.rows.data_ptr(), c.codes.data_ptr())
+    t = _pack_target(c, past, row, False)
+    assert t.map_rows is None and t.map_codes is None

@@ -49,9 +49,12 @@ PAST, NQ, FRAME = 8128, 64, 64
 MIX = ([4, 8, 16], [0.5, 0.3, 0.2])
 ROW_BYTES = {4: 32 + 8, 8: 64 + 8, 16: 128}  # code bytes + (offset, scale) per row
 METRIC = 'packed-KV attention HBM GB/s at 8K ctx'
-# DRAM bytes (read + write) of attention_tc_kernel for one call of this shape,
-# from the ncu capture summarised in profiles/attention_tc_kernel_c3_8k.md.
-NCU_TRAFFIC_BYTES = 5_805_056  # dram__bytes_read.sum + write of one attention_tc_kernel launch (profiles/attention_tc_kernel_c3_8k.md)
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one attention_tc_kernel
+# launch of this exact call shape (P = 8128, 64 queries, 15Q/5KV, the frame mix of
+# seed 0), from an ncu --set full capture of `bench.py --layers 2` (one launch of the
+# timed sweep, after warm-up). It is a recorded figure, not measured by this run: a
+# kernel change is re-captured and this constant updated with it.
+NCU_TRAFFIC_BYTES = 5_805_056
 WORKLOAD = 'C3 frame-append attention, 8K ctx, 32-layer cache'
 
 
@@ -193,10 +196,11 @@ def cpu_baseline(seconds, threads=None):
     q = torch.randn(1, HEADS * GROUP, NQ, DIM, generator=gen).bfloat16().float()
     kn = torch.randn(1, HEADS, NQ, DIM, generator=gen).bfloat16().float()
     vn = torch.randn(1, HEADS, NQ, DIM, generator=gen).bfloat16().float()
-    cpu_path.cpu_cache_attention(frames, q, kn, vn)  # warm-up
+    bits = random.Random(0).choices(MIX[0], weights=MIX[1], k=len(plan) + 1)[-1]  # the appended frame's
+    cpu_path.cpu_cache_update(frames, q, kn, vn, bits)  # warm-up
     calls, start = 0, time.perf_counter()
     while True:
-        cpu_path.cpu_cache_attention(frames, q, kn, vn)
+        cpu_path.cpu_cache_update(frames, q, kn, vn, bits)
         calls += 1
         elapsed = time.perf_counter() - start
         if elapsed >= seconds or calls >= 10000:
@@ -204,7 +208,8 @@ def cpu_baseline(seconds, threads=None):
     gbs = attention_bytes(plan) * calls / elapsed / 1e9
     return {'value': gbs, 'unit': 'GB/s', 'cores': threads, 'kind': 'port',
             'sample': f'{calls} single-layer calls (P={PAST}, n={NQ}, 15Q/5KV) of the reference CPU path '
-                      f'(unpack all frames + cat + torch SDPA) in {elapsed:.1f} s; ms/call {1e3 * elapsed / calls:.2f}'}
+                      f'(MixedPrecisionCache.update: unpack all frames + pack of the current frame\'s K and V at '
+                      f'{bits} bits + cat, then torch SDPA) in {elapsed:.1f} s; ms/call {1e3 * elapsed / calls:.2f}'}
 
 
 def measured_peaks():
@@ -246,13 +251,15 @@ def bench_c1(seconds=2.0):
         frames.append(pools.pack_frame(to_bits(k), to_bits(v), b))
     q = torch.randn(1, HEADS * GROUP, NQ, DIM, generator=gen)
     kn, vn = torch.randn(1, HEADS, NQ, DIM, generator=gen), torch.randn(1, HEADS, NQ, DIM, generator=gen)
-    cpu_path.cpu_cache_attention(frames, q, kn, vn)
+    new_bits = random.Random(1).choices(MIX[0], weights=MIX[1], k=17)[-1]
+    cpu_path.cpu_cache_update(frames, q, kn, vn, new_bits)
     calls, t0 = 0, time.perf_counter()
     while time.perf_counter() - t0 < seconds:
-        cpu_path.cpu_cache_attention(frames, q, kn, vn)
+        cpu_path.cpu_cache_update(frames, q, kn, vn, new_bits)
         calls += 1
     return {'ms_per_call': 1e3 * (time.perf_counter() - t0) / calls, 'cores': os.cpu_count(), 'past': 1024,
-            'what': 'reference CPU path (unpack + cat + SDPA), one layer, 64-token append'}
+            'what': 'reference CPU path (unpack + pack of the current frame + cat + SDPA), one layer, '
+                    '64-token append'}
 
 
 def bench_c3_sweep(device, cases=((1024, 256), (4096, 64))):

@@ -5,6 +5,9 @@
 #include <cstddef>
 #include <cstdio>
 #include <cstring>
+#include <map>
+#include <mutex>
+#include <utility>
 
 #include "attention.cuh"
 
@@ -89,6 +92,54 @@ namespace dkv {
 int set_last_error(int code, const char* message) { return fail(code, "%s", message); }
 }  // namespace dkv
 
+namespace {
+
+// What the last launch of this library on each (device, stream) wrote that an
+// attention call may read as history: nothing, one layer's pool rows, or token
+// maps (read by every layer). Every kernel here releases its programmatic
+// dependents only after its own griddepcontrol.wait, so when a kernel starts,
+// every kernel launched two or more before it on its stream has completed: only
+// the immediately preceding one may still be writing. An attention call streams
+// its history before its own wait unless that preceding launch wrote this layer's
+// rows or the maps (then it waits first). Kernels of other libraries launched in
+// between only make this conservative: they are either ordinary launches (which
+// start after everything before them completed) or, if programmatic, must not
+// release their dependents before their own wait either.
+constexpr int kWroteNothing = -1;
+constexpr int kWroteMaps = -2;
+std::mutex g_write_mu;
+std::map<std::pair<int, const void*>, int> g_last_write;
+
+std::pair<int, const void*> stream_key(void* stream) {
+  int dev = -1;
+  cudaGetDevice(&dev);
+  return {dev, stream};
+}
+
+int last_write(void* stream) {
+  const auto key = stream_key(stream);
+  std::lock_guard<std::mutex> lock(g_write_mu);
+  const auto it = g_last_write.find(key);
+  return it == g_last_write.end() ? kWroteNothing : it->second;
+}
+
+// Records what a launch that succeeded on `stream` wrote; passes `rc` through.
+int note_write(void* stream, int wrote, int rc) {
+  if (rc == DKV_OK) {
+    const auto key = stream_key(stream);
+    std::lock_guard<std::mutex> lock(g_write_mu);
+    g_last_write[key] = wrote;
+  }
+  return rc;
+}
+
+bool history_may_be_fresh(void* stream, int layer) {
+  const int w = last_write(stream);
+  return w == kWroteMaps || w == layer;
+}
+
+}  // namespace
+
 extern "C" {
 
 int32_t dkv_version(void) { return DKV_VERSION; }
@@ -112,9 +163,10 @@ int dkv_pack_rows(const void* k, const void* v, void* p4, void* m4, void* p8, vo
     return fail(DKV_ECAPACITY, "rows [%lld, %lld) exceed the %d-bit pool capacity %lld",
                 (long long)row_start, (long long)(row_start + n), bits, (long long)cap);
   if (2LL * heads * n * 8 > INT32_MAX) return fail(DKV_EINVAL, "frame too large");
-  return cuda_status(dkv::launch_pack(k, v, p4, m4, p8, m8, p16, kh, kt, vh, vt, layer, row_start, n, cap,
-                                      heads, bits, status, static_cast<cudaStream_t>(stream)),
-                     "pack_rows launch");
+  return note_write(stream, layer,
+                    cuda_status(dkv::launch_pack(k, v, p4, m4, p8, m8, p16, kh, kt, vh, vt, layer, row_start, n,
+                                                 cap, heads, bits, status, static_cast<cudaStream_t>(stream)),
+                                "pack_rows launch"));
 }
 
 size_t dkv_packed_attention_workspace(int32_t past, int32_t nq, int32_t heads, int32_t group, int32_t dim) {
@@ -184,9 +236,15 @@ int launch_planned(dkv::AttnArgs& a, const dkv::AttnPlan& p, const void* q, cons
       return fail(DKV_EINVAL, "a pack destination by value serves one request");
     }
   }
+  a.hist_wait = history_may_be_fresh(stream, layer) ? 1 : 0;
   cudaError_t e = dkv::launch_attention_tc(a, zdim, st, table, device_table);
-  if (e == cudaSuccess && p.splits > 1 && !a.fused) e = dkv::launch_attention_combine(a, zdim, st);
-  return cuda_status(e, "packed_attention launch");
+  const bool combine = p.splits > 1 && !a.fused;
+  if (e == cudaSuccess && combine) e = dkv::launch_attention_combine(a, zdim, st);
+  // A fused pack runs after the attention kernel has released its dependents; a
+  // combine launch after it completes it first.
+  int wrote = kWroteNothing;
+  if (pack != nullptr && !combine) wrote = (pack_on_device || pack->map_rows != nullptr) ? kWroteMaps : layer;
+  return note_write(stream, wrote, cuda_status(e, "packed_attention launch"));
 }
 
 int attention_impl(const void* q, const void* knew, const void* vnew, const void* p4, const void* m4,
@@ -280,9 +338,12 @@ int dkv_pack_rows_many(const void* k, const void* v, const dkv_pack_target* targ
       return fail(DKV_ECAPACITY, "GPU context limit exceeded");
   }
   if (n == 0) return ok();
-  return cuda_status(dkv::launch_pack_many(k, v, targets, false, count, kh, kt, vh, vt, kc, vc, layer, n, heads,
-                                           static_cast<cudaStream_t>(stream)),
-                     "pack_rows_many launch");
+  bool maps = false;
+  for (int r = 0; r < count; ++r) maps = maps || targets[r].map_rows != nullptr;
+  return note_write(stream, maps ? kWroteMaps : layer,
+                    cuda_status(dkv::launch_pack_many(k, v, targets, false, count, kh, kt, vh, vt, kc, vc, layer, n,
+                                                      heads, static_cast<cudaStream_t>(stream)),
+                                "pack_rows_many launch"));
 }
 
 int dkv_pack_rows_many_device(const void* k, const void* v, const dkv_pack_target* targets, int32_t count,
@@ -297,9 +358,10 @@ int dkv_pack_rows_many_device(const void* k, const void* v, const dkv_pack_targe
     return fail(DKV_EINVAL, "k/v rows must be 16-byte aligned (strides multiples of 8)");
   if (2LL * heads * n * 8 > INT32_MAX) return fail(DKV_EINVAL, "frame too large");
   if (n == 0) return ok();
-  return cuda_status(dkv::launch_pack_many(k, v, targets, true, count, kh, kt, vh, vt, kc, vc, layer, n, heads,
-                                           static_cast<cudaStream_t>(stream)),
-                     "pack_rows_many_device launch");
+  return note_write(stream, kWroteMaps,  // device targets may update the maps
+                    cuda_status(dkv::launch_pack_many(k, v, targets, true, count, kh, kt, vh, vt, kc, vc, layer, n,
+                                                      heads, static_cast<cudaStream_t>(stream)),
+                                "pack_rows_many_device launch"));
 }
 
 size_t dkv_packed_attention_many_workspace(int32_t max_past, int32_t nq, int32_t heads, int32_t group, int32_t dim,
@@ -446,9 +508,10 @@ int dkv_reconstruct(const void* p4, const void* m4, const void* p8, const void* 
   dkv::Pools P{static_cast<const uint8_t*>(p4), static_cast<const float2*>(m4),
                static_cast<const uint8_t*>(p8), static_cast<const float2*>(m8),
                static_cast<const uint16_t*>(p16), cap4, cap8, cap16, heads};
-  return cuda_status(dkv::launch_reconstruct(P, rows, codes, out, layer, n, status,
-                                             static_cast<cudaStream_t>(stream)),
-                     "reconstruct launch");
+  return note_write(stream, kWroteNothing,
+                    cuda_status(dkv::launch_reconstruct(P, rows, codes, out, layer, n, status,
+                                                        static_cast<cudaStream_t>(stream)),
+                                "reconstruct launch"));
 }
 
 int dkv_map_fill(int32_t* rows, uint8_t* codes, int64_t start, int32_t n, int64_t row, int32_t bits,
@@ -459,8 +522,10 @@ int dkv_map_fill(int32_t* rows, uint8_t* codes, int64_t start, int32_t n, int64_
   if (start + n > capacity) return fail(DKV_ECAPACITY, "GPU context limit exceeded");
   if (row + n > INT32_MAX) return fail(DKV_ECAPACITY, "pool row exceeds int32");
   if (n == 0) return ok();
-  return cuda_status(dkv::launch_map_fill(rows, codes, start, n, row, bits, static_cast<cudaStream_t>(stream)),
-                     "map_fill launch");
+  return note_write(stream, kWroteMaps,
+                    cuda_status(dkv::launch_map_fill(rows, codes, start, n, row, bits,
+                                                     static_cast<cudaStream_t>(stream)),
+                                "map_fill launch"));
 }
 
 int dkv_rotary(const void* x, const float* cos_t, const float* sin_t, void* out, int64_t xb, int64_t xt,
@@ -474,9 +539,10 @@ int dkv_rotary(const void* x, const float* cos_t, const float* sin_t, void* out,
   if (xb < 0 || xt < static_cast<int64_t>(heads) * dim || xb % 8 || xt % 8)
     return fail(DKV_EINVAL, "rotary: token strides must hold the heads and be multiples of 8 elements");
   if (cb < 0 || cb % 4) return fail(DKV_EINVAL, "rotary: table batch stride must be a multiple of 4");
-  return cuda_status(dkv::launch_rotary(x, cos_t, sin_t, out, xb, xt, cb, b, n, heads,
-                                        static_cast<cudaStream_t>(stream)),
-                     "rotary launch");
+  return note_write(stream, kWroteNothing,
+                    cuda_status(dkv::launch_rotary(x, cos_t, sin_t, out, xb, xt, cb, b, n, heads,
+                                                   static_cast<cudaStream_t>(stream)),
+                                "rotary launch"));
 }
 
 int dkv_silu_mul(const void* gate, const void* up, void* out, int64_t gs, int64_t us, int64_t rows, int32_t width,
@@ -488,8 +554,10 @@ int dkv_silu_mul(const void* gate, const void* up, void* out, int64_t gs, int64_
     return fail(DKV_EINVAL, "silu_mul: tensors must be 16-byte aligned");
   if (gs < width || us < width || gs % 8 || us % 8)
     return fail(DKV_EINVAL, "silu_mul: row strides must hold a row and be multiples of 8 elements");
-  return cuda_status(dkv::launch_silu_mul(gate, up, out, gs, us, rows, width, static_cast<cudaStream_t>(stream)),
-                     "silu_mul launch");
+  return note_write(stream, kWroteNothing,
+                    cuda_status(dkv::launch_silu_mul(gate, up, out, gs, us, rows, width,
+                                                     static_cast<cudaStream_t>(stream)),
+                                "silu_mul launch"));
 }
 
 }  // extern "C"

@@ -111,6 +111,10 @@ struct AttnArgs {
   float2* ws_ml;  // [heads * mblocks][cta_rows][even(splits)] (running max in log2 units, sum)
   uint32_t* sync;  // [2][kSyncGroups] arrival / departure counters of the in-kernel merge
   int fused;       // 1: the attention kernel merges the splits itself (no combine launch)
+  // 1: the launch just before this one on the stream may have written history rows
+  // of this layer or the token maps, so the history is read only after
+  // griddepcontrol.wait; 0: it is streamed while the previous kernel finishes.
+  int hist_wait;
   // Fused pack of the call's new K/V rows into the pools (append + attend in one
   // launch; tensor-core kernel only): 0 none, 1 every chunk's frame into `pack`,
   // 2 chunk c's frame into pack_table[c] (device memory).

@@ -404,7 +404,6 @@ attention_tc_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ 
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + kOffTmem);
-  pdl_trigger();  // the combine grid may be scheduled now; it waits for our completion
 
   if (warp == kSWarp) {
     // ================= S = Q K^T issuer =================
@@ -526,6 +525,7 @@ attention_tc_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ 
     };
 
     const int lw = load_index(warp);  // this warp's tiles: lw, lw + 2, ...
+    if (a.hist_wait) pdl_wait();      // the previous launch may have written history rows or maps
     if (lane == 0) {
       for (int t = lw; t < kMapStages && t < ntiles; t += kLoadWarps) map_tile(t);
     }
@@ -999,6 +999,10 @@ attention_tc_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ 
 
   tc_fence_before();
   __syncthreads();
+  // Every thread is now ordered after the softmax warps' griddepcontrol.wait: only
+  // now may the dependent grid be scheduled, so that when it starts, every kernel
+  // before this one has completed.
+  pdl_trigger();
   if (warp == kSWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);

@@ -54,8 +54,8 @@ __device__ __forceinline__ void store8(uint16_t* p, const float* y) {
 __global__ void __launch_bounds__(kOpThreads)
 rotary_kernel(const uint16_t* __restrict__ x, const float* __restrict__ cos_t, const float* __restrict__ sin_t,
               uint16_t* __restrict__ out, int64_t xb, int64_t xt, int64_t cb, int n, int heads, int64_t total) {
-  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
   asm volatile("griddepcontrol.wait;\n" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
   const int64_t gtid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (gtid >= total) return;
   const int part = static_cast<int>(gtid & 3);
@@ -90,8 +90,8 @@ rotary_kernel(const uint16_t* __restrict__ x, const float* __restrict__ cos_t, c
 __global__ void __launch_bounds__(kOpThreads)
 silu_mul_kernel(const uint16_t* __restrict__ gate, const uint16_t* __restrict__ up, uint16_t* __restrict__ out,
                 int64_t gs, int64_t us, int width, int64_t total) {
-  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
   asm volatile("griddepcontrol.wait;\n" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
   const int64_t gtid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (gtid >= total) return;
   const int chunks = width / 8;
@@ -111,8 +111,9 @@ silu_mul_kernel(const uint16_t* __restrict__ gate, const uint16_t* __restrict__ 
 namespace {
 
 // Launched as a programmatic dependent, like the pack kernel: each kernel waits
-// (griddepcontrol.wait) before its first read, and lets its own dependent (the
-// attention kernel after the rotary) start its set-up early.
+// (griddepcontrol.wait) before its first read and only then lets its own
+// dependent (the attention kernel after the rotary) start its set-up, so the
+// dependent knows every kernel before this one has completed.
 template <class Kernel, class... Args>
 cudaError_t launch_pdl(int64_t threads, cudaStream_t stream, Kernel kernel, Args... args) {
   cudaLaunchConfig_t cfg = {};

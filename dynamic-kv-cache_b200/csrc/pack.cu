@@ -22,11 +22,12 @@ pack_rows_kernel(const uint16_t* __restrict__ k, const uint16_t* __restrict__ v,
                  float2* __restrict__ m8, uint16_t* __restrict__ p16, int64_t kh, int64_t kt,
                  int64_t vh, int64_t vt, int layer, int64_t row_start, int n, int64_t cap,
                  int heads, int32_t* status) {
-  // Launched as a programmatic dependent: the next kernel (the frame's attention,
-  // which reads the new K/V natively and only history rows of the pools) may start
-  // streaming history at once; k / v are the previous kernels' output.
-  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+  // Launched as a programmatic dependent; k / v are the previous kernels' output.
+  // The dependents are released only after this grid's own wait: once any kernel
+  // of this library has released its dependent, every kernel launched before it
+  // has completed, so a dependent may read their results before its own wait.
   asm volatile("griddepcontrol.wait;\n" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
   const int gtid = blockIdx.x * blockDim.x + threadIdx.x;
   const int row = gtid >> 3;
   const int part = gtid & 7;
@@ -66,8 +67,8 @@ __global__ void __launch_bounds__(kPackThreads)
 pack_rows_many_kernel(const uint16_t* __restrict__ k, const uint16_t* __restrict__ v,
                       const __grid_constant__ Targets tab, int64_t kh, int64_t kt, int64_t vh, int64_t vt,
                       int64_t kc, int64_t vc, int layer, int n, int heads) {
-  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
   asm volatile("griddepcontrol.wait;\n" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
   const dkv_pack_target& d = tab[blockIdx.y];
   if (!pack_target_ok(d, n)) {
     if (blockIdx.x == 0 && threadIdx.x == 0) report_bad_target(d, n, blockIdx.y);

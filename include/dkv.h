@@ -170,7 +170,9 @@ int32_t dkv_packed_attention_launches(int32_t past, int32_t nq, int32_t heads,
  * overlap on one GPU (e.g. on two streams) race and must be serialised. Nothing
  * in it needs clearing between calls. The first call on each device looks the
  * array's device address up (cudaGetSymbolAddress); make that first call before
- * any stream capture. Shapes needing more scratch than the array holds return
+ * any stream capture. The address is kept for the life of the process, so calls
+ * must not span a cudaDeviceReset (which unloads the library's device image and
+ * may move the array). Shapes needing more scratch than the array holds return
  * DKV_EWORKSPACE (the planner never asks for more).
  */
 int dkv_packed_attention_noalloc(const void* q, const void* knew, const void* vnew,

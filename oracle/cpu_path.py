@@ -8,8 +8,10 @@ mask and GQA expansion follow the reference's own checks
 visible to query m iff t <= past + m, KV heads repeated `group` times.
 
 Used as (1) the attention oracle of the parity tests and (2) the timed CPU
-baseline of bench.py (kind "port": the reference's path on the host cores).
+baseline of bench.py (kind "port": the reference's path on the host cores;
+cpu_cache_update is the whole per-call update, the current frame's pack included).
 """
+import numpy as np
 import torch
 import torch.nn.functional as F
 
@@ -59,3 +61,17 @@ def cpu_cache_attention(frames, q, knew, vnew, round_history_bf16=False):
     if round_history_bf16:
         hist_k, hist_v = hist_k.bfloat16().float(), hist_v.bfloat16().float()
     return reference_attention(q, hist_k, hist_v, knew, vnew)
+
+
+def cpu_cache_update(frames, q, knew, vnew, bits):
+    """One layer's call of the reference CPU cache path in full, as
+    MixedPrecisionCache.update (src/cache_manager.py:43-63) and the attention
+    after it run it: dequantise every stored frame, pack the current frame's K and
+    V at `bits` (the compressed copy the next call reads; its result does not enter
+    this call's output), concatenate with the native current frame and attend.
+    knew / vnew are float32 tensors, packed as the reference packs float32 inputs.
+    Returns (attention output [1, n, HQ, D], (K Packed, V Packed) of the frame)."""
+    out = cpu_cache_attention(frames, q, knew, vnew)
+    packed = (kvq.pack(knew.contiguous().numpy().astype(np.float32), bits, dtype='float32'),
+              kvq.pack(vnew.contiguous().numpy().astype(np.float32), bits, dtype='float32'))
+    return out, packed

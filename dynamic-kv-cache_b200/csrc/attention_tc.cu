@@ -1161,11 +1161,16 @@ cudaError_t launch_attention_tc(AttnArgs& a, int heads, cudaStream_t stream, con
   cfg.blockDim = dim3(kThreadsTc);
   cfg.dynamicSmemBytes = kSmemTc;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // overlap our set-up and
   attr[0].val.programmaticStreamSerializationAllowed = 1;          // history streaming with the
   cfg.attrs = attr;                                                 // previous kernel's tail
   cfg.numAttrs = 1;
+  if (a.fused) {  // the in-kernel merge waits for every block of its group: have them co-scheduled
+    attr[1].id = cudaLaunchAttributeCooperative;
+    attr[1].val.cooperative = 1;
+    cfg.numAttrs = 2;
+  }
   if (table != nullptr) return cudaLaunchKernelEx(&cfg, attention_tc_kernel<HistoryTable>, a, *table);
   if (device_table != nullptr)
     return cudaLaunchKernelEx(&cfg, attention_tc_kernel<DeviceHistories>, a, DeviceHistories{device_table});

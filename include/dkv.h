@@ -96,7 +96,9 @@ int dkv_pack_rows(const void* k, const void* v,
  *
  * When every block of the launch fits on the GPU at once (one block per SM, at
  * most 148 blocks) the history splits are merged inside the attention kernel:
- * one launch per call. Otherwise, or with the environment variable
+ * one launch per call, made as a cooperative launch so that all its blocks are
+ * co-scheduled (each waits for the others of its group; work on other streams
+ * only delays the launch). Otherwise, or with the environment variable
  * DKV_ATTENTION_MERGE=combine (e.g. under MPS, where a grid may not be resident
  * at once), a second kernel merges them. Both merges do the same arithmetic in
  * the same order: the output is bit-identical either way.

@@ -176,11 +176,13 @@ size_t dkv_packed_attention_workspace(int32_t past, int32_t nq, int32_t heads, i
 size_t dkv_packed_attention_batched_workspace(int32_t past, int32_t nq, int32_t heads, int32_t group, int32_t dim,
                                               int32_t chunks) {
   if (past < 0 || nq <= 0 || heads <= 0 || group <= 0 || dim != dkv::kDim || chunks <= 0) return 0;
+  if (static_cast<int64_t>(group) * nq <= dkv::kSplitRows) return 0;  // split-K kernel: merges in its clusters
   return dkv::make_plan(past, nq, heads, group, chunks).workspace_bytes();
 }
 
 int32_t dkv_packed_attention_launches(int32_t past, int32_t nq, int32_t heads, int32_t group, int32_t dim) {
   if (past < 0 || nq <= 0 || heads <= 0 || group <= 0 || dim != dkv::kDim) return 0;
+  if (static_cast<int64_t>(group) * nq <= dkv::kSplitRows) return 1;  // split-K kernel
   const dkv::AttnPlan p = dkv::make_plan(past, nq, heads, group);
   if (p.splits == 1) return 1;
   bool fused = false;
@@ -200,7 +202,7 @@ int launch_planned(dkv::AttnArgs& a, const dkv::AttnPlan& p, const void* q, cons
                    int64_t qc, int64_t kc, int64_t vc, int64_t oc, int32_t layer, int32_t nq, int32_t heads,
                    int32_t group, void* workspace, void* stream, const dkv::HistoryTable* table,
                    const dkv_history* device_table = nullptr, const dkv_pack_target* pack = nullptr,
-                   bool pack_on_device = false) {
+                   bool pack_on_device = false, bool split = false) {
   a.q = static_cast<const uint16_t*>(q);
   a.knew = static_cast<const uint16_t*>(knew);
   a.vnew = static_cast<const uint16_t*>(vnew);
@@ -217,7 +219,7 @@ int launch_planned(dkv::AttnArgs& a, const dkv::AttnPlan& p, const void* q, cons
   a.mblocks = p.mblocks;
   a.splits = p.splits;
   a.chunk = p.chunk;
-  if (p.workspace_bytes() > 0) {  // [merge counters][partial outputs][partial (max, sum)]
+  if (!split && p.workspace_bytes() > 0) {  // [merge counters][partial outputs][partial (max, sum)]
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     a.sync = reinterpret_cast<uint32_t*>(ws);
     a.ws_o = reinterpret_cast<float*>(ws + dkv::kSyncBytes);
@@ -237,8 +239,8 @@ int launch_planned(dkv::AttnArgs& a, const dkv::AttnPlan& p, const void* q, cons
     }
   }
   a.hist_wait = history_may_be_fresh(stream, layer) ? 1 : 0;
-  cudaError_t e = dkv::launch_attention_tc(a, zdim, st, table, device_table);
-  const bool combine = p.splits > 1 && !a.fused;
+  cudaError_t e = split ? dkv::launch_attention_split(a, zdim, st) : dkv::launch_attention_tc(a, zdim, st, table, device_table);
+  const bool combine = !split && p.splits > 1 && !a.fused;
   if (e == cudaSuccess && combine) e = dkv::launch_attention_combine(a, zdim, st);
   // A fused pack runs after the attention kernel has released its dependents; a
   // combine launch after it completes it first.
@@ -271,8 +273,11 @@ int attention_impl(const void* q, const void* knew, const void* vnew, const void
   if (!rows_aligned(q, qh, qt) || !rows_aligned(knew, kh, kt) || !rows_aligned(vnew, vh, vt))
     return fail(DKV_EINVAL, "q/k/v rows must be 16-byte aligned (head/token strides multiples of 8)");
   if (out == nullptr || !aligned16(out)) return fail(DKV_EINVAL, "out must be 16-byte aligned");
-  const dkv::AttnPlan p = dkv::make_plan(past, nq, heads, group, chunks);
-  const size_t need = p.workspace_bytes();
+  // short chunks (decode steps, small candidate chunks) take the split-K kernel
+  const bool split = static_cast<int64_t>(group) * nq <= dkv::kSplitRows;
+  const dkv::AttnPlan p = split ? dkv::make_plan_split(past, nq, heads, group, chunks)
+                                : dkv::make_plan(past, nq, heads, group, chunks);
+  const size_t need = split ? 0 : p.workspace_bytes();
   if (need > 0 && (workspace == nullptr || workspace_bytes < need))
     return fail(DKV_EWORKSPACE, "attention workspace needs %zu bytes, got %zu", need, workspace_bytes);
   if (need > 0 && (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
@@ -280,7 +285,7 @@ int attention_impl(const void* q, const void* knew, const void* vnew, const void
   dkv::AttnArgs a{};
   a.hist = dkv_history{p4, m4, p8, m8, p16, rows, codes, cap4, cap8, cap16, past, past, status};
   return launch_planned(a, p, q, knew, vnew, out, qh, qt, kh, kt, vh, vt, chunks, qc, kc, vc, oc, layer, nq, heads,
-                        group, workspace, stream, nullptr, nullptr, pack, false);
+                        group, workspace, stream, nullptr, nullptr, pack, false, split);
 }
 
 }  // namespace

@@ -58,6 +58,31 @@ inline AttnPlan make_plan(int past, int nq, int heads, int group, int chunks = 1
   return p;
 }
 
+// Short query chunks (at most kSplitRows stacked rows per KV head: decode steps,
+// small candidate chunks) run on the split-K kernel: one CTA of four warps per
+// (chunk, KV head, split), up to 16 splits per group forming one cluster, each
+// split a multiple of 32 keys and at least one 32-key tile per warp, no more CTAs
+// than two per SM. No workspace: the splits merge inside their cluster.
+constexpr int kSplitRows = 16;
+constexpr int kSplitKeys = 32;
+inline AttnPlan make_plan_split(int past, int nq, int heads, int group, int chunks = 1) {
+  AttnPlan p{};
+  p.mrows = group * nq;
+  p.cta_rows = kSplitRows;
+  p.mblocks = 1;
+  const int groups = heads * chunks;
+  const int tiles = (past + nq + kSplitKeys - 1) / kSplitKeys;
+  int s = (tiles + 3) / 4;
+  if (s > 16) s = 16;
+  const int cap = 2 * kTargetCtas / groups;
+  if (s > cap) s = cap;
+  if (s < 1) s = 1;
+  const int per = (tiles + s - 1) / s;
+  p.chunk = per * kSplitKeys;
+  p.splits = (tiles + per - 1) / per;
+  return p;  // no workspace
+}
+
 // Plan of a call over `count` independent requests whose histories are at most
 // max_past tokens: as many splits as fill one wave (never more than the longest
 // history has tiles), and each request divides its own history evenly among them
@@ -213,5 +238,7 @@ cudaError_t launch_attention_tc(AttnArgs& a, int heads, cudaStream_t stream, con
 // on the current device (one launch) or needs the combine kernel (two).
 cudaError_t attention_tc_merges_in_kernel(const AttnPlan& p, int heads, bool* fused);
 cudaError_t launch_attention_combine(const AttnArgs& a, int heads, cudaStream_t stream);
+// The split-K kernel for plans of make_plan_split (a.hist holds the history).
+cudaError_t launch_attention_split(const AttnArgs& a, int heads, cudaStream_t stream);
 
 }  // namespace dkv

@@ -18,9 +18,23 @@ import torch.nn.functional as F
 from . import kvq
 
 
-def unpack_torch(packed, dtype=torch.float32):
+def unpack_torch(packed, dtype=torch.float32, memo=False):
     """torch restatement of unpack: 16-bit payloads are reinterpreted; 4/8-bit codes
-    are dequantised as q * scale + offset in fp32, then cast to `dtype`."""
+    are dequantised as q * scale + offset in fp32, then cast to `dtype`. memo=True
+    (the oracle decoder, never the timed baseline, which must pay every unpack as
+    the reference does) keeps the fp32 result on the Packed object, so a stored
+    segment is unpacked once however many later calls read it."""
+    if not memo:
+        return _unpack_torch(packed).to(dtype)
+    cached = getattr(packed, '_unpacked', None)
+    if cached is None:
+        cached = _unpack_torch(packed)
+        packed._unpacked = cached
+    return cached.to(dtype)
+
+
+def _unpack_torch(packed):
+    dtype = torch.float32
     bits, code, shape, group, numel, groups = packed.fields()
     payload = torch.from_numpy(packed.payload)
     if bits == 16:
@@ -47,13 +61,13 @@ def reference_attention(q, hist_k, hist_v, knew, vnew):
     return out.transpose(1, 2)
 
 
-def cpu_cache_attention(frames, q, knew, vnew, round_history_bf16=False):
+def cpu_cache_attention(frames, q, knew, vnew, round_history_bf16=False, memo=False):
     """The reference CPU path for one layer: `frames` is a list of (K Packed,
     V Packed) per stored frame; dequantise all, append the native current frame
     and attend. round_history_bf16 mimics dequantised history held in bf16, as
-    the GPU kernel's tiles are (src/gpu_kernels.py:93-94)."""
-    ks = [unpack_torch(k) for k, _ in frames]
-    vs = [unpack_torch(v) for _, v in frames]
+    the GPU kernel's tiles are (src/gpu_kernels.py:93-94); memo as unpack_torch."""
+    ks = [unpack_torch(k, memo=memo) for k, _ in frames]
+    vs = [unpack_torch(v, memo=memo) for _, v in frames]
     if not ks:
         empty = torch.zeros(1, knew.shape[1], 0, knew.shape[3])
         ks, vs = [empty], [empty]

@@ -32,10 +32,14 @@ def _bf(x):
 
 
 class OracleDecoder:
-    def __init__(self, cfg, params):
+    def __init__(self, cfg, params, memo=False):
         """params: dict name -> tensor (embed, qkv[i], o[i], gate_up[i], down[i],
-        norm_attn[i], norm_mlp[i], norm_out), any dtype/device."""
+        norm_attn[i], norm_mlp[i], norm_out), any dtype/device. memo=True keeps
+        each stored segment's unpacked values after its first use (parity tests at
+        full model shape); the timed CPU baseline leaves it off and unpacks the
+        whole history on every call, as the reference does."""
         self.cfg = cfg
+        self.memo = memo
         self.p = {k: v.detach().float().cpu() for k, v in params.items()}
 
     def _rms(self, x, w):
@@ -66,7 +70,7 @@ class OracleDecoder:
             q = _bf(self._rot(q.view(1, n, c.q_heads, c.head_dim).transpose(1, 2), cos, sin))
             k = _bf(self._rot(k.view(1, n, c.kv_heads, c.head_dim).transpose(1, 2), cos, sin))
             v = v.view(1, n, c.kv_heads, c.head_dim).transpose(1, 2)
-            out = _bf(cpu_path.cpu_cache_attention(history[layer], q, k, v))  # [1, n, q_heads, d]
+            out = _bf(cpu_path.cpu_cache_attention(history[layer], q, k, v, memo=self.memo))  # [1, n, q_heads, d]
             if store_bits is not None:
                 history[layer].append((kvq.pack(_bits(k), store_bits), kvq.pack(_bits(v), store_bits)))
             x = _bf(x + _bf(F.linear(out.reshape(1, n, -1), self.p[f'o.{layer}'])))

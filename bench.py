@@ -54,7 +54,10 @@ METRIC = 'packed-KV attention HBM GB/s at 8K ctx'
 # seed 0), from an ncu --set full capture of `bench.py --layers 2` (one launch of the
 # timed sweep, after warm-up). It is a recorded figure, not measured by this run: a
 # kernel change is re-captured and this constant updated with it.
-NCU_TRAFFIC_BYTES = 5_805_056
+NCU_TRAFFIC_BYTES = 5_804_800
+# The same for one attention_split_kernel launch of the decode shape (one query after
+# the same 8128 tokens), from the matching capture with -k regex:attention_split.
+NCU_DECODE_TRAFFIC_BYTES = 5_585_408
 WORKLOAD = 'C3 frame-append attention, 8K ctx, 32-layer cache'
 
 
@@ -91,19 +94,26 @@ def frame_plan(seed, past=None):
     return list(zip(bits, sizes))
 
 
-def attention_bytes(plan):
+def attention_bytes(plan, nq=None):
     """Algorithmic HBM bytes of one attention call: each history row once (codes +
     metadata), the 5-byte token map entry per history token, Q and the output
     once, the native new K/V once."""
+    nq = NQ if nq is None else nq
     hist = sum(2 * HEADS * n * ROW_BYTES[b] for b, n in plan)
     maps = 5 * sum(n for _, n in plan)
-    q_out = 2 * NQ * HEADS * GROUP * DIM * 2
-    new_kv = 2 * NQ * HEADS * DIM * 2
+    q_out = 2 * nq * HEADS * GROUP * DIM * 2
+    new_kv = 2 * nq * HEADS * DIM * 2
     return hist + maps + q_out + new_kv
 
 
-def attention_flops():
-    return 4 * HEADS * GROUP * DIM * (NQ * PAST + NQ * (NQ + 1) // 2)
+def attention_flops(nq=None):
+    nq = NQ if nq is None else nq
+    return 4 * HEADS * GROUP * DIM * (nq * PAST + nq * (nq + 1) // 2)
+
+
+def attention_exps(nq=None):
+    """Exponentials of one call: one per visible (query row, key) pair."""
+    return attention_flops(nq) // (4 * DIM)
 
 
 def pack_bytes(bits):
@@ -721,6 +731,10 @@ def main():
     hbm, tflops, peak_kind = measured_peaks()
     achieved = bytes_call / (us_call * 1e-6) / 1e9
     achieved_tf = attention_flops() / (us_call * 1e-6) / 1e12
+    sm_mhz = clock.get('sm_mhz') or 1965.0
+    mufu_peak = 16 * torch.cuda.get_device_properties(device).multi_processor_count * sm_mhz * 1e6 / 1e12  # T ex2/s
+    achieved_ex = attention_exps() / (us_call * 1e-6) / 1e12
+    decode_bytes = attention_bytes(plan, nq=1)
     line = {
         'metric': METRIC, 'value': value, 'unit': 'GB/s', 'n_gpus': world, 'steps': args.steps,
         'warmup': args.warmup, 'ms_per_step': ms_step, 'higher_is_better': True, 'scaling': 'weak',
@@ -733,6 +747,10 @@ def main():
                    'requests': f'one independent request per rank (seed 1000+rank)', 'parallelism': f'dp{world}'},
         'us_per_layer_call': us_call,
         'decode_us_per_layer_call': decode_us,
+        'decode': {'us_per_layer_call': decode_us, 'GB_per_s': decode_bytes / (decode_us * 1e-6) / 1e9,
+                   'hbm_frac': decode_bytes / (decode_us * 1e-6) / 1e9 / hbm, 'bytes_per_call': decode_bytes,
+                   'traffic': NCU_DECODE_TRAFFIC_BYTES,
+                   'kernel': 'attention_split_kernel (split-K, mma.sync, cluster merge; 3 stacked rows per KV head)'},
         'frame_append_tokens_per_s': fa_tokens_s,
         'frame_append_ms_per_frame': fa_ms_step,
         'e2e': {'value': e2e_value, 'unit': 'GB/s', 'h2d_bytes_per_step': h2d, 'd2h_bytes_per_step': d2h,
@@ -741,10 +759,16 @@ def main():
                                               'outputs copied back to pinned host memory'},
         'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': hbm, 'unit': 'GB/s', 'frac': achieved / hbm,
                      'traffic': NCU_TRAFFIC_BYTES, 'peak_kind': peak_kind,
-                     'bytes_per_launch': bytes_call, 'note': 'attention op per layer call (tensor-core kernel with in-kernel split merge)'},
+                     'bytes_per_launch': bytes_call,
+                     'note': 'attention op per layer call: attention_tc_kernel (tcgen05 / TMEM), history splits merged '
+                             'in the same cooperative launch'},
         'roofline_tensor': {'bound': 'tensor', 'achieved': achieved_tf, 'peak': tflops, 'unit': 'TFLOP/s',
                             'frac': achieved_tf / tflops, 'peak_kind': peak_kind,
                             'flops_per_launch': attention_flops()},
+        'roofline_mufu': {'bound': 'mufu', 'achieved': achieved_ex, 'peak': mufu_peak, 'unit': 'T ex2/s',
+                          'frac': achieved_ex / mufu_peak, 'exps_per_launch': attention_exps(),
+                          'note': 'every exponential on MUFU ex2 at 16 per clock per SM at the sampled SM clock; '
+                                  'the kernel moves one pair in four to the FMA pipes'},
         'gpu_launches': args.steps * LAYERS * launches_per_call,
         'clocks': clock,
     }

@@ -14,7 +14,7 @@ CSRC = HERE / 'csrc'
 INCLUDE = HERE.parent / 'include'
 LIB = HERE / 'libdkv.so'
 SOURCES = ['api.cu', 'pack.cu', 'attention_combine.cu', 'attention_tc.cu', 'attention_split.cu',
-           'attention_noalloc.cu', 'decoder_ops.cu']
+           'attention_noalloc.cu', 'decoder_ops.cu', 'pool.cu']
 NVCC_FLAGS = ['-O3', '-std=c++17', '-gencode', 'arch=compute_100a,code=sm_100a', '-lineinfo',
               '-Xcompiler', '-fPIC', '-shared', '-Xptxas', '-warn-spills']
 

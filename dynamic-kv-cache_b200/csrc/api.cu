@@ -14,7 +14,7 @@
 namespace dkv {
 cudaError_t launch_pack(const void* k, const void* v, void* p4, void* m4, void* p8, void* m8,
                         void* p16, int64_t kh, int64_t kt, int64_t vh, int64_t vt, int layer,
-                        int64_t row_start, int n, int64_t cap, int heads, int bits,
+                        int64_t row_start, int n, int blocks, int heads, int bits,
                         int32_t* status, cudaStream_t stream);
 cudaError_t launch_reconstruct(const Pools& P, const int32_t* rows, const uint8_t* codes, void* out,
                                int layer, int n, int32_t* status, cudaStream_t stream);
@@ -26,7 +26,7 @@ cudaError_t launch_silu_mul(const void* gate, const void* up, void* out, int64_t
                             int width, cudaStream_t stream);
 cudaError_t launch_pack_many(const void* k, const void* v, const dkv_pack_target* targets, bool on_device, int count,
                              int64_t kh, int64_t kt, int64_t vh, int64_t vt, int64_t kc, int64_t vc, int layer, int n,
-                             int heads, cudaStream_t stream);
+                             int heads, int blocks, cudaStream_t stream);
 }  // namespace dkv
 
 // The request descriptors cross the C ABI by layout: keep it fixed (the Python
@@ -71,6 +71,7 @@ bool rows_aligned(const void* p, int64_t hs, int64_t ts) {
 int check_geometry(int32_t heads, int32_t dim, int32_t layers, int32_t layer) {
   if (dim != dkv::kDim) return fail(DKV_EINVAL, "GPU kernel currently supports head_dim=64");
   if (heads <= 0 || layers <= 0) return fail(DKV_EINVAL, "heads and layers must be positive");
+  if (static_cast<int64_t>(layers) * 2 * heads > (1 << 24)) return fail(DKV_EINVAL, "too many layers x heads");
   if (layer < 0 || layer >= layers) return fail(DKV_EINVAL, "layer %d outside [0, %d)", layer, layers);
   return DKV_OK;
 }
@@ -90,6 +91,14 @@ int check_pools(const void* p4, const void* m4, const void* p8, const void* m8, 
 
 namespace dkv {
 int set_last_error(int code, const char* message) { return fail(code, "%s", message); }
+int api_fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_error, sizeof(g_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+int api_ok() { return ok(); }
 }  // namespace dkv
 
 namespace {
@@ -165,7 +174,8 @@ int dkv_pack_rows(const void* k, const void* v, void* p4, void* m4, void* p8, vo
   if (2LL * heads * n * 8 > INT32_MAX) return fail(DKV_EINVAL, "frame too large");
   return note_write(stream, layer,
                     cuda_status(dkv::launch_pack(k, v, p4, m4, p8, m8, p16, kh, kt, vh, vt, layer, row_start, n,
-                                                 cap, heads, bits, status, static_cast<cudaStream_t>(stream)),
+                                                 layers * 2 * heads, heads, bits, status,
+                                                 static_cast<cudaStream_t>(stream)),
                                 "pack_rows launch"));
 }
 
@@ -200,7 +210,7 @@ namespace {
 int launch_planned(dkv::AttnArgs& a, const dkv::AttnPlan& p, const void* q, const void* knew, const void* vnew,
                    void* out, int64_t qh, int64_t qt, int64_t kh, int64_t kt, int64_t vh, int64_t vt, int32_t chunks,
                    int64_t qc, int64_t kc, int64_t vc, int64_t oc, int32_t layer, int32_t nq, int32_t heads,
-                   int32_t group, void* workspace, void* stream, const dkv::HistoryTable* table,
+                   int32_t group, int32_t layers, void* workspace, void* stream, const dkv::HistoryTable* table,
                    const dkv_history* device_table = nullptr, const dkv_pack_target* pack = nullptr,
                    bool pack_on_device = false, bool split = false) {
   a.q = static_cast<const uint16_t*>(q);
@@ -214,6 +224,7 @@ int launch_planned(dkv::AttnArgs& a, const dkv::AttnPlan& p, const void* q, cons
   a.heads = heads;
   a.G = group;
   a.HQ = heads * group;
+  a.blocks = layers * 2 * heads;
   a.mrows = p.mrows;
   a.cta_rows = p.cta_rows;
   a.mblocks = p.mblocks;
@@ -285,7 +296,7 @@ int attention_impl(const void* q, const void* knew, const void* vnew, const void
   dkv::AttnArgs a{};
   a.hist = dkv_history{p4, m4, p8, m8, p16, rows, codes, cap4, cap8, cap16, past, past, status};
   return launch_planned(a, p, q, knew, vnew, out, qh, qt, kh, kt, vh, vt, chunks, qc, kc, vc, oc, layer, nq, heads,
-                        group, workspace, stream, nullptr, nullptr, pack, false, split);
+                        group, layers, workspace, stream, nullptr, nullptr, pack, false, split);
 }
 
 }  // namespace
@@ -347,7 +358,7 @@ int dkv_pack_rows_many(const void* k, const void* v, const dkv_pack_target* targ
   for (int r = 0; r < count; ++r) maps = maps || targets[r].map_rows != nullptr;
   return note_write(stream, maps ? kWroteMaps : layer,
                     cuda_status(dkv::launch_pack_many(k, v, targets, false, count, kh, kt, vh, vt, kc, vc, layer, n,
-                                                      heads, static_cast<cudaStream_t>(stream)),
+                                                      heads, layers * 2 * heads, static_cast<cudaStream_t>(stream)),
                                 "pack_rows_many launch"));
 }
 
@@ -365,7 +376,7 @@ int dkv_pack_rows_many_device(const void* k, const void* v, const dkv_pack_targe
   if (n == 0) return ok();
   return note_write(stream, kWroteMaps,  // device targets may update the maps
                     cuda_status(dkv::launch_pack_many(k, v, targets, true, count, kh, kt, vh, vt, kc, vc, layer, n,
-                                                      heads, static_cast<cudaStream_t>(stream)),
+                                                      heads, layers * 2 * heads, static_cast<cudaStream_t>(stream)),
                                 "pack_rows_many_device launch"));
 }
 
@@ -381,7 +392,7 @@ static int attention_many_launch(const void* q, const void* knew, const void* vn
                           const dkv_history* device_table, int32_t count, int32_t max_past, void* out, int64_t qh,
                           int64_t qt, int64_t kh, int64_t kt, int64_t vh, int64_t vt, int64_t qc, int64_t kc,
                           int64_t vc, int64_t oc, int32_t layer, int32_t nq, int32_t heads, int32_t group,
-                          void* workspace, size_t workspace_bytes, void* stream,
+                          int32_t layers, void* workspace, size_t workspace_bytes, void* stream,
                           const dkv_pack_target* device_pack = nullptr) {
   if (nq == 0) return ok();
   if (!rows_aligned(q, qh, qt) || !rows_aligned(knew, kh, kt) || !rows_aligned(vnew, vh, vt))
@@ -397,7 +408,7 @@ static int attention_many_launch(const void* q, const void* knew, const void* vn
   if (2LL * heads * nq * 8 > INT32_MAX) return fail(DKV_EINVAL, "frame too large");
   dkv::AttnArgs a{};
   return launch_planned(a, p, q, knew, vnew, out, qh, qt, kh, kt, vh, vt, count, qc, kc, vc, oc, layer, nq, heads,
-                        group, workspace, stream, table, device_table, device_pack, device_pack != nullptr);
+                        group, layers, workspace, stream, table, device_table, device_pack, device_pack != nullptr);
 }
 
 int dkv_packed_attention_many(const void* q, const void* knew, const void* vnew, const dkv_history* requests,
@@ -429,7 +440,7 @@ int dkv_packed_attention_many(const void* q, const void* knew, const void* vnew,
     max_past = h.past > max_past ? h.past : max_past;
   }
   return attention_many_launch(q, knew, vnew, &table, nullptr, count, max_past, out, qh, qt, kh, kt, vh, vt, qc, kc,
-                               vc, oc, layer, nq, heads, group, workspace, workspace_bytes, stream);
+                               vc, oc, layer, nq, heads, group, layers, workspace, workspace_bytes, stream);
 }
 
 int dkv_packed_attention_many_device(const void* q, const void* knew, const void* vnew, const dkv_history* requests,
@@ -448,7 +459,7 @@ int dkv_packed_attention_many_device(const void* q, const void* knew, const void
   if ((qc % 8) || (kc % 8) || (vc % 8) || (oc % 8))
     return fail(DKV_EINVAL, "chunk strides must keep rows 16-byte aligned (multiples of 8 elements)");
   return attention_many_launch(q, knew, vnew, nullptr, requests, count, max_past, out, qh, qt, kh, kt, vh, vt, qc, kc,
-                               vc, oc, layer, nq, heads, group, workspace, workspace_bytes, stream);
+                               vc, oc, layer, nq, heads, group, layers, workspace, workspace_bytes, stream);
 }
 
 int dkv_append_attention(const void* q, const void* knew, const void* vnew, void* p4, void* m4, void* p8, void* m8,
@@ -495,7 +506,7 @@ int dkv_append_attention_many_device(const void* q, const void* knew, const void
   if ((qc % 8) || (kc % 8) || (vc % 8) || (oc % 8))
     return fail(DKV_EINVAL, "chunk strides must keep rows 16-byte aligned (multiples of 8 elements)");
   return attention_many_launch(q, knew, vnew, nullptr, requests, count, max_past, out, qh, qt, kh, kt, vh, vt, qc, kc,
-                               vc, oc, layer, nq, heads, group, workspace, workspace_bytes, stream, targets);
+                               vc, oc, layer, nq, heads, group, layers, workspace, workspace_bytes, stream, targets);
 }
 
 int dkv_reconstruct(const void* p4, const void* m4, const void* p8, const void* m8, const void* p16,
@@ -512,7 +523,7 @@ int dkv_reconstruct(const void* p4, const void* m4, const void* p8, const void* 
   if (2LL * heads * n * 8 > INT32_MAX) return fail(DKV_EINVAL, "history too large");
   dkv::Pools P{static_cast<const uint8_t*>(p4), static_cast<const float2*>(m4),
                static_cast<const uint8_t*>(p8), static_cast<const float2*>(m8),
-               static_cast<const uint16_t*>(p16), cap4, cap8, cap16, heads};
+               static_cast<const uint16_t*>(p16), cap4, cap8, cap16, heads, layers * 2 * heads};
   return note_write(stream, kWroteNothing,
                     cuda_status(dkv::launch_reconstruct(P, rows, codes, out, layer, n, status,
                                                         static_cast<cudaStream_t>(stream)),

@@ -127,6 +127,7 @@ struct AttnArgs {
   uint16_t* out;
   int64_t qh, qt, kh, kt, vh, vt;
   int layer, nq, heads, G, HQ;  // heads: KV heads of one chunk
+  int blocks;                   // layers * 2 * heads: the pools' blocks (page arithmetic, pool_row)
   int mrows, cta_rows, mblocks, splits;
   int chunk;  // keys per split; 0: each request splits its own history evenly (request_chunk)
   // Batched calls: blockIdx.z = chunk * heads + KV head; chunk c's q / knew / vnew /

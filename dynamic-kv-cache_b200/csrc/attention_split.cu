@@ -257,8 +257,8 @@ attention_split_kernel(const __grid_constant__ AttnArgs a, const __grid_constant
         cp_async16_cg(base + kSpRawV + sp_swz(lane, c), vr + c * 8);
       }
     } else if (code == 16) {
-      const uint8_t* kr = p16 + (blk_k * H.cap16 + row) * kRowBytes16;
-      const uint8_t* vr = p16 + (blk_v * H.cap16 + row) * kRowBytes16;
+      const uint8_t* kr = p16 + pool_row(blk_k, row, a.blocks) * kRowBytes16;
+      const uint8_t* vr = p16 + pool_row(blk_v, row, a.blocks) * kRowBytes16;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         cp_async16_cg(base + kSpRawK + sp_swz(lane, c), kr + c * 16);
@@ -266,17 +266,17 @@ attention_split_kernel(const __grid_constant__ AttnArgs a, const __grid_constant
       }
     } else if (code == 8 || code == 4) {
       const int rb = code == 8 ? kRowBytes8 : kRowBytes4;
-      const int64_t cap = code == 8 ? H.cap8 : H.cap4;
       const uint8_t* pool = code == 8 ? p8 : p4;
       const float2* meta = code == 8 ? m8 : m4;
-      const uint8_t* kr = pool + (blk_k * cap + row) * rb;
-      const uint8_t* vr = pool + (blk_v * cap + row) * rb;
+      const int64_t at_k = pool_row(blk_k, row, a.blocks), at_v = pool_row(blk_v, row, a.blocks);
+      const uint8_t* kr = pool + at_k * rb;
+      const uint8_t* vr = pool + at_v * rb;
       for (int c = 0; c < rb / 16; ++c) {
         cp_async16_cg(base + kSpRawK + sp_swz(lane, c), kr + c * 16);
         cp_async16_cg(base + kSpRawV + sp_swz(lane, c), vr + c * 16);
       }
-      cp_async8(base + kSpRawMK + lane * 8, meta + blk_k * cap + row);
-      cp_async8(base + kSpRawMV + lane * 8, meta + blk_v * cap + row);
+      cp_async8(base + kSpRawMK + lane * 8, meta + at_k);
+      cp_async8(base + kSpRawMV + lane * 8, meta + at_v);
     }
   };
 
@@ -445,7 +445,7 @@ attention_split_kernel(const __grid_constant__ AttnArgs a, const __grid_constant
       const uint16_t* v = a.vnew + chunk * a.vc;
       for (int r = split * per + (threadIdx.x >> 3); r < r_end; r += kSpThreads / 8) {  // r: kv * nq + token
         const int kv = r >= a.nq;
-        pack_frame_row(*d, k, v, a.kh, a.kt, a.vh, a.vt, a.layer, a.nq, a.heads, kv, g, r - kv * a.nq,
+        pack_frame_row(*d, k, v, a.kh, a.kt, a.vh, a.vt, a.layer, a.nq, a.heads, a.blocks, kv, g, r - kv * a.nq,
                        threadIdx.x & 7, r);
       }
     }

@@ -463,10 +463,12 @@ attention_tc_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ 
     __syncwarp();
   } else if (is_load_warp(warp)) {
     // ================= loader: token maps and packed runs by TMA =================
-    // Per-CTA block bases (layer, K|V, this head) of every pool, and the parity of
-    // each meta block's first pair index, so the per-tile work is 32-bit math.
+    // The pools are paged (pool_row): the rows of a page of one block are
+    // contiguous, so a run of consecutive rows that stays inside one 64-row page
+    // is one copy; runs are cut at page boundaries below.
     const int64_t blk_k = (static_cast<int64_t>(a.layer) * 2) * a.heads + g;  // (layer, K, head)
     const int64_t blk_v = blk_k + a.heads;                                    // (layer, V, head)
+    const int64_t nblk = a.blocks;
     const int cap4 = static_cast<int>(H.cap4), cap8 = static_cast<int>(H.cap8);
     const int cap16 = static_cast<int>(H.cap16);
     const uint8_t* const p4 = static_cast<const uint8_t*>(H.p4);
@@ -476,24 +478,11 @@ attention_tc_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ 
     const float2* const m8 = static_cast<const float2*>(H.m8);
     const int32_t* const map_rows = H.rows;
     const uint8_t* const map_codes = H.codes;
-    const uint8_t* const pk4 = p4 + blk_k * cap4 * kRowBytes4;
-    const uint8_t* const pv4 = p4 + blk_v * cap4 * kRowBytes4;
-    const uint8_t* const pk8 = p8 + blk_k * cap8 * kRowBytes8;
-    const uint8_t* const pv8 = p8 + blk_v * cap8 * kRowBytes8;
-    const uint8_t* const pk16 = p16 + blk_k * cap16 * kRowBytes16;
-    const uint8_t* const pv16 = p16 + blk_v * cap16 * kRowBytes16;
-    const float2* const mk4 = m4 + blk_k * cap4;
-    const float2* const mv4 = m4 + blk_v * cap4;
-    const float2* const mk8 = m8 + blk_k * cap8;
-    const float2* const mv8 = m8 + blk_v * cap8;
-    const int pbk4 = static_cast<int>((blk_k * cap4) & 1), pbv4 = static_cast<int>((blk_v * cap4) & 1);
-    const int pbk8 = static_cast<int>((blk_k * cap8) & 1), pbv8 = static_cast<int>((blk_v * cap8) & 1);
+    // pool row index of row r of this head's K (kv = 0) or V block
+    auto row_at = [&](int kv, int r) -> int64_t { return pool_row(kv ? blk_v : blk_k, r, nblk); };
     // selectors (no dynamic array indexing: keeps everything in registers)
-    auto pool_of = [&](int code, int kv) -> const uint8_t* {
-      return code == 4 ? (kv ? pv4 : pk4) : (code == 8 ? (kv ? pv8 : pk8) : (kv ? pv16 : pk16));
-    };
-    auto meta_of = [&](int code, int kv) -> const float2* { return code == 4 ? (kv ? mv4 : mk4) : (kv ? mv8 : mk8); };
-    auto mpar_of = [&](int code, int kv) -> int { return code == 4 ? (kv ? pbv4 : pbk4) : (kv ? pbv8 : pbk8); };
+    auto pool_of = [&](int code) -> const uint8_t* { return code == 4 ? p4 : (code == 8 ? p8 : p16); };
+    auto meta_of = [&](int code) -> const float2* { return code == 4 ? m4 : m8; };
     const uint16_t* const knew_g = a.knew + chunk * a.kc + g * a.kh;
     const uint16_t* const vnew_g = a.vnew + chunk * a.vc + g * a.vh;
 
@@ -508,19 +497,19 @@ attention_tc_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ 
       mbar_arrive(bar(B_MAPFULL + slot));
     };
     // (offset, scale) pairs of a run of `cnt` rows from block-relative row r0 for
-    // K (kv = 0) or V: one aligned bulk copy when the 16-byte span stays inside the
-    // block and holds >= 2 rows; returns the pair shift (0/1), or -1 for "caller
-    // stores the pairs with plain loads".
+    // K (kv = 0) or V, the run inside one page: one 16-byte aligned bulk copy of
+    // the even-aligned span around it (a page starts at an even pair index and
+    // holds an even number of rows, so the span stays inside the page) when the
+    // run holds >= 2 rows; returns the pair shift (0/1), or -1 for "caller stores
+    // the pairs with plain loads".
     auto meta_run = [&](int code, int kv, int r0, int cnt, uint32_t dst, uint32_t rbar) -> int {
-      const int cap = code == 4 ? cap4 : cap8;
-      const int pb = mpar_of(code, kv);
-      const int par = pb ^ (r0 & 1);
+      if (cnt < 2) return -1;
+      const int par = r0 & 1;
       const int end = r0 + cnt;
-      const int hi = end + (pb ^ (end & 1));
-      if (cnt < 2 || hi > cap) return -1;
+      const int hi = end + (end & 1);
       const uint32_t bytes = static_cast<uint32_t>(hi - (r0 - par)) * 8u;
       mbar_expect_tx(rbar, bytes);
-      bulk_g2s(dst, meta_of(code, kv) + (r0 - par), bytes, rbar);
+      bulk_g2s(dst, meta_of(code) + row_at(kv, r0 - par), bytes, rbar);
       return par;
     };
 
@@ -576,13 +565,16 @@ attention_tc_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ 
           }
         }
       }
-      // --- runs: a token starts one unless it continues the previous token's pool run ---
+      // --- runs: a token starts one unless it continues the previous token's pool
+      // run inside the same page (the first row of a page always starts a run) ---
       const int pcode = __shfl_up_sync(0xffffffffu, code[1], 1);
       const int prow = __shfl_up_sync(0xffffffffu, row[1], 1);
       const bool pooled0 = code[0] == 4 || code[0] == 8 || code[0] == 16;
       const bool pooled1 = code[1] == 4 || code[1] == 8 || code[1] == 16;
-      const bool start0 = lane == 0 || !pooled0 || pcode != code[0] || prow + 1 != row[0];
-      const bool start1 = !pooled1 || code[0] != code[1] || row[0] + 1 != row[1];
+      const bool start0 =
+          lane == 0 || !pooled0 || pcode != code[0] || prow + 1 != row[0] || (row[0] & (kPageRows - 1)) == 0;
+      const bool start1 =
+          !pooled1 || code[0] != code[1] || row[0] + 1 != row[1] || (row[1] & (kPageRows - 1)) == 0;
       const uint32_t even_starts = __ballot_sync(0xffffffffu, start0);
       const uint32_t odd_starts = __ballot_sync(0xffffffffu, start1);
       const int code0 = __shfl_sync(0xffffffffu, code[0], 0);
@@ -590,14 +582,15 @@ attention_tc_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ 
       const uint32_t sst = sbase + kOffRaw + rs * kRawStage;
       const uint32_t rbar = bar(B_RAWFULL + rs);
       if (even_starts == 1u && odd_starts == 0u && (code0 == 4 || code0 == 8 || code0 == 16)) {
-        // ---- uniform tile: one run of 64 rows, copies from lane 0, no per-token table ----
+        // ---- uniform tile: one run of 64 rows (one whole page), copies from lane 0,
+        // no per-token table ----
         const int rb = row_bytes(code0);
         const int r0 = __shfl_sync(0xffffffffu, row[0], 0);
         int park = 0, parv = 0;
         if (lane == 0) {
           mbar_expect_tx(rbar, 2 * kBN * rb);
-          bulk_g2s(sst + kRawK, pool_of(code0, 0) + static_cast<int64_t>(r0) * rb, kBN * rb, rbar);
-          bulk_g2s(sst + kRawV, pool_of(code0, 1) + static_cast<int64_t>(r0) * rb, kBN * rb, rbar);
+          bulk_g2s(sst + kRawK, pool_of(code0) + row_at(0, r0) * rb, kBN * rb, rbar);
+          bulk_g2s(sst + kRawV, pool_of(code0) + row_at(1, r0) * rb, kBN * rb, rbar);
           if (code0 != 16) {
             park = meta_run(code0, 0, r0, kBN, sst + kRawMetaK, rbar);
             parv = meta_run(code0, 1, r0, kBN, sst + kRawMetaV, rbar);
@@ -605,12 +598,12 @@ attention_tc_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ 
         }
         park = __shfl_sync(0xffffffffu, park, 0);
         parv = __shfl_sync(0xffffffffu, parv, 0);
-        if (code0 != 16 && (park < 0 || parv < 0)) {  // block-final odd run: pairs by plain loads
+        if (code0 != 16 && (park < 0 || parv < 0)) {  // no bulk copy of the pairs: plain loads
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
             const int j = 2 * lane + e;
-            if (park < 0) *reinterpret_cast<float2*>(st + kRawMetaK + j * 8) = __ldg(meta_of(code0, 0) + r0 + j);
-            if (parv < 0) *reinterpret_cast<float2*>(st + kRawMetaV + j * 8) = __ldg(meta_of(code0, 1) + r0 + j);
+            if (park < 0) *reinterpret_cast<float2*>(st + kRawMetaK + j * 8) = __ldg(meta_of(code0) + row_at(0, r0 + j));
+            if (parv < 0) *reinterpret_cast<float2*>(st + kRawMetaV + j * 8) = __ldg(meta_of(code0) + row_at(1, r0 + j));
           }
           park = max(park, 0);
           parv = max(parv, 0);
@@ -659,23 +652,20 @@ attention_tc_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ 
             raw_off = j0 * 128 + (j - j0) * rb;
             if (j == j0) {
               mbar_expect_tx(rbar, 2 * cnt * rb);
-              bulk_g2s(sst + kRawK + j0 * 128, pool_of(cd, 0) + static_cast<int64_t>(r0) * rb, cnt * rb, rbar);
-              bulk_g2s(sst + kRawV + j0 * 128, pool_of(cd, 1) + static_cast<int64_t>(r0) * rb, cnt * rb, rbar);
+              bulk_g2s(sst + kRawK + j0 * 128, pool_of(cd) + row_at(0, r0) * rb, cnt * rb, rbar);
+              bulk_g2s(sst + kRawV + j0 * 128, pool_of(cd) + row_at(1, r0) * rb, cnt * rb, rbar);
             }
             if (cd != 16) {
 #pragma unroll
               for (int kv = 0; kv < 2; ++kv) {
-                const int cap = cd == 4 ? cap4 : cap8;
-                const int pb = mpar_of(cd, kv);
-                const int end = r0 + cnt;
-                const bool bulk = cnt >= 2 && end + (pb ^ (end & 1)) <= cap;
-                const int par = bulk ? (pb ^ (r0 & 1)) : 0;
+                const bool bulk = cnt >= 2;  // the run's pairs by meta_run's one copy
+                const int par = bulk ? (r0 & 1) : 0;
                 moff[kv] = j0 * 16 + (par + (j - j0)) * 8;
                 if (bulk && j == j0) {
                   meta_run(cd, kv, r0, cnt, sst + (kv ? kRawMetaV : kRawMetaK) + j0 * 16, rbar);
-                } else if (!bulk) {  // short or block-final odd run: this token's pair by a plain load
+                } else if (!bulk) {  // a one-row run: this token's pair by a plain load
                   *reinterpret_cast<float2*>(st + (kv ? kRawMetaV : kRawMetaK) + moff[kv]) =
-                      __ldg(meta_of(cd, kv) + row[e]);
+                      __ldg(meta_of(cd) + row_at(kv, row[e]));
                 }
               }
             }
@@ -1029,7 +1019,7 @@ attention_tc_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ 
     const uint16_t* v = a.vnew + pchunk * a.vc;
     for (int r = j * per + (threadIdx.x >> 3); r < r_end; r += kThreadsTc / 8) {  // r: kv * nq + token
       const int kv = r >= a.nq;
-      pack_frame_row(*d, k, v, a.kh, a.kt, a.vh, a.vt, a.layer, a.nq, a.heads, kv, pg, r - kv * a.nq,
+      pack_frame_row(*d, k, v, a.kh, a.kt, a.vh, a.vt, a.layer, a.nq, a.heads, a.blocks, kv, pg, r - kv * a.nq,
                      threadIdx.x & 7, r);
     }
   };

@@ -14,6 +14,16 @@ constexpr int kRowBytes4 = 32;  // packed 4-bit row
 constexpr int kRowBytes8 = 64;  // 8-bit row
 constexpr int kRowBytes16 = 128;
 
+// Pools are paged (dkv.h): row r of block b ((layer, K|V, head): b = (layer * 2 +
+// kv) * heads + head, of `blocks` = layers * 2 * heads) sits in page r / 64, and
+// page p of every block is stored side by side, so growing a pool appends pages
+// and moves no row. Returns the row's index in units of pool rows.
+constexpr int kPageRows = DKV_PAGE_ROWS;
+static_assert(kPageRows == 64, "page arithmetic below assumes 64-row pages");
+__host__ __device__ __forceinline__ int64_t pool_row(int64_t block, int64_t row, int64_t blocks) {
+  return ((row >> 6) * blocks + block) * kPageRows + (row & 63);
+}
+
 // Records the first device-side error. Kernels never trap: they skip the bad
 // access and leave the code for the host to read after a synchronisation.
 __device__ __forceinline__ void report(int32_t* status, int code, int detail) {
@@ -71,6 +81,7 @@ struct Pools {
   const uint16_t* p16;
   int64_t cap4, cap8, cap16;
   int heads;
+  int blocks;  // layers * 2 * heads: pages of the blocks side by side
 };
 
 // Raw bytes + metadata of 8 dims (one eighth) of a history row.
@@ -94,26 +105,27 @@ __device__ __forceinline__ RowPart load_history_part(const Pools& P, const int32
   const int code = codes[t];
   const int64_t row = rows[t];
   const int64_t base = (static_cast<int64_t>(layer) * 2 + kv) * P.heads + head;
+  const int64_t at = row >= 0 ? pool_row(base, row, P.blocks) : 0;  // used only once row is checked
   if (code == 16) {
     if (row < 0 || row >= P.cap16) { report(status, DKV_ECAPACITY, t); return r; }
-    const uint4* src = reinterpret_cast<const uint4*>(P.p16 + (base * P.cap16 + row) * kDim) + part;
+    const uint4* src = reinterpret_cast<const uint4*>(P.p16 + at * kDim) + part;
     r.raw = __ldg(src);
     r.bits = 16;
   } else if (code == 8) {
     if (row < 0 || row >= P.cap8) { report(status, DKV_ECAPACITY, t); return r; }
-    const uint2* src = reinterpret_cast<const uint2*>(P.p8 + (base * P.cap8 + row) * kRowBytes8) + part;
+    const uint2* src = reinterpret_cast<const uint2*>(P.p8 + at * kRowBytes8) + part;
     uint2 w = __ldg(src);
     r.raw.x = w.x;
     r.raw.y = w.y;
-    float2 m = __ldg(P.m8 + base * P.cap8 + row);
+    float2 m = __ldg(P.m8 + at);
     r.offset = m.x;
     r.scale = m.y;
     r.bits = 8;
   } else if (code == 4) {
     if (row < 0 || row >= P.cap4) { report(status, DKV_ECAPACITY, t); return r; }
-    const uint32_t* src = reinterpret_cast<const uint32_t*>(P.p4 + (base * P.cap4 + row) * kRowBytes4) + part;
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(P.p4 + at * kRowBytes4) + part;
     r.raw.x = __ldg(src);
-    float2 m = __ldg(P.m4 + base * P.cap4 + row);
+    float2 m = __ldg(P.m4 + at);
     r.offset = m.x;
     r.scale = m.y;
     r.bits = 4;

@@ -20,7 +20,7 @@ __global__ void __launch_bounds__(kPackThreads)
 pack_rows_kernel(const uint16_t* __restrict__ k, const uint16_t* __restrict__ v,
                  uint8_t* __restrict__ p4, float2* __restrict__ m4, uint8_t* __restrict__ p8,
                  float2* __restrict__ m8, uint16_t* __restrict__ p16, int64_t kh, int64_t kt,
-                 int64_t vh, int64_t vt, int layer, int64_t row_start, int n, int64_t cap,
+                 int64_t vh, int64_t vt, int layer, int64_t row_start, int n, int blocks,
                  int heads, int32_t* status) {
   // Launched as a programmatic dependent; k / v are the previous kernels' output.
   // The dependents are released only after this grid's own wait: once any kernel
@@ -40,7 +40,7 @@ pack_rows_kernel(const uint16_t* __restrict__ k, const uint16_t* __restrict__ v,
   const uint16_t* src = kv == 0 ? k + head * kh + token * kt : v + head * vh + token * vt;
   const uint4 raw = __ldg(reinterpret_cast<const uint4*>(src) + part);
   const int64_t block = (static_cast<int64_t>(layer) * 2 + kv) * heads + head;
-  pack_row_part<BITS>(raw, part, p4, m4, p8, m8, p16, block, cap, row_start + token, status, row);
+  pack_row_part<BITS>(raw, part, p4, m4, p8, m8, p16, pool_row(block, row_start + token, blocks), status, row);
 }
 
 // Per-request destinations of pack_rows_many_kernel: by value in the kernel
@@ -66,7 +66,7 @@ template <class Targets>
 __global__ void __launch_bounds__(kPackThreads)
 pack_rows_many_kernel(const uint16_t* __restrict__ k, const uint16_t* __restrict__ v,
                       const __grid_constant__ Targets tab, int64_t kh, int64_t kt, int64_t vh, int64_t vt,
-                      int64_t kc, int64_t vc, int layer, int n, int heads) {
+                      int64_t kc, int64_t vc, int layer, int n, int heads, int blocks) {
   asm volatile("griddepcontrol.wait;\n" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
   const dkv_pack_target& d = tab[blockIdx.y];
@@ -77,7 +77,8 @@ pack_rows_many_kernel(const uint16_t* __restrict__ k, const uint16_t* __restrict
   const int gtid = blockIdx.x * blockDim.x + threadIdx.x;
   const int row = gtid >> 3;
   if (row >= 2 * heads * n) return;  // whole 8-lane groups leave together
-  pack_target_row(d, k + blockIdx.y * kc, v + blockIdx.y * vc, kh, kt, vh, vt, layer, n, heads, row, gtid & 7);
+  pack_target_row(d, k + blockIdx.y * kc, v + blockIdx.y * vc, kh, kt, vh, vt, layer, n, heads, blocks, row,
+                  gtid & 7);
 }
 
 __global__ void __launch_bounds__(kPackThreads)
@@ -110,10 +111,10 @@ __global__ void map_fill_kernel(int32_t* __restrict__ rows, uint8_t* __restrict_
 
 cudaError_t launch_pack(const void* k, const void* v, void* p4, void* m4, void* p8, void* m8,
                         void* p16, int64_t kh, int64_t kt, int64_t vh, int64_t vt, int layer,
-                        int64_t row_start, int n, int64_t cap, int heads, int bits,
+                        int64_t row_start, int n, int blocks, int heads, int bits,
                         int32_t* status, cudaStream_t stream) {
   const int threads = 2 * heads * n * 8;
-  const int blocks = (threads + kPackThreads - 1) / kPackThreads;
+  const int grid = (threads + kPackThreads - 1) / kPackThreads;
   const uint16_t* kk = static_cast<const uint16_t*>(k);
   const uint16_t* vv = static_cast<const uint16_t*>(v);
   uint8_t* q4 = static_cast<uint8_t*>(p4);
@@ -122,7 +123,7 @@ cudaError_t launch_pack(const void* k, const void* v, void* p4, void* m4, void* 
   float2* s8 = static_cast<float2*>(m8);
   uint16_t* h = static_cast<uint16_t*>(p16);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(blocks);
+  cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kPackThreads);
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -131,14 +132,14 @@ cudaError_t launch_pack(const void* k, const void* v, void* p4, void* m4, void* 
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   auto kernel = bits == 4 ? pack_rows_kernel<4> : (bits == 8 ? pack_rows_kernel<8> : pack_rows_kernel<16>);
-  return cudaLaunchKernelEx(&cfg, kernel, kk, vv, q4, s4, q8, s8, h, kh, kt, vh, vt, layer, row_start, n, cap,
+  return cudaLaunchKernelEx(&cfg, kernel, kk, vv, q4, s4, q8, s8, h, kh, kt, vh, vt, layer, row_start, n, blocks,
                             heads, status);
 }
 
 template <class Targets>
 cudaError_t launch_pack_many_with(const void* k, const void* v, const Targets& tab, int count, int64_t kh,
                                   int64_t kt, int64_t vh, int64_t vt, int64_t kc, int64_t vc, int layer, int n,
-                                  int heads, cudaStream_t stream) {
+                                  int heads, int blocks, cudaStream_t stream) {
   const int threads = 2 * heads * n * 8;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((threads + kPackThreads - 1) / kPackThreads, count);
@@ -150,19 +151,19 @@ cudaError_t launch_pack_many_with(const void* k, const void* v, const Targets& t
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, pack_rows_many_kernel<Targets>, static_cast<const uint16_t*>(k),
-                            static_cast<const uint16_t*>(v), tab, kh, kt, vh, vt, kc, vc, layer, n, heads);
+                            static_cast<const uint16_t*>(v), tab, kh, kt, vh, vt, kc, vc, layer, n, heads, blocks);
 }
 
 // targets: host array (copied into the launch) or, with on_device, device memory.
 cudaError_t launch_pack_many(const void* k, const void* v, const dkv_pack_target* targets, bool on_device, int count,
                              int64_t kh, int64_t kt, int64_t vh, int64_t vt, int64_t kc, int64_t vc, int layer, int n,
-                             int heads, cudaStream_t stream) {
+                             int heads, int blocks, cudaStream_t stream) {
   if (on_device)
     return launch_pack_many_with(k, v, DevicePackTargets{targets}, count, kh, kt, vh, vt, kc, vc, layer, n, heads,
-                                 stream);
+                                 blocks, stream);
   PackTable tab{};
   for (int r = 0; r < count; ++r) tab.t[r] = targets[r];
-  return launch_pack_many_with(k, v, tab, count, kh, kt, vh, vt, kc, vc, layer, n, heads, stream);
+  return launch_pack_many_with(k, v, tab, count, kh, kt, vh, vt, kc, vc, layer, n, heads, blocks, stream);
 }
 
 cudaError_t launch_reconstruct(const Pools& P, const int32_t* rows, const uint8_t* codes, void* out,

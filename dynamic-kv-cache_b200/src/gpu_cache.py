@@ -3,10 +3,19 @@
 Drop-in for the reference's src/gpu_cache.py: same class name, constructor
 keywords, methods, attributes and error messages (GPUCache, src/gpu_cache.py:
 10-149; install_packed_attention, :151-183). The pools keep the reference's
-physical layout and growth policy, so `caps`, `host_counts`, `plan`, the token
+growth policy and row numbering, so `caps`, `host_counts`, `plan`, the token
 maps `rows`/`codes` and `accounting()` read exactly as the reference's do. The
 Triton launches are replaced by the sm_100a kernels of libdkv.so (gpu_kernels),
 and the per-token map update is one device launch (map_fill).
+
+Pools are paged (include/dkv.h): the rows of every (layer, K|V, head) block come
+in pages of 64 and page p of every block is stored side by side, so
+`p4` is [pages, layers, 2, heads, 64, 32] where the reference has
+[layers, 2, heads, cap4, 32]; `pool_rows` reads rows in the reference's
+terms. On CUDA each pool lives in a device region that reserves the address
+space of the largest capacity the cache can reach and maps memory as it grows:
+growth appends pages and copies no row (the reference allocates a larger tensor
+and copies, src/gpu_cache.py:44-59), and the pool pointers never move.
 """
 import ctypes
 import types
@@ -18,6 +27,20 @@ from transformers.cache_utils import DynamicCache
 from . import gpu_kernels as K
 
 BITS = (4, 8, 16)
+PAGE_ROWS = 64
+# pool attribute -> (dtype, row width in elements, precision)
+POOLS = {'p4': (torch.uint8, 32, 4), 'm4': (torch.float32, 2, 4), 'p8': (torch.uint8, 64, 8),
+         'm8': (torch.float32, 2, 8), 'p16': (torch.bfloat16, 64, 16)}
+
+
+def _pages(rows):
+    return max(1, (rows + PAGE_ROWS - 1) // PAGE_ROWS)
+
+
+def _growth(old, needed):
+    """The reference's new capacity for a pool of `old` rows that must hold `needed`
+    (src/gpu_cache.py:47)."""
+    return max(needed, ((int(old * 1.5) + 63) // 64) * 64)
 
 
 class GPUCache(DynamicCache):
@@ -54,38 +77,90 @@ class GPUCache(DynamicCache):
         else:
             self.rows = torch.tensor(rows, dtype=torch.int32, device=self.device)
             self.codes = torch.tensor(codes, dtype=torch.uint8, device=self.device)
-        common = (layers, 2, heads)
-        self.p4 = torch.empty((*common, self.caps[4], dim // 2), dtype=torch.uint8, device=self.device)
-        self.p8 = torch.empty((*common, self.caps[8], dim), dtype=torch.uint8, device=self.device)
-        self.p16 = torch.empty((*common, self.caps[16], dim), dtype=dtype, device=self.device)
-        self.m4 = torch.empty((*common, self.caps[4], 2), dtype=torch.float32, device=self.device)
-        self.m8 = torch.empty((*common, self.caps[8], 2), dtype=torch.float32, device=self.device)
+        # An online pool never holds more rows than the cache has tokens, so the
+        # reference's growth stops at _growth(capacity - 1, capacity); an offline
+        # plan fixes the capacities up front.
+        limit = _growth(self.capacity - 1, self.capacity) if self.online else 0
+        self._leases = {}
+        for name, (_, _, bits) in POOLS.items():
+            self._allocate(name, self.caps[bits], max(limit, self.caps[bits]))
         self.host_counts = counts
         # Device status word written by the kernels (first error code, detail index).
         self.status = torch.zeros(4, dtype=torch.int32, device=self.device)
 
     # -- capacity ---------------------------------------------------------------
+    def _page_shape(self, name, pages):
+        return (pages, self.layers, 2, self.heads, PAGE_ROWS, POOLS[name][1])
+
+    def _page_bytes(self, name):
+        dtype, width, _ = POOLS[name]
+        return self.layers * 2 * self.heads * PAGE_ROWS * width * dtype.itemsize
+
+    def _allocate(self, name, rows, limit_rows):
+        """Pool `name` with room for `rows` rows per block; on CUDA in a region
+        reserved for `limit_rows`."""
+        dtype = POOLS[name][0]
+        pages = _pages(rows)
+        if self.device.type != 'cuda':  # host-side bookkeeping (tests): a plain tensor
+            setattr(self, name, torch.empty(self._page_shape(name, pages), dtype=dtype, device=self.device))
+            return
+        lease = K.lease_region(self.device, _pages(limit_rows) * self._page_bytes(name))
+        lease.region.map(pages * self._page_bytes(name))
+        self._leases[name] = lease
+        setattr(self, name, K.region_tensor(lease, self._page_shape(name, pages), dtype))
+
+    def _grow(self, name, rows):
+        """Pool `name` to `rows` rows per block, its old rows left where they are."""
+        dtype = POOLS[name][0]
+        old = getattr(self, name)
+        pages = _pages(rows)
+        if pages <= old.shape[0]:
+            return
+        lease = self._leases.get(name)
+        if lease is not None and pages * self._page_bytes(name) <= lease.region.reserved:
+            lease.region.map(pages * self._page_bytes(name))  # new pages behind the old ones
+            setattr(self, name, K.region_tensor(lease, self._page_shape(name, pages), dtype))
+            return
+        # beyond the reservation (an explicit reserve() past the cache's token
+        # capacity) or a host tensor: a larger pool and one copy of the old pages
+        self._leases = dict(self._leases)  # a fork's pools stay with the base
+        self._allocate(name, rows, 2 * rows)
+        getattr(self, name)[:old.shape[0]].copy_(old)
+
     def reserve(self, bits, needed):
         """Grows pool `bits` to at least `needed` rows: max(needed, 1.5x rounded up
-        to 64), as src/gpu_cache.py:44-59, copying the old rows on the device."""
+        to 64), as src/gpu_cache.py:44-59. On CUDA the new pages are mapped behind
+        the old ones; no row moves."""
         old = self.caps[bits]
         if needed <= old:
             return
-        cap = max(needed, ((int(old * 1.5) + 63) // 64) * 64)
-        common = (self.layers, 2, self.heads)
-        attr = {4: 'p4', 8: 'p8', 16: 'p16'}[bits]
-        source = getattr(self, attr)
-        target = torch.empty((*common, cap, self.dim // 2 if bits == 4 else self.dim),
-                             dtype=source.dtype, device=self.device)
-        target[:, :, :, :old].copy_(source)
-        setattr(self, attr, target)
-        if bits != 16:
-            attr = 'm4' if bits == 4 else 'm8'
-            source = getattr(self, attr)
-            target = torch.empty((*common, cap, 2), dtype=source.dtype, device=self.device)
-            target[:, :, :, :old].copy_(source)
-            setattr(self, attr, target)
+        cap = _growth(old, needed)
+        for name, (_, _, b) in POOLS.items():
+            if b == bits:
+                self._grow(name, cap)
         self.caps[bits] = cap
+
+    def pool_rows(self, name, layer, kv, start, n):
+        """Rows [start, start + n) of pool `name` ('p4', 'm4', 'p8', 'm8', 'p16')
+        for (layer, K = 0 | V = 1) as [heads, n, width]: the reference's
+        `<pool>[layer, kv, :, start:start + n]` (a gathered copy)."""
+        self._check_rows(name, layer, kv, start, n)
+        r = torch.arange(start, start + n, device=self.device)
+        return getattr(self, name)[r // PAGE_ROWS, layer, kv, :, r % PAGE_ROWS].transpose(0, 1)
+
+    def write_pool_rows(self, name, layer, kv, start, rows):
+        """Stores `rows` ([heads, n, width]) at rows [start, start + n) of pool
+        `name` for (layer, kv)."""
+        self._check_rows(name, layer, kv, start, rows.shape[1])
+        r = torch.arange(start, start + rows.shape[1], device=self.device)
+        getattr(self, name)[r // PAGE_ROWS, layer, kv, :, r % PAGE_ROWS] = rows.transpose(0, 1).to(self.device)
+
+    def _check_rows(self, name, layer, kv, start, n):
+        """Host-side bounds of a pool_rows / write_pool_rows range (a device-side
+        index error would end the CUDA context)."""
+        if name not in POOLS or not 0 <= layer < self.layers or kv not in (0, 1) or start < 0 or n < 0 \
+                or start + n > self.caps[POOLS[name][2]]:
+            raise ValueError(f'rows [{start}, {start + n}) of {name} outside the pool')
 
     def select(self, bits, frame_id=-1):
         self.pending_bits, self.frame_id = bits, frame_id
@@ -235,7 +310,8 @@ class GPUCache(DynamicCache):
         """QA branch sharing the pools and maps; host bookkeeping is copied, so a
         branch's appends and growth never move the base (src/gpu_cache.py:121-132).
         Branches overwrite the same reserved rows and must run one after another
-        on one stream."""
+        on one stream. A branch's growth maps pages behind the base's rows in the
+        shared regions; the base's capacities and rows stay as they were."""
         other = object.__new__(GPUCache)
         other.__dict__ = self.__dict__.copy()
         other.seen = self.seen.copy()
@@ -254,8 +330,10 @@ class GPUCache(DynamicCache):
 
     def accounting(self):
         """Used/allocated bytes with the reference's formulas (src/gpu_cache.py:134-149)."""
-        tensors = [self.p4, self.p8, self.p16, self.m4, self.m8, self.rows, self.codes]
-        allocated = sum(t.numel() * t.element_size() for t in tensors)
+        # the reference's allocation, [layers, 2, heads, cap, width] per pool
+        blocks = self.layers * 2 * self.heads
+        allocated = sum(blocks * self.caps[b] * w * dtype.itemsize for dtype, w, b in POOLS.values())
+        allocated += self.rows.numel() * self.rows.element_size() + self.codes.numel() * self.codes.element_size()
         used = {4: 0, 8: 0, 16: 0}
         n = self.seen[0]
         for start, end, bits, row in self.plan:

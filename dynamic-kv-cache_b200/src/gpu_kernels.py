@@ -15,6 +15,7 @@ There is no fallback: importing this module without the built library raises.
 """
 import ctypes
 import functools
+import threading
 from pathlib import Path
 
 import torch
@@ -51,7 +52,7 @@ def _load():
         raise ImportError(f'{_LIB_PATH} is not built; run `python __graft_entry__.py build` '
                           '(or dynamic-kv-cache_b200/build.py) first. There is no CPU fallback.')
     lib = ctypes.CDLL(str(_LIB_PATH))
-    P, I32, I64, SZ = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_size_t
+    P, I32, I64, SZ, U64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_size_t, ctypes.c_uint64
     sigs = {
         'dkv_version': ([], I32),
         'dkv_last_error': ([], ctypes.c_char_p),
@@ -85,6 +86,13 @@ def _load():
         'dkv_silu_mul': ([P, P, P, I64, I64, I64, I32, P], ctypes.c_int),
         'dkv_append_attention_many_device': ([P, P, P, P, P, I32, I32, P, I64, I64, I64, I64, I64, I64, I64, I64, I64,
                                               I64, I32, I32, I32, I32, I32, I32, P, SZ, P], ctypes.c_int),
+        'dkv_pool_granularity': ([I32], U64),
+        'dkv_pool_create': ([I32, U64, ctypes.POINTER(P)], ctypes.c_int),
+        'dkv_pool_map': ([P, U64], ctypes.c_int),
+        'dkv_pool_base': ([P], P),
+        'dkv_pool_mapped_bytes': ([P], U64),
+        'dkv_pool_reserved_bytes': ([P], U64),
+        'dkv_pool_destroy': ([P], ctypes.c_int),
     }
     for name, (args, res) in sigs.items():
         fn = getattr(lib, name)
@@ -98,7 +106,8 @@ EXPORTS = ('dkv_version', 'dkv_last_error', 'dkv_pack_rows', 'dkv_packed_attenti
            'dkv_packed_attention_batched_workspace', 'dkv_reconstruct', 'dkv_map_fill', 'dkv_pack_rows_many',
            'dkv_packed_attention_many', 'dkv_packed_attention_many_workspace', 'dkv_pack_rows_many_device',
            'dkv_packed_attention_many_device', 'dkv_append_attention', 'dkv_append_attention_many_device',
-           'dkv_rotary', 'dkv_silu_mul')
+           'dkv_rotary', 'dkv_silu_mul', 'dkv_pool_granularity', 'dkv_pool_create', 'dkv_pool_map',
+           'dkv_pool_base', 'dkv_pool_mapped_bytes', 'dkv_pool_reserved_bytes', 'dkv_pool_destroy')
 
 
 def _check(rc):
@@ -378,3 +387,105 @@ def raise_for_status(status):
     if code == DKV_ENONFINITE:
         raise ValueError('Nonfinite KV tensor')
     raise ValueError(f'{STATUS_NAMES.get(code, f"status {code}")} (index {detail})')
+
+
+# -- growable device pools (dkv_pool_*; no reference counterpart) -----------------
+# The reference grows a pool by allocating a larger tensor and copying every old
+# row (src/gpu_cache.py:44-59). A region here reserves the largest size a pool can
+# reach as device address space and maps memory onto its front as the pool grows
+# (the pools are paged, so growth only appends pages): the base address never
+# moves and nothing is copied. A region whose last user (cache, fork or tensor
+# view) is gone goes to a per-device free list, memory still mapped, and the next
+# reservation that fits reuses it; work the old owner queued is ordered before the
+# new owner's through the stream current at release (a cache's kernels run on one
+# stream, as in the reference). release_pool_memory() returns the free list's
+# memory to the device.
+
+class Region:
+    """One reservation: `reserved` bytes of address space from `base`, the first
+    `mapped` of them backed by device memory."""
+
+    def __init__(self, device, handle):
+        self.device, self.handle = device, handle
+        self.base = LIB.dkv_pool_base(handle)
+        self.reserved = LIB.dkv_pool_reserved_bytes(handle)
+
+    @property
+    def mapped(self):
+        return LIB.dkv_pool_mapped_bytes(self.handle)
+
+    def map(self, nbytes):
+        _check(LIB.dkv_pool_map(self.handle, nbytes))
+
+
+class RegionLease:
+    """A region in use. Dropping the last reference returns the region to the free
+    list together with the stream that was current then."""
+
+    def __init__(self, region):
+        self.region = region
+
+    def __del__(self):
+        try:
+            stream = torch.cuda.current_stream(self.region.device)
+        except Exception:  # interpreter shutdown: the driver releases everything at exit
+            return
+        with _FREE_LOCK:
+            _FREE.setdefault(self.region.device, []).append((self.region, stream))
+
+
+_FREE = {}
+_FREE_LOCK = threading.Lock()
+
+
+def lease_region(device, nbytes):
+    """A region of at least `nbytes` of address space on `device` (torch.device):
+    the smallest fitting one of the free list, else a new reservation."""
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    taken = None
+    with _FREE_LOCK:
+        free = _FREE.get(index, [])
+        fits = [i for i, (r, _) in enumerate(free) if r.reserved >= nbytes]
+        if fits:
+            taken = free.pop(min(fits, key=lambda i: free[i][0].reserved))
+    if taken is not None:
+        region, stream = taken
+        current = torch.cuda.current_stream(index)
+        if stream != current:  # the old owner's queued work first
+            current.wait_stream(stream)
+        return RegionLease(region)
+    handle = ctypes.c_void_p()
+    _check(LIB.dkv_pool_create(index, nbytes, ctypes.byref(handle)))
+    return RegionLease(Region(index, handle))
+
+
+def release_pool_memory():
+    """Unmaps and frees every region on the free list (each release synchronises its
+    device first). Regions still in use are untouched."""
+    with _FREE_LOCK:
+        regions = [r for free in _FREE.values() for r, _ in free]
+        _FREE.clear()
+    for r in regions:
+        _check(LIB.dkv_pool_destroy(r.handle))
+
+
+class _DeviceBytes:
+    """The first `nbytes` of a leased region as a CUDA array (keeps the lease alive
+    for as long as a tensor made from it)."""
+
+    def __init__(self, lease, nbytes):
+        self.lease = lease
+        self.__cuda_array_interface__ = {'shape': (nbytes,), 'typestr': '|u1',
+                                         'data': (lease.region.base, False), 'version': 2, 'strides': None}
+
+
+def region_tensor(lease, shape, dtype):
+    """A tensor of `shape` and `dtype` over the front of a leased region (no copy);
+    the region must have that many bytes mapped."""
+    nbytes = dtype.itemsize
+    for d in shape:
+        nbytes *= d
+    if nbytes > lease.region.mapped:
+        raise ValueError('region view beyond its mapped bytes')
+    raw = torch.as_tensor(_DeviceBytes(lease, nbytes), device=torch.device('cuda', lease.region.device))
+    return raw.view(dtype).view(shape)

@@ -91,12 +91,12 @@ def export_segment(cache, layer, index):
     out = []
     for kv in (0, 1):
         if bits == 16:
-            payload = cache.p16[layer, kv, :, row:row + n].contiguous().view(torch.uint8).flatten().cpu()
+            payload = cache.pool_rows('p16', layer, kv, row, n).contiguous().view(torch.uint8).flatten().cpu()
             scales = offsets = torch.empty(0, dtype=torch.float32)
         else:
-            pool, meta = (cache.p4, cache.m4) if bits == 4 else (cache.p8, cache.m8)
-            payload = pool[layer, kv, :, row:row + n].contiguous().flatten().cpu()
-            pairs = meta[layer, kv, :, row:row + n].reshape(-1, 2).cpu()
+            pool, meta = ('p4', 'm4') if bits == 4 else ('p8', 'm8')
+            payload = cache.pool_rows(pool, layer, kv, row, n).contiguous().flatten().cpu()
+            pairs = cache.pool_rows(meta, layer, kv, row, n).reshape(-1, 2).cpu()
             offsets, scales = pairs[:, 0].contiguous(), pairs[:, 1].contiguous()
         out.append(PackedTensor(payload, scales, offsets, _header(bits, cache.heads, n, cache.dim)))
     return tuple(out)
@@ -127,12 +127,11 @@ def import_frame(cache, k_packed, v_packed, layer):
     for kv, packed in enumerate((k_packed, v_packed)):
         if bits == 16:
             rows = packed.payload.view(torch.bfloat16).reshape(cache.heads, n, cache.dim)
-            cache.p16[layer, kv, :, row:row + n].copy_(rows.to(dev))
+            cache.write_pool_rows('p16', layer, kv, row, rows.to(dev))
         else:
-            pool, meta = (cache.p4, cache.m4) if bits == 4 else (cache.p8, cache.m8)
-            rows = packed.payload.reshape(cache.heads, n, -1)
-            pool[layer, kv, :, row:row + n].copy_(rows.to(dev))
+            pool, meta = ('p4', 'm4') if bits == 4 else ('p8', 'm8')
+            cache.write_pool_rows(pool, layer, kv, row, packed.payload.reshape(cache.heads, n, -1).to(dev))
             pairs = torch.stack((packed.offsets, packed.scales), dim=-1).reshape(cache.heads, n, 2)
-            meta[layer, kv, :, row:row + n].copy_(pairs.to(dev))
+            cache.write_pool_rows(meta, layer, kv, row, pairs.to(dev))
     cache.seen[layer] = past + n
     return past

@@ -12,13 +12,21 @@
  *  - Every pointer is a device pointer unless stated; nothing is freed or retained.
  *  - Strides are in ELEMENTS (bf16), exactly as torch's Tensor.stride() reports
  *    them; the innermost (head_dim) stride must be 1.
- *  - bf16 tensors are passed as void*; pools use the reference's physical layout:
- *      p4  uint8 [layers, 2, heads, cap4, dim/2]   two 4-bit codes per byte, lo = even
- *      m4  f32   [layers, 2, heads, cap4, 2]       (offset, scale) per row
- *      p8  uint8 [layers, 2, heads, cap8, dim]
- *      m8  f32   [layers, 2, heads, cap8, 2]
- *      p16 bf16  [layers, 2, heads, cap16, dim]
- *    (index 1 selects K = 0 or V = 1), and the token maps
+ *  - bf16 tensors are passed as void*. Pools are paged: the rows of every
+ *    (layer, K|V, head) block come in pages of DKV_PAGE_ROWS = 64, and page p of
+ *    every block is stored side by side, so a pool of more rows is the same pool
+ *    with more pages at the end (growth maps pages, see dkv_pool_*, and copies
+ *    nothing). With P = ceil(cap / 64) pages:
+ *      p4  uint8 [P4, layers, 2, heads, 64, dim/2]  two 4-bit codes per byte, lo = even
+ *      m4  f32   [P4, layers, 2, heads, 64, 2]      (offset, scale) per row
+ *      p8  uint8 [P8, layers, 2, heads, 64, dim]
+ *      m8  f32   [P8, layers, 2, heads, 64, 2]
+ *      p16 bf16  [P16, layers, 2, heads, 64, dim]
+ *    (index 2 selects K = 0 or V = 1; row r of a block is at page r / 64, slot
+ *    r % 64). cap4 / cap8 / cap16 are the rows in use per block (the reference's
+ *    pool capacities, src/gpu_cache.py:36-41), a row r is valid when r < cap; the
+ *    reference lays the same rows out as [layers, 2, heads, cap, ...], and the
+ *    token maps
  *      rows  int32 [capacity]  pool row of logical token t
  *      codes uint8 [capacity]  storage bits of logical token t (4, 8 or 16)
  *  - `stream` is a cudaStream_t (NULL = legacy default stream). All work is
@@ -42,7 +50,8 @@
 extern "C" {
 #endif
 
-#define DKV_VERSION 1
+#define DKV_VERSION 2
+#define DKV_PAGE_ROWS 64
 
 enum dkv_status {
   DKV_OK = 0,
@@ -188,6 +197,40 @@ int dkv_packed_attention_noalloc(const void* q, const void* knew, const void* vn
                                  int32_t heads, int32_t group, int32_t dim,
                                  int32_t block_m, int32_t block_n,
                                  int32_t layers, int32_t* status, void* stream);
+
+/*
+ * ---- Growable device pools (no reference counterpart) ----
+ * The reference grows a precision pool by allocating a larger tensor and copying
+ * every old row into it (GPUCache.reserve, src/gpu_cache.py:44-59). A dkv_pool
+ * reserves the largest size a pool can reach as device address space once and
+ * maps physical memory onto the front of that range as the pool grows (CUDA
+ * virtual memory management, in multiples of dkv_pool_granularity() bytes). With
+ * the paged layout above, growing cap only appends pages, so the base address
+ * never moves and no row is copied; descriptors captured in a CUDA graph stay
+ * valid across a growth. Pages are uninitialised, as the reference's torch.empty.
+ */
+typedef struct dkv_pool dkv_pool;
+
+/* Mapping granularity of `device` in bytes (0 if the driver offers none). */
+uint64_t dkv_pool_granularity(int32_t device);
+
+/* Reserves reserve_bytes (rounded up to the granularity) of address space on
+   `device` with nothing mapped; *pool receives the handle. */
+int dkv_pool_create(int32_t device, uint64_t reserve_bytes, dkv_pool** pool);
+
+/* Maps physical memory so that [base, base + bytes) is usable (rounded up to the
+   granularity; never shrinks). DKV_ECAPACITY beyond the reservation, DKV_ECUDA
+   when the device is out of memory. Host-side only: enqueues nothing. */
+int dkv_pool_map(dkv_pool* pool, uint64_t bytes);
+
+/* First byte of the reservation (fixed for the pool's lifetime). */
+void* dkv_pool_base(const dkv_pool* pool);
+uint64_t dkv_pool_mapped_bytes(const dkv_pool* pool);
+uint64_t dkv_pool_reserved_bytes(const dkv_pool* pool);
+
+/* Synchronises the pool's device (work still queued may read the pages), then
+   unmaps and releases everything. The handle is invalid afterwards. */
+int dkv_pool_destroy(dkv_pool* pool);
 
 /*
  * ---- Request batching (no reference counterpart) ----

@@ -20,10 +20,10 @@ def gpu_tensor(bits16):
 def pool_rows(cache, layer, kv, bits, row0, n):
     """Pool bytes of rows [row0, row0+n) as (payload [H, n, rowbytes] uint8, meta [H, n, 2] f32 | None)."""
     if bits == 16:
-        payload = cache.p16[layer, kv, :, row0:row0 + n].contiguous().view(torch.uint8)
+        payload = cache.pool_rows('p16', layer, kv, row0, n).contiguous().view(torch.uint8)
         return payload.cpu().numpy(), None
-    p = (cache.p4 if bits == 4 else cache.p8)[layer, kv, :, row0:row0 + n]
-    m = (cache.m4 if bits == 4 else cache.m8)[layer, kv, :, row0:row0 + n]
+    p = cache.pool_rows('p4' if bits == 4 else 'p8', layer, kv, row0, n)
+    m = cache.pool_rows('m4' if bits == 4 else 'm8', layer, kv, row0, n)
     return p.cpu().numpy(), m.cpu().numpy()
 
 

@@ -22,7 +22,8 @@ def test_offline_plan_rows_codes_and_caps():
     assert c.rows.tolist() == list(range(20)) + list(range(10)) + list(range(20, 25)) + list(range(3))
     assert c.codes.tolist() == [4] * 20 + [16] * 10 + [4] * 5 + [8] * 3
     assert c.caps == {4: 25, 8: 3, 16: 10} and c.capacity == 38
-    assert c.p4.shape == (2, 2, 3, 25, 32) and c.m8.shape == (2, 2, 3, 3, 2)
+    # paged pools: [pages, layers, 2, heads, 64, width], ceil(cap / 64) pages
+    assert c.p4.shape == (1, 2, 2, 3, 64, 32) and c.m8.shape == (1, 2, 2, 3, 64, 2)
     assert c.p16.dtype == torch.bfloat16 and len(c) == 2 and c.get_seq_length() == 0
 
 
@@ -32,14 +33,24 @@ def test_online_growth_policy_matches_reference():
     sentinel = torch.arange(c.p4.numel(), dtype=torch.int64).remainder(251).to(torch.uint8).view(c.p4.shape)
     c.p4.copy_(sentinel)
     c.reserve(4, 79)           # max(79, ceil64(96)) = 128
-    assert c.caps[4] == 128 and c.p4.shape[3] == 128 and c.m4.shape[3] == 128
-    assert torch.equal(c.p4[:, :, :, :64], sentinel)  # old rows copied
+    assert c.caps[4] == 128 and c.p4.shape[0] == 2 and c.m4.shape[0] == 2  # pages of 64 rows
+    assert torch.equal(c.p4[:1], sentinel)  # old rows kept: growth appends pages
     c.reserve(4, 167)          # max(167, ceil64(192)) = 192
-    assert c.caps[4] == 192
+    assert c.caps[4] == 192 and c.p4.shape[0] == 3
     c.reserve(4, 100)          # no shrink / no-op
     assert c.caps[4] == 192
     c.reserve(16, 400)         # needed beats 1.5x
-    assert c.caps[16] == 400 and c.p16.shape[3] == 400
+    assert c.caps[16] == 400 and c.p16.shape[0] == 7
+
+
+def test_pool_rows_read_and_write_in_reference_terms():
+    c = GPUCache(None, layers=2, heads=3, device='cpu', max_tokens=512)
+    c.reserve(8, 200)
+    rows = torch.arange(3 * 150 * 64, dtype=torch.int64).remainder(253).to(torch.uint8).view(3, 150, 64)
+    c.write_pool_rows('p8', 1, 1, 30, rows)  # rows 30..179: across pages 0, 1, 2
+    assert torch.equal(c.pool_rows('p8', 1, 1, 30, 150), rows)
+    assert torch.equal(c.p8[1, 1, 1, :, 0], rows[:, 34])  # row 64 = page 1, slot 0
+    assert torch.equal(c.p8[2, 1, 1, :, 51], rows[:, 149])  # row 179 = page 2, slot 51
 
 
 def test_append_requires_cuda_and_batch_one():
@@ -122,7 +133,7 @@ def test_claim_frame_online_grows_and_records_the_segment_once():
         assert past == 64 * i and a.seen == [64 * (i + 1)] * 4
         assert a.plan[-1] == (past, past + 64, bits, row)
     assert a.host_counts == {4: 192, 8: 64, 16: 64}
-    assert a.caps[4] >= 192 and a.p4.shape[3] == a.caps[4]
+    assert a.caps[4] >= 192 and a.p4.shape[0] == (a.caps[4] + 63) // 64
     with pytest.raises(ValueError, match='Cache append does not match plan|context limit'):
         a._claim_frame(512)
 

@@ -266,15 +266,23 @@ def test_frame_graph_replay_matches_its_eager_step(cuda):
     a, b = caches(), caches()
     ga = FrameGraph(model.model, a, 64, logits=3, max_past=512)
     gb = FrameGraph(model.model, b, 64, logits=3, max_past=512)
+    pools = ('p4', 'm4', 'p8', 'm8', 'p16')
+    ptrs, caps = [[getattr(c, n).data_ptr() for n in pools] for c in a], [dict(c.caps) for c in a]
     with torch.inference_mode():
         for i, x in enumerate(frames):
             for c, bt in zip(a + b, (4, 16, 4, 16) if i % 2 else (8, 4, 8, 4)):
                 c.select(bt, i)
             la = ga.step(embeds=x).clone()  # eager at i = 0, replayed afterwards
+            if i == 1:
+                graph = ga.graph
             gb.batch.prepare()             # b: the eager device-descriptor step every time
             gb.x.copy_(x)
             lb = model.model.forward_device(gb.batch, gb.x, 3)
             assert torch.equal(la, lb), i
+    # the pools grew during replayed steps: the same graph kept serving them, at the
+    # same addresses (growth maps pages behind the old rows)
+    assert ga.graph is graph and all(c.caps != c0 for c, c0 in zip(a, caps))
+    assert [[getattr(c, n).data_ptr() for n in pools] for c in a] == ptrs
     for x, y in zip(a, b):
         x.check()
         for layer in range(TINY.layers):

@@ -245,8 +245,13 @@ attention_split_kernel(const __grid_constant__ AttnArgs a, const __grid_constant
       code = 0;
     }
   };
-  // Starts the copies of this lane's K and V row (and pairs) into raw stage st.
-  auto issue_rows = [&](int st, int code, int row) {
+  // Starts the copies of the warp's tile into raw stage st, every lane giving its
+  // token's (code, row) from load_map. Runs of consecutive pool rows (one
+  // precision, one page: contiguous bytes) are copied by the whole warp in
+  // consecutive 16-byte chunks, so a request covers whole cache lines (a 32-row
+  // bf16 run: 8 requests of 512 contiguous bytes per K and V) and every sector is
+  // fetched once; a token of the current chunk brings its native row itself.
+  auto issue_tile = [&](int st, int code, int row) {
     const uint32_t base = wsm_a + st * kSpRawStage;
     if (code == kSpCodeNew) {
       const uint16_t* kr = knew_g + static_cast<int64_t>(row) * a.kt;
@@ -256,27 +261,35 @@ attention_split_kernel(const __grid_constant__ AttnArgs a, const __grid_constant
         cp_async16_cg(base + kSpRawK + sp_swz(lane, c), kr + c * 8);
         cp_async16_cg(base + kSpRawV + sp_swz(lane, c), vr + c * 8);
       }
-    } else if (code == 16) {
-      const uint8_t* kr = p16 + pool_row(blk_k, row, a.blocks) * kRowBytes16;
-      const uint8_t* vr = p16 + pool_row(blk_v, row, a.blocks) * kRowBytes16;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        cp_async16_cg(base + kSpRawK + sp_swz(lane, c), kr + c * 16);
-        cp_async16_cg(base + kSpRawV + sp_swz(lane, c), vr + c * 16);
+    }
+    const bool pooled = code == 4 || code == 8 || code == 16;
+    const int pcode = __shfl_up_sync(0xffffffffu, code, 1);
+    const int prow = __shfl_up_sync(0xffffffffu, row, 1);
+    const bool start = pooled && (lane == 0 || pcode != code || prow + 1 != row || (row & (kPageRows - 1)) == 0);
+    uint32_t starts = __ballot_sync(0xffffffffu, start);
+    const uint32_t breaks = __ballot_sync(0xffffffffu, !pooled);  // a run ends before these
+    while (starts != 0u) {
+      const int j0 = __ffs(starts) - 1;
+      starts &= starts - 1u;
+      const uint32_t after = (starts | breaks) & ~((2u << j0) - 1u);  // lanes above j0
+      const int cnt = (after != 0u ? __ffs(after) - 1 : 32) - j0;
+      const int rc = __shfl_sync(0xffffffffu, code, j0);
+      const int r0 = __shfl_sync(0xffffffffu, row, j0);
+      const int lg = rc == 4 ? 1 : (rc == 8 ? 2 : 3);  // log2 of 16-byte chunks per row
+      const int rb = 16 << lg;
+      const uint8_t* pool = rc == 4 ? p4 : (rc == 8 ? p8 : p16);
+      const uint8_t* ks = pool + pool_row(blk_k, r0, a.blocks) * rb;
+      const uint8_t* vs = pool + pool_row(blk_v, r0, a.blocks) * rb;
+      for (int q = lane; q < (cnt << lg); q += 32) {
+        const uint32_t at = sp_swz(j0 + (q >> lg), q & ((1 << lg) - 1));
+        cp_async16_cg(base + kSpRawK + at, ks + q * 16);
+        cp_async16_cg(base + kSpRawV + at, vs + q * 16);
       }
-    } else if (code == 8 || code == 4) {
-      const int rb = code == 8 ? kRowBytes8 : kRowBytes4;
-      const uint8_t* pool = code == 8 ? p8 : p4;
-      const float2* meta = code == 8 ? m8 : m4;
-      const int64_t at_k = pool_row(blk_k, row, a.blocks), at_v = pool_row(blk_v, row, a.blocks);
-      const uint8_t* kr = pool + at_k * rb;
-      const uint8_t* vr = pool + at_v * rb;
-      for (int c = 0; c < rb / 16; ++c) {
-        cp_async16_cg(base + kSpRawK + sp_swz(lane, c), kr + c * 16);
-        cp_async16_cg(base + kSpRawV + sp_swz(lane, c), vr + c * 16);
+      if (rc != 16 && lane < cnt) {
+        const float2* meta = rc == 8 ? m8 : m4;
+        cp_async8(base + kSpRawMK + (j0 + lane) * 8, meta + pool_row(blk_k, r0, a.blocks) + lane);
+        cp_async8(base + kSpRawMV + (j0 + lane) * 8, meta + pool_row(blk_v, r0, a.blocks) + lane);
       }
-      cp_async8(base + kSpRawMK + lane * 8, meta + at_k);
-      cp_async8(base + kSpRawMV + lane * 8, meta + at_v);
     }
   };
 
@@ -293,9 +306,9 @@ attention_split_kernel(const __grid_constant__ AttnArgs a, const __grid_constant
     pdl_wait();
     waited = true;
   }
-  issue_rows(0, code_c[0], row_c[0]);
+  issue_tile(0, code_c[0], row_c[0]);
   cp_async_commit();
-  issue_rows(1, code_c[1], row_c[1]);
+  issue_tile(1, code_c[1], row_c[1]);
   cp_async_commit();
 
   // ---- Q fragments (rows g0 = lane / 4 and g0 + 8; zeros past the last row) ----
@@ -345,7 +358,7 @@ attention_split_kernel(const __grid_constant__ AttnArgs a, const __grid_constant
     row_c[0] = row_c[1];
     code_c[1] = code_c[2];
     row_c[1] = row_c[2];
-    issue_rows(st, code_c[1], row_c[1]);
+    issue_tile(st, code_c[1], row_c[1]);
     cp_async_commit();
     load_map(jj + 3, code_c[2], row_c[2]);
 

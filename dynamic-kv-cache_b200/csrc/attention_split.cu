@@ -250,8 +250,9 @@ attention_split_kernel(const __grid_constant__ AttnArgs a, const __grid_constant
   // precision, one page: contiguous bytes) are copied by the whole warp in
   // consecutive 16-byte chunks, so a request covers whole cache lines (a 32-row
   // bf16 run: 8 requests of 512 contiguous bytes per K and V) and every sector is
-  // fetched once; a token of the current chunk brings its native row itself.
-  auto issue_tile = [&](int st, int code, int row) {
+  // fetched once; a token of the current chunk brings its native row itself
+  // (issue_new; with news = false the caller does that later).
+  auto issue_new = [&](int st, int code, int row) {
     const uint32_t base = wsm_a + st * kSpRawStage;
     if (code == kSpCodeNew) {
       const uint16_t* kr = knew_g + static_cast<int64_t>(row) * a.kt;
@@ -262,6 +263,10 @@ attention_split_kernel(const __grid_constant__ AttnArgs a, const __grid_constant
         cp_async16_cg(base + kSpRawV + sp_swz(lane, c), vr + c * 8);
       }
     }
+  };
+  auto issue_tile = [&](int st, int code, int row, bool news) {
+    const uint32_t base = wsm_a + st * kSpRawStage;
+    if (news) issue_new(st, code, row);
     const bool pooled = code == 4 || code == 8 || code == 16;
     const int pcode = __shfl_up_sync(0xffffffffu, code, 1);
     const int prow = __shfl_up_sync(0xffffffffu, row, 1);
@@ -293,27 +298,28 @@ attention_split_kernel(const __grid_constant__ AttnArgs a, const __grid_constant
     }
   };
 
-  // ---- prologue: maps of tiles 0..2, rows of tiles 0 and 1 (before the wait
-  // unless the previous launch may have written this history) ----
+  // ---- prologue: maps of tiles 0..2 and the history rows of tiles 0 and 1 (before
+  // the wait unless the previous launch may have written this history); the rows
+  // of the call's own new tokens, Q and every write after the wait ----
   if (a.hist_wait) pdl_wait();
   int code_c[3], row_c[3];  // maps of tiles jj, jj + 1, jj + 2 (rotating)
   load_map(0, code_c[0], row_c[0]);
   load_map(1, code_c[1], row_c[1]);
   load_map(2, code_c[2], row_c[2]);
-  bool waited = a.hist_wait != 0;
-  auto needs_wait = [&](int jj) { return jj < mine && min(tile_t0(jj) + kSpKeys, ke) > past; };
-  if (needs_wait(0) || needs_wait(1)) {  // a tile of new tokens: the previous kernel's output
-    pdl_wait();
-    waited = true;
-  }
-  issue_tile(0, code_c[0], row_c[0]);
+  issue_tile(0, code_c[0], row_c[0], false);
   cp_async_commit();
-  issue_tile(1, code_c[1], row_c[1]);
+  issue_tile(1, code_c[1], row_c[1], false);
+  cp_async_commit();
+  if (!a.hist_wait) pdl_wait();  // new K/V and Q are the previous kernels' output
+  pdl_trigger();                 // the next kernel may start streaming its own history
+  // new-token rows of tiles 0 and 1 as a third group (empty for most warps), so
+  // tile 0 waits for it and every later tile keeps waiting for all but one group
+  const bool late = __any_sync(0xffffffffu, code_c[0] == kSpCodeNew || code_c[1] == kSpCodeNew);
+  issue_new(0, code_c[0], row_c[0]);
+  issue_new(1, code_c[1], row_c[1]);
   cp_async_commit();
 
   // ---- Q fragments (rows g0 = lane / 4 and g0 + 8; zeros past the last row) ----
-  if (!waited) pdl_wait();  // Q is the previous kernels' output; our output writes follow too
-  pdl_trigger();            // the next kernel may start streaming its own history
   const int g0 = lane >> 2, q4 = lane & 3;
   uint32_t qa[4][4];  // [k-step][a0..a3]
   {
@@ -349,7 +355,11 @@ attention_split_kernel(const __grid_constant__ AttnArgs a, const __grid_constant
   for (int dt = 0; dt < 8; ++dt) o[dt][0] = o[dt][1] = o[dt][2] = o[dt][3] = 0.f;
   for (int jj = 0; jj < mine; ++jj) {
     const int st = jj & 1;
-    cp_async_wait<1>();  // tile jj's copies (this lane's) have landed
+    if (jj == 0 && late) {
+      cp_async_wait<0>();  // tile 0's copies and the new-token rows of tiles 0 and 1
+    } else {
+      cp_async_wait<1>();  // tile jj's copies (this lane's) have landed
+    }
     __syncwarp();
     sp_convert_row(wsm + st * kSpRawStage, tile, lane, code_c[0]);
     __syncwarp();  // the whole tile is in shared memory; raw stage st is free
@@ -358,7 +368,7 @@ attention_split_kernel(const __grid_constant__ AttnArgs a, const __grid_constant
     row_c[0] = row_c[1];
     code_c[1] = code_c[2];
     row_c[1] = row_c[2];
-    issue_tile(st, code_c[1], row_c[1]);
+    issue_tile(st, code_c[1], row_c[1], true);
     cp_async_commit();
     load_map(jj + 3, code_c[2], row_c[2]);
 

@@ -415,7 +415,13 @@ class Region:
         return LIB.dkv_pool_mapped_bytes(self.handle)
 
     def map(self, nbytes):
-        _check(LIB.dkv_pool_map(self.handle, nbytes))
+        """Makes the first `nbytes` usable. Mapping is a driver call that can take
+        milliseconds, so a region that must grow maps at least twice what it has
+        (up to its reservation) and grows rarely."""
+        mapped = self.mapped
+        if nbytes <= mapped:
+            return
+        _check(LIB.dkv_pool_map(self.handle, max(nbytes, min(self.reserved, 2 * mapped))))
 
 
 class RegionLease:
@@ -440,14 +446,16 @@ _FREE_LOCK = threading.Lock()
 
 def lease_region(device, nbytes):
     """A region of at least `nbytes` of address space on `device` (torch.device):
-    the smallest fitting one of the free list, else a new reservation."""
+    from the free list the smallest fitting reservation, among equal ones the one
+    with the most memory mapped already (so it rarely has to map more); else a
+    new reservation."""
     index = device.index if device.index is not None else torch.cuda.current_device()
     taken = None
     with _FREE_LOCK:
         free = _FREE.get(index, [])
         fits = [i for i, (r, _) in enumerate(free) if r.reserved >= nbytes]
         if fits:
-            taken = free.pop(min(fits, key=lambda i: free[i][0].reserved))
+            taken = free.pop(min(fits, key=lambda i: (free[i][0].reserved, -free[i][0].mapped)))
     if taken is not None:
         region, stream = taken
         current = torch.cuda.current_stream(index)

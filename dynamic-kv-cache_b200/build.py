@@ -1,12 +1,15 @@
-"""Builds libdkv.so (the sm_100a CUDA library) in-tree with nvcc.
+"""Builds libdkv.so (the sm_100a CUDA library) in-tree with nvcc, and the C++
+host binding of GPUCache's per-layer calls (_dkv_torch, csrc/torch_ops.cpp) with
+g++ against PyTorch's headers.
 
 The library is compiled for sm_100a only, without fast-math (the pack kernel
-relies on IEEE fp32 division and subtraction for bit-exact codes), and is placed
-next to this file so it travels with the source tree.
+relies on IEEE fp32 division and subtraction for bit-exact codes); both files are
+placed next to this file so they travel with the source tree.
 """
 import os
 import subprocess
 import sys
+import sysconfig
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
@@ -33,16 +36,44 @@ def stale():
     return any(p.stat().st_mtime > built for p in inputs)
 
 
-def build(force=False, verbose=False):
-    """Compiles libdkv.so if any source is newer than it; returns its path."""
-    if not force and not stale():
-        return LIB
-    tmp = LIB.with_suffix('.so.tmp')
-    cmd = [_nvcc(), *NVCC_FLAGS, '-I', str(INCLUDE), '-o', str(tmp), *[str(CSRC / s) for s in SOURCES]]
+BINDING = HERE / ('_dkv_torch' + sysconfig.get_config_var('EXT_SUFFIX'))
+BINDING_SOURCE = CSRC / 'torch_ops.cpp'
+
+
+def build_binding(verbose=False):
+    """Compiles the C++ host binding (a CPython extension over libdkv.so's C ABI,
+    using PyTorch's tensor and stream types) next to libdkv.so."""
+    import torch
+    from torch.utils import cpp_extension as ce
+    tmp = BINDING.with_name(BINDING.name + '.tmp')
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    cmd = ['g++', '-O2', '-std=c++17', '-shared', '-fPIC', '-DTORCH_EXTENSION_NAME=_dkv_torch',
+           '-DTORCH_API_INCLUDE_EXTENSION_H', f'-D_GLIBCXX_USE_CXX11_ABI={abi}',
+           '-I', str(INCLUDE), '-I', sysconfig.get_paths()['include'],
+           *[f'-I{p}' for p in ce.include_paths(device_type='cuda')],
+           str(BINDING_SOURCE), '-o', str(tmp), '-L', str(HERE), '-ldkv', "-Wl,-rpath,$ORIGIN",
+           *[f'-L{p}' for p in ce.library_paths(device_type='cuda')],
+           '-lc10', '-lc10_cuda', '-ltorch', '-ltorch_cpu', '-ltorch_python', '-lcudart']
     if verbose:
         print(' '.join(cmd), file=sys.stderr)
     subprocess.run(cmd, check=True)
-    os.replace(tmp, LIB)
+    os.replace(tmp, BINDING)
+    return BINDING
+
+
+def build(force=False, verbose=False):
+    """Compiles libdkv.so if any source is newer than it, and the host binding if
+    it or libdkv.so is newer than the binding; returns libdkv.so's path."""
+    if force or stale():
+        tmp = LIB.with_suffix('.so.tmp')
+        cmd = [_nvcc(), *NVCC_FLAGS, '-I', str(INCLUDE), '-o', str(tmp), *[str(CSRC / s) for s in SOURCES]]
+        if verbose:
+            print(' '.join(cmd), file=sys.stderr)
+        subprocess.run(cmd, check=True)
+        os.replace(tmp, LIB)
+    if force or not BINDING.exists() or any(p.stat().st_mtime > BINDING.stat().st_mtime
+                                            for p in [LIB, BINDING_SOURCE, *INCLUDE.glob('*.h')]):
+        build_binding(verbose)
     return LIB
 
 

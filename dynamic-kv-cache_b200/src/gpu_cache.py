@@ -87,6 +87,13 @@ class GPUCache(DynamicCache):
         self.host_counts = counts
         # Device status word written by the kernels (first error code, detail index).
         self.status = torch.zeros(4, dtype=torch.int32, device=self.device)
+        self._refresh_ptrs()
+
+    def _refresh_ptrs(self):
+        """Device addresses the per-layer calls pass (pools, maps, status word): one
+        list, renewed whenever a pool tensor changes."""
+        self._ptrs = [t.data_ptr() for t in (self.p4, self.m4, self.p8, self.m8, self.p16, self.rows, self.codes,
+                                             self.status)]
 
     # -- capacity ---------------------------------------------------------------
     def _page_shape(self, name, pages):
@@ -139,6 +146,7 @@ class GPUCache(DynamicCache):
             if b == bits:
                 self._grow(name, cap)
         self.caps[bits] = cap
+        self._refresh_ptrs()
 
     def pool_rows(self, name, layer, kv, start, n):
         """Rows [start, start + n) of pool `name` ('p4', 'm4', 'p8', 'm8', 'p16')
@@ -200,8 +208,8 @@ class GPUCache(DynamicCache):
         if k.shape[0] != 1 or k.shape[-1] != self.dim or k.device.type != 'cuda':
             raise ValueError('GPU cache requires CUDA, batch one and the configured head dimension')
         past, n, row = self._claim(layer, k.shape[-2])
-        K.pack_rows(k, v, *self._pools(), layer, row, n, self.caps[4], self.caps[8], self.caps[16],
-                    self.heads, self.dim, self.pending_bits, self.layers, self.status)
+        K.FAST.pack(k, v, self._ptrs, layer, row, (self.caps[4], self.caps[8], self.caps[16]), self.heads,
+                    self.pending_bits, self.layers)
         self.seen[layer] = past + n
         return past
 
@@ -215,11 +223,9 @@ class GPUCache(DynamicCache):
         n = q.shape[-2]
         new_segment = self.online and layer == 0
         past, n, row = self._claim(layer, k.shape[-2], fill_map=False)
-        out = torch.empty((1, n, q.shape[1], self.dim), dtype=q.dtype, device=q.device)
-        K.append_attention(q, k, v, *self._pools(), self.rows, self.codes, out, layer, past, n, row,
-                           self.pending_bits, new_segment, self.capacity, self.caps[4], self.caps[8], self.caps[16],
-                           self.heads, q.shape[1] // self.heads, self.dim, self.block_m, self.block_n, self.layers,
-                           self.status)
+        out = K.FAST.append_attend(q, k, v, self._ptrs, layer, past, row, self.pending_bits, new_segment,
+                                   self.capacity, (self.caps[4], self.caps[8], self.caps[16]), self.heads,
+                                   self.block_m, self.block_n, self.layers)
         self.seen[layer] = past + n
         return out
 
@@ -271,12 +277,8 @@ class GPUCache(DynamicCache):
     def attend(self, q, k, v, layer, past):
         """Causal GQA attention of the n new queries over the packed history plus
         the native new K/V; returns [1, n, query_heads, dim] (src/gpu_cache.py:96-104)."""
-        n = q.shape[-2]
-        out = torch.empty((1, n, q.shape[1], self.dim), dtype=q.dtype, device=q.device)
-        K.packed_attention(q, k, v, *self._pools(), self.rows, self.codes, out, layer, past, n,
-                           self.caps[4], self.caps[8], self.caps[16], self.heads, q.shape[1] // self.heads,
-                           self.dim, self.block_m, self.block_n, self.layers, self.status)
-        return out
+        return K.FAST.attend(q, k, v, self._ptrs, layer, past, (self.caps[4], self.caps[8], self.caps[16]),
+                             self.heads, self.block_m, self.block_n, self.layers)
 
     def attend_batched(self, q, k, v, layer, past):
         """B independent query chunks over the same packed history (batched candidate

@@ -101,6 +101,12 @@ def _load():
 
 
 LIB = _load()
+
+try:  # the C++ host binding of the per-layer calls (csrc/torch_ops.cpp), built with libdkv.so
+    import _dkv_torch as FAST
+except ImportError as e:
+    raise ImportError(f'{_LIB_PATH.with_name("_dkv_torch")}*.so is not built or does not load ({e}); run '
+                      '`python __graft_entry__.py build` first. There is no CPU fallback.') from e
 EXPORTS = ('dkv_version', 'dkv_last_error', 'dkv_pack_rows', 'dkv_packed_attention',
            'dkv_packed_attention_workspace', 'dkv_packed_attention_launches', 'dkv_packed_attention_batched',
            'dkv_packed_attention_batched_workspace', 'dkv_reconstruct', 'dkv_map_fill', 'dkv_pack_rows_many',
@@ -166,24 +172,14 @@ def attention_launches(past, nq, heads, group, dim=64):
     return n
 
 
-# Attention workspaces, one per (device, stream): the library keeps the merge
-# counters at the head of a workspace zero between calls, so a workspace is
-# zero-filled once and reused; calls on one stream never overlap, calls on
-# different streams get different workspaces. Outgrown workspaces stay referenced
-# so that CUDA graphs captured with them keep valid addresses.
-_WORKSPACES = {}
-_RETIRED = []
-
-
 def _workspace(device, stream, size):
-    key = (device.index, stream)
-    ws = _WORKSPACES.get(key)
-    if ws is None or ws.numel() < size:
-        if ws is not None:
-            _RETIRED.append(ws)
-        ws = torch.zeros(size, dtype=torch.uint8, device=device)
-        _WORKSPACES[key] = ws
-    return ws
+    """The attention workspace of (device, stream) with at least `size` bytes. One
+    registry (in the C++ binding) serves both host paths: the library leaves the
+    merge counters at a workspace's head zero after every call, so a workspace is
+    zero-filled once and reused; calls on one stream never overlap, calls on other
+    streams get other workspaces; outgrown ones stay referenced, so CUDA graphs
+    captured with them keep valid addresses. `stream` is the current stream."""
+    return FAST.workspace(torch.empty(0, device=device), size)
 
 
 def packed_attention(q, knew, vnew, p4, m4, p8, m8, p16, rows, codes, out, layer, past, nq, cap4, cap8,

@@ -34,5 +34,5 @@ def test_merge_counters_return_to_zero(cuda):
         run_case(*case)
         run_case(*case, seed=1)
     torch.cuda.synchronize()
-    ws = K._WORKSPACES[(torch.cuda.current_device(), torch.cuda.current_stream().cuda_stream)]
+    ws = K._workspace(torch.device('cuda', torch.cuda.current_device()), None, 1)  # this stream's workspace
     assert int(ws[:1024].count_nonzero()) == 0

@@ -6,6 +6,7 @@
 // kernels from Python once per layer (src/gpu_cache.py:90-92, 99-103), so this host
 // cost is paid on every layer of every frame.
 #include <torch/extension.h>
+#include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
 
 #include <map>
@@ -89,6 +90,7 @@ at::Tensor attend(const at::Tensor& q_in, const at::Tensor& k_in, const at::Tens
   check_ptrs(p, caps);
   const at::Tensor q = rows_ready(q_in), k = rows_ready(k_in), v = rows_ready(v_in);
   same_device(q, k, v);
+  const c10::cuda::CUDAGuard guard(q.device());  // the library launches on the current device
   const int64_t nq = q.size(2), hq = q.size(1);
   if (heads <= 0 || hq % heads) throw pybind11::value_error("query heads must be a positive multiple of KV heads");
   const int64_t group = hq / heads;
@@ -111,6 +113,7 @@ void pack(const at::Tensor& k_in, const at::Tensor& v_in, const Ptrs& p, int64_t
   check_ptrs(p, caps);
   const at::Tensor k = rows_ready(k_in), v = rows_ready(v_in);
   same_device(k, k, v);
+  const c10::cuda::CUDAGuard guard(k.device());
   check(dkv_pack_rows(k.data_ptr(), v.data_ptr(), vp(p[0]), vp(p[1]), vp(p[2]), vp(p[3]), vp(p[4]), k.stride(1),
                       k.stride(2), v.stride(1), v.stride(2), layer, row_start, k.size(2), caps[0], caps[1], caps[2],
                       heads, k.size(3), bits, layers, static_cast<int32_t*>(vp(p[7])), current_stream(k)));
@@ -125,6 +128,7 @@ at::Tensor append_attend(const at::Tensor& q_in, const at::Tensor& k_in, const a
   check_ptrs(p, caps);
   const at::Tensor q = rows_ready(q_in), k = rows_ready(k_in), v = rows_ready(v_in);
   same_device(q, k, v);
+  const c10::cuda::CUDAGuard guard(q.device());  // the library launches on the current device
   const int64_t nq = q.size(2), hq = q.size(1);
   if (heads <= 0 || hq % heads) throw pybind11::value_error("query heads must be a positive multiple of KV heads");
   const int64_t group = hq / heads;

@@ -24,6 +24,9 @@ cudaError_t launch_rotary(const void* x, const float* cos_t, const float* sin_t,
                           int64_t cb, int b, int n, int heads, cudaStream_t stream);
 cudaError_t launch_silu_mul(const void* gate, const void* up, void* out, int64_t gs, int64_t us, int64_t rows,
                             int width, cudaStream_t stream);
+cudaError_t launch_add_rms_norm(const void* x, const void* y, void* x_out, void* h_out, const void* weight,
+                                int64_t rows, int width, int64_t xs, int64_t ys, int64_t os, int64_t hs, float eps,
+                                cudaStream_t stream);
 cudaError_t launch_pack_many(const void* k, const void* v, const dkv_pack_target* targets, bool on_device, int count,
                              int64_t kh, int64_t kt, int64_t vh, int64_t vt, int64_t kc, int64_t vc, int layer, int n,
                              int heads, int blocks, cudaStream_t stream);
@@ -574,6 +577,24 @@ int dkv_silu_mul(const void* gate, const void* up, void* out, int64_t gs, int64_
                     cuda_status(dkv::launch_silu_mul(gate, up, out, gs, us, rows, width,
                                                      static_cast<cudaStream_t>(stream)),
                                 "silu_mul launch"));
+}
+
+int dkv_add_rms_norm(const void* x, const void* y, void* x_out, void* h_out, const void* weight, int64_t rows,
+                     int32_t width, int64_t xs, int64_t ys, int64_t os, int64_t hs, float eps, void* stream) {
+  if (rows < 0 || width <= 0 || width % 8 || width > 2048)
+    return fail(DKV_EINVAL, "add_rms_norm: width must be a multiple of 8 in [8, 2048]");
+  if (rows == 0) return ok();
+  if (!x || !h_out || !weight || (y != nullptr && x_out == nullptr)) return fail(DKV_EINVAL, "add_rms_norm: null pointer");
+  if (!aligned16(x) || !aligned16(h_out) || !aligned16(weight) || (y && (!aligned16(y) || !aligned16(x_out))))
+    return fail(DKV_EINVAL, "add_rms_norm: tensors must be 16-byte aligned");
+  if (xs < width || hs < width || xs % 8 || hs % 8 || (y && (ys < width || os < width || ys % 8 || os % 8)))
+    return fail(DKV_EINVAL, "add_rms_norm: row strides must hold a row and be multiples of 8 elements");
+  if (!(eps >= 0.f)) return fail(DKV_EINVAL, "add_rms_norm: eps must be non-negative");
+  if (rows > INT32_MAX / 32) return fail(DKV_EINVAL, "add_rms_norm: too many rows");
+  return note_write(stream, kWroteNothing,
+                    cuda_status(dkv::launch_add_rms_norm(x, y, x_out, h_out, weight, rows, width, xs, ys, os, hs, eps,
+                                                         static_cast<cudaStream_t>(stream)),
+                                "add_rms_norm launch"));
 }
 
 }  // extern "C"

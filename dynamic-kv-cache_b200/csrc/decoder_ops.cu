@@ -9,9 +9,16 @@
 //                    products, sum, downcast) become one.
 // silu_mul_kernel <- activation_product, silu(gate) * up (src/gpu_ops.py:14-17):
 //                    two launches become one.
+// add_rms_norm_kernel <- the decoder layer's residual add followed by the next
+//                    RMSNorm and its weight (cuda_rms, src/gpu_ops.py:9-12): three
+//                    launches become one. Its rounding points are PyTorch's (the sum
+//                    rounded to bf16, the normalised row rounded to bf16 before the
+//                    weight product), but its fp32 sum of squares has its own order,
+//                    so the normalised output can differ from torch's rms_norm in the
+//                    last bf16 bit; it serves the streaming decoder, not cuda_rms.
 //
-// Both keep PyTorch's rounding points exactly, so their outputs are bit-identical
-// to the PyTorch ops they replace: every product and sum is one IEEE fp32 operation
+// The first two keep PyTorch's rounding points exactly, so their outputs are
+// bit-identical to the PyTorch ops they replace: every product and sum is one IEEE fp32 operation
 // rounded to nearest (no contraction into FMA), and each value PyTorch stores as
 // bf16 is rounded to bf16 (nearest-even) at the same point.
 #include "dkv_common.cuh"
@@ -108,6 +115,57 @@ silu_mul_kernel(const uint16_t* __restrict__ gate, const uint16_t* __restrict__ 
   store8(out + row * width + col, y);
 }
 
+// One warp per row of `width` (<= kNormMaxWidth) elements: with `y`, x_out = bf16(x +
+// y) (fp32 sum rounded, PyTorch's bf16 add) and the norm is taken of x_out; without
+// it, of x. Sum of squares in fp32 (each lane its chunks in order, then a fixed xor
+// butterfly), rstd = rsqrt(sum / width + eps), h = bf16(bf16(v * rstd) * weight).
+// Rows of x / y / x_out / h_out start xs / ys / os / hs elements apart.
+constexpr int kNormMaxWidth = 2048;  // 8 chunks of 8 per lane
+template <bool ADD>
+__global__ void __launch_bounds__(kOpThreads)
+add_rms_norm_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ y, uint16_t* __restrict__ x_out,
+                    uint16_t* __restrict__ h_out, const uint16_t* __restrict__ weight, int64_t rows, int width,
+                    int64_t xs, int64_t ys, int64_t os, int64_t hs, float eps) {
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+  const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;  // whole warps leave together
+  const int chunks = width / 8;
+  float v[kNormMaxWidth / 256][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kNormMaxWidth / 256; ++i) {
+    const int c = lane + 32 * i;
+    if (c < chunks) {
+      load8(x + row * xs + c * 8, v[i]);
+      if (ADD) {
+        float b[8];
+        load8(y + row * ys + c * 8, b);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] = __bfloat162float(__float2bfloat16_rn(__fadd_rn(v[i][j], b[j])));
+        store8(x_out + row * os + c * 8, v[i]);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss = __fmaf_rn(v[i][j], v[i][j], ss);
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  const float rstd = rsqrtf(__fdiv_rn(ss, static_cast<float>(width)) + eps);
+#pragma unroll
+  for (int i = 0; i < kNormMaxWidth / 256; ++i) {
+    const int c = lane + 32 * i;
+    if (c < chunks) {
+      float w[8], h[8];
+      load8(weight + c * 8, w);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) h[j] = __fmul_rn(__bfloat162float(__float2bfloat16_rn(__fmul_rn(v[i][j], rstd))), w[j]);
+      store8(h_out + row * hs + c * 8, h);
+    }
+  }
+}
+
 namespace {
 
 // Launched as a programmatic dependent, like the pack kernel: each kernel waits
@@ -142,6 +200,19 @@ cudaError_t launch_silu_mul(const void* gate, const void* up, void* out, int64_t
   const int64_t total = rows * (width / 8);
   return launch_pdl(total, stream, silu_mul_kernel, static_cast<const uint16_t*>(gate),
                     static_cast<const uint16_t*>(up), static_cast<uint16_t*>(out), gs, us, width, total);
+}
+
+cudaError_t launch_add_rms_norm(const void* x, const void* y, void* x_out, void* h_out, const void* weight,
+                                int64_t rows, int width, int64_t xs, int64_t ys, int64_t os, int64_t hs, float eps,
+                                cudaStream_t stream) {
+  const auto* xx = static_cast<const uint16_t*>(x);
+  const auto* yy = static_cast<const uint16_t*>(y);
+  auto* xo = static_cast<uint16_t*>(x_out);
+  auto* ho = static_cast<uint16_t*>(h_out);
+  const auto* w = static_cast<const uint16_t*>(weight);
+  if (y != nullptr)
+    return launch_pdl(rows * 32, stream, add_rms_norm_kernel<true>, xx, yy, xo, ho, w, rows, width, xs, ys, os, hs, eps);
+  return launch_pdl(rows * 32, stream, add_rms_norm_kernel<false>, xx, yy, xo, ho, w, rows, width, xs, ys, os, hs, eps);
 }
 
 }  // namespace dkv

@@ -145,10 +145,39 @@ at::Tensor append_attend(const at::Tensor& q_in, const at::Tensor& k_in, const a
   return out;
 }
 
+// The decoder layer's x + y followed by RMSNorm and its weight (dkv_add_rms_norm)
+// over the rows of x / y [..., width]: returns (x + y, norm) — (x, norm) without y.
+std::vector<at::Tensor> add_rms_norm(const at::Tensor& x_in, const c10::optional<at::Tensor>& y_in,
+                                     const at::Tensor& weight_in, double eps) {
+  if (!x_in.is_cuda() || x_in.scalar_type() != at::kBFloat16 || weight_in.scalar_type() != at::kBFloat16)
+    throw pybind11::value_error("add_rms_norm takes CUDA bfloat16 tensors");
+  const int64_t width = x_in.size(-1);
+  const at::Tensor x = x_in.contiguous(), w = weight_in.contiguous();
+  if (w.numel() != width || w.device() != x.device()) throw pybind11::value_error("add_rms_norm: weight must be [width]");
+  const c10::cuda::CUDAGuard guard(x.device());
+  at::Tensor h = at::empty_like(x);
+  at::Tensor x_out = x;
+  const void* yp = nullptr;
+  at::Tensor y;
+  if (y_in.has_value()) {
+    y = y_in->contiguous();
+    if (y.sizes() != x.sizes() || y.scalar_type() != at::kBFloat16 || y.device() != x.device())
+      throw pybind11::value_error("add_rms_norm: y must match x");
+    yp = y.data_ptr();
+    x_out = at::empty_like(x);
+  }
+  const int64_t rows = width ? x.numel() / width : 0;
+  check(dkv_add_rms_norm(x.data_ptr(), yp, yp ? x_out.data_ptr() : nullptr, h.data_ptr(), w.data_ptr(), rows,
+                         static_cast<int32_t>(width), width, width, width, width, static_cast<float>(eps),
+                         current_stream(x)));
+  return {x_out, h};
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "C++ host path of GPUCache's per-layer calls into libdkv.so";
   m.def("workspace", &workspace);
   m.def("attend", &attend);
   m.def("pack", &pack);
   m.def("append_attend", &append_attend);
+  m.def("add_rms_norm", &add_rms_norm);
 }

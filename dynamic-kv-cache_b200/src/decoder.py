@@ -17,7 +17,7 @@ import torch.nn.functional as F
 
 from . import gpu_kernels as K
 from .gpu_cache import GPUCache, RequestBatch, append_many, attend_many
-from .gpu_ops import activation_product, cuda_rms
+from .gpu_ops import activation_product, add_rms, cuda_rms
 
 
 @dataclass(frozen=True)
@@ -98,6 +98,26 @@ class Decoder(torch.nn.Module):
     def rms(self, x, weight):
         return cuda_rms(x, weight, self.cfg.rms_eps)
 
+    def add_norm(self, x, y, weight):
+        """(x + y, its RMSNorm * weight): the residual add and the next norm of a
+        layer in one call (one launch on CUDA); y None: (x, norm of x)."""
+        return add_rms(x, y, weight, self.cfg.rms_eps)
+
+    def run_layers(self, x, attend):
+        """The decoder layers over x: attend(h, layer) is a layer's attention of the
+        normed input h, o_proj included. Returns the last residual stream."""
+        c = self.cfg
+        x, h = self.add_norm(x, None, self.norm_attn[0])
+        for layer in range(c.layers):
+            x, h = self.add_norm(x, attend(h, layer), self.norm_mlp[layer])
+            gate, up = F.linear(h, self.gate_up[layer]).chunk(2, dim=-1)
+            m = F.linear(activation_product(gate, up), self.down[layer])
+            if layer + 1 < c.layers:
+                x, h = self.add_norm(x, m, self.norm_attn[layer + 1])
+            else:
+                x = x + m
+        return x
+
     def project_qkv(self, x, layer, cos, sin):
         """q [B, q_heads, n, d] and k / v [B, kv_heads, n, d] of x [B, n, hidden]: one
         joined projection and one rotary pass over the query and key heads together
@@ -171,11 +191,7 @@ class Decoder(torch.nn.Module):
         pasts = torch.tensor([c.get_seq_length(0) for c in caches], device=x.device)
         positions = pasts[:, None] + torch.arange(n, device=x.device)[None, :]  # [B, n]
         cos, sin = self.rotary(positions, b, n, x.device)
-        for layer in range(self.cfg.layers):
-            x = x + self.attention_many(self.rms(x, self.norm_attn[layer]), layer, caches, cos, sin)
-            h = self.rms(x, self.norm_mlp[layer])
-            gate, up = F.linear(h, self.gate_up[layer]).chunk(2, dim=-1)
-            x = x + F.linear(activation_product(gate, up), self.down[layer])
+        x = self.run_layers(x, lambda h, layer: self.attention_many(h, layer, caches, cos, sin))
         if not logits:
             return None
         h = self.rms(x[:, -logits:], self.norm_out)
@@ -189,9 +205,10 @@ class Decoder(torch.nn.Module):
         c = self.cfg
         b, n = x.shape[0], x.shape[1]
         cos, sin = self.rotary(batch.positions, b, n, x.device)
-        for layer in range(c.layers):
-            q, k, v = self.project_qkv(self.rms(x, self.norm_attn[layer]), layer, cos, sin)
-            out = torch.empty((b, n, c.q_heads, c.head_dim), dtype=x.dtype, device=x.device)
+
+        def attend(h, layer):
+            q, k, v = self.project_qkv(h, layer, cos, sin)
+            out = torch.empty((b, n, c.q_heads, c.head_dim), dtype=h.dtype, device=h.device)
             if batch.append:
                 K.append_attention_many_device(q, k, v, batch.targets_ptr, batch.histories_ptr, b, batch.max_past,
                                                out, layer, n, c.kv_heads, c.q_heads // c.kv_heads, c.head_dim,
@@ -199,10 +216,9 @@ class Decoder(torch.nn.Module):
             else:
                 K.packed_attention_many_device(q, k, v, batch.histories_ptr, b, batch.max_past, out, layer, n,
                                                c.kv_heads, c.q_heads // c.kv_heads, c.head_dim, c.layers)
-            x = x + F.linear(out.reshape(b, n, -1), self.o[layer])
-            h = self.rms(x, self.norm_mlp[layer])
-            gate, up = F.linear(h, self.gate_up[layer]).chunk(2, dim=-1)
-            x = x + F.linear(activation_product(gate, up), self.down[layer])
+            return F.linear(out.reshape(b, n, -1), self.o[layer])
+
+        x = self.run_layers(x, attend)
         if not logits:
             return None
         h = self.rms(x[:, -logits:], self.norm_out)
@@ -216,11 +232,7 @@ class Decoder(torch.nn.Module):
         n = x.shape[1]
         past = cache.get_seq_length(0)
         cos, sin = self.rotary(torch.arange(past, past + n, device=x.device), 1, n, x.device)
-        for layer in range(self.cfg.layers):
-            x = x + self.attention_chunks(self.rms(x, self.norm_attn[layer]), layer, cache, cos, sin)
-            h = self.rms(x, self.norm_mlp[layer])
-            gate, up = F.linear(h, self.gate_up[layer]).chunk(2, dim=-1)
-            x = x + F.linear(activation_product(gate, up), self.down[layer])
+        x = self.run_layers(x, lambda h, layer: self.attention_chunks(h, layer, cache, cos, sin))
         h = self.rms(x[:, -logits:], self.norm_out)
         return F.linear(h, self.embed).float()
 
@@ -232,11 +244,7 @@ class Decoder(torch.nn.Module):
         n = x.shape[1]
         past = cache.get_seq_length(0)
         cos, sin = self.rotary(torch.arange(past, past + n, device=x.device), 1, n, x.device)
-        for layer in range(self.cfg.layers):
-            x = x + self.attention(self.rms(x, self.norm_attn[layer]), layer, cache, cos, sin)
-            h = self.rms(x, self.norm_mlp[layer])
-            gate, up = F.linear(h, self.gate_up[layer]).chunk(2, dim=-1)
-            x = x + F.linear(activation_product(gate, up), self.down[layer])
+        x = self.run_layers(x, lambda h, layer: self.attention(h, layer, cache, cos, sin))
         if not logits:
             return None
         h = self.rms(x[:, -logits:], self.norm_out)

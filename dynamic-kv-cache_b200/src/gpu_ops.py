@@ -20,6 +20,22 @@ def cuda_rms(x, weight, eps):
     return torch.nn.functional.rms_norm(x, (x.shape[-1],), None, eps) * weight
 
 
+def add_rms(x, y, weight, eps):
+    """(x + y, RMSNorm(x + y) * weight), or (x, RMSNorm(x) * weight) when y is None:
+    the decoder layer's residual add and the next norm. On CUDA bf16 one
+    dkv_add_rms_norm launch (PyTorch's rounding points, its own fp32 reduction
+    order: the norm can differ from cuda_rms in the last bf16 bit); elsewhere the
+    PyTorch ops. Not in the reference, whose decoder makes the add and cuda_rms
+    separate calls."""
+    if x.is_cuda and x.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16 and x.shape[-1] <= 2048 \
+            and x.shape[-1] % 8 == 0:
+        out = K.FAST.add_rms_norm(x, y, weight, eps)
+        return out[0], out[1]
+    if y is not None:
+        x = x + y
+    return x, cuda_rms(x, weight, eps)
+
+
 def activation_product(gate, up):
     """silu(gate) * up (src/gpu_ops.py:14-17): one dkv_silu_mul launch for CUDA bf16
     tensors, the reference's PyTorch form otherwise."""

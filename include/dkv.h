@@ -427,6 +427,19 @@ int dkv_rotary(const void* x, const float* cos_t, const float* sin_t, void* out,
 int dkv_silu_mul(const void* gate, const void* up, void* out, int64_t gs, int64_t us,
                  int64_t rows, int32_t width, void* stream);
 
+/*
+ * Residual add + RMSNorm + weight over `rows` rows of `width` (8..2048, a multiple
+ * of 8) elements, one launch (the decoder layer's x = x + y, then cuda_rms,
+ * src/gpu_ops.py:9-12, of the new x): x_out = bf16(x + y); h_out =
+ * bf16(bf16(x_out * rsqrt(mean(x_out^2) + eps)) * weight). With y == NULL there
+ * is no add and the norm is of x (x_out unused). The rounding points are
+ * PyTorch's; the fp32 sum of squares has this kernel's own order, so h_out may
+ * differ from torch.nn.functional.rms_norm in the last bf16 bit. bf16 tensors,
+ * row strides xs / ys / os / hs in elements, weight [width] contiguous.
+ */
+int dkv_add_rms_norm(const void* x, const void* y, void* x_out, void* h_out, const void* weight, int64_t rows,
+                     int32_t width, int64_t xs, int64_t ys, int64_t os, int64_t hs, float eps, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -71,3 +71,33 @@ def test_activation_product_routes_cuda_bf16_to_the_kernel(cuda):
                        (torch.nn.functional.silu(gate) * up).view(torch.int16))
     g32, u32 = gate.float(), up.float()  # other dtypes keep the reference's PyTorch form
     assert torch.equal(activation_product(g32, u32), torch.nn.functional.silu(g32) * u32)
+
+
+@pytest.mark.parametrize('shape', [(8, 64, 960), (1, 25, 960), (1, 1, 64), (3, 7, 2048)])
+def test_add_rms_norm_against_torch(cuda, shape):
+    """x + y is PyTorch's bf16 add bit for bit; the norm keeps PyTorch's rounding points
+    and, its fp32 sum of squares running in another order, differs from
+    rms_norm(x + y) * w by at most one bf16 unit after the norm and one more after the
+    weight product (2 units in the last place), on every element."""
+    from src.gpu_ops import add_rms
+    gen = torch.Generator().manual_seed(sum(shape))
+    x = (torch.randn(*shape, generator=gen) * 3).bfloat16().cuda()
+    y = (torch.randn(*shape, generator=gen) * 3).bfloat16().cuda()
+    w = (1 + 0.1 * torch.randn(shape[-1], generator=gen)).bfloat16().cuda()
+    s, h = add_rms(x, y, w, 1e-5)
+    ref_s = x + y
+    ref_h = torch.nn.functional.rms_norm(ref_s, (shape[-1],), None, 1e-5) * w
+    assert torch.equal(s.view(torch.int16), ref_s.view(torch.int16))
+    ulps = (h.view(torch.int16).int() - ref_h.view(torch.int16).int()).abs()
+    assert int(ulps.max()) <= 2, int(ulps.max())
+    s2, h2 = add_rms(x, None, w, 1e-5)  # no add: the norm of x itself
+    assert s2 is x
+    ref2 = torch.nn.functional.rms_norm(x, (shape[-1],), None, 1e-5) * w
+    assert int((h2.view(torch.int16).int() - ref2.view(torch.int16).int()).abs().max()) <= 2
+
+
+def test_add_rms_norm_rejects_bad_widths(cuda):
+    from src import gpu_kernels as K
+    x = torch.zeros(2, 4100, device='cuda').bfloat16()
+    with pytest.raises(ValueError, match='width'):
+        K.FAST.add_rms_norm(x, None, torch.ones(4100, device='cuda').bfloat16(), 1e-5)

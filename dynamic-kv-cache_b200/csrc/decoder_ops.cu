@@ -121,8 +121,9 @@ silu_mul_kernel(const uint16_t* __restrict__ gate, const uint16_t* __restrict__ 
 // butterfly), rstd = rsqrt(sum / width + eps), h = bf16(bf16(v * rstd) * weight).
 // Rows of x / y / x_out / h_out start xs / ys / os / hs elements apart.
 constexpr int kNormMaxWidth = 2048;  // 8 chunks of 8 per lane
+constexpr int kNormThreads = 128;  // 4 rows per block: a 512-row step spreads over 128 SMs
 template <bool ADD>
-__global__ void __launch_bounds__(kOpThreads)
+__global__ void __launch_bounds__(kNormThreads)
 add_rms_norm_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ y, uint16_t* __restrict__ x_out,
                     uint16_t* __restrict__ h_out, const uint16_t* __restrict__ weight, int64_t rows, int width,
                     int64_t xs, int64_t ys, int64_t os, int64_t hs, float eps) {
@@ -133,11 +134,13 @@ add_rms_norm_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__
   if (row >= rows) return;  // whole warps leave together
   const int chunks = width / 8;
   float v[kNormMaxWidth / 256][8];
+  uint4 wv[kNormMaxWidth / 256];  // the weights, loaded with the row (no second round trip)
   float ss = 0.f;
 #pragma unroll
   for (int i = 0; i < kNormMaxWidth / 256; ++i) {
     const int c = lane + 32 * i;
     if (c < chunks) {
+      wv[i] = __ldg(reinterpret_cast<const uint4*>(weight + c * 8));
       load8(x + row * xs + c * 8, v[i]);
       if (ADD) {
         float b[8];
@@ -158,7 +161,10 @@ add_rms_norm_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__
     const int c = lane + 32 * i;
     if (c < chunks) {
       float w[8], h[8];
-      load8(weight + c * 8, w);
+      w[0] = bf16_lo(wv[i].x); w[1] = bf16_hi(wv[i].x);
+      w[2] = bf16_lo(wv[i].y); w[3] = bf16_hi(wv[i].y);
+      w[4] = bf16_lo(wv[i].z); w[5] = bf16_hi(wv[i].z);
+      w[6] = bf16_lo(wv[i].w); w[7] = bf16_hi(wv[i].w);
 #pragma unroll
       for (int j = 0; j < 8; ++j) h[j] = __fmul_rn(__bfloat162float(__float2bfloat16_rn(__fmul_rn(v[i][j], rstd))), w[j]);
       store8(h_out + row * hs + c * 8, h);
@@ -173,10 +179,10 @@ namespace {
 // dependent (the attention kernel after the rotary) start its set-up, so the
 // dependent knows every kernel before this one has completed.
 template <class Kernel, class... Args>
-cudaError_t launch_pdl(int64_t threads, cudaStream_t stream, Kernel kernel, Args... args) {
+cudaError_t launch_pdl_block(int block, int64_t threads, cudaStream_t stream, Kernel kernel, Args... args) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>((threads + kOpThreads - 1) / kOpThreads));
-  cfg.blockDim = dim3(kOpThreads);
+  cfg.gridDim = dim3(static_cast<unsigned>((threads + block - 1) / block));
+  cfg.blockDim = dim3(block);
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -184,6 +190,11 @@ cudaError_t launch_pdl(int64_t threads, cudaStream_t stream, Kernel kernel, Args
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+template <class Kernel, class... Args>
+cudaError_t launch_pdl(int64_t threads, cudaStream_t stream, Kernel kernel, Args... args) {
+  return launch_pdl_block(kOpThreads, threads, stream, kernel, args...);
 }
 
 }  // namespace
@@ -211,8 +222,10 @@ cudaError_t launch_add_rms_norm(const void* x, const void* y, void* x_out, void*
   auto* ho = static_cast<uint16_t*>(h_out);
   const auto* w = static_cast<const uint16_t*>(weight);
   if (y != nullptr)
-    return launch_pdl(rows * 32, stream, add_rms_norm_kernel<true>, xx, yy, xo, ho, w, rows, width, xs, ys, os, hs, eps);
-  return launch_pdl(rows * 32, stream, add_rms_norm_kernel<false>, xx, yy, xo, ho, w, rows, width, xs, ys, os, hs, eps);
+    return launch_pdl_block(kNormThreads, rows * 32, stream, add_rms_norm_kernel<true>, xx, yy, xo, ho, w, rows, width,
+                            xs, ys, os, hs, eps);
+  return launch_pdl_block(kNormThreads, rows * 32, stream, add_rms_norm_kernel<false>, xx, yy, xo, ho, w, rows, width,
+                          xs, ys, os, hs, eps);
 }
 
 }  // namespace dkv

@@ -123,3 +123,29 @@ def test_fork_growth_leaves_the_base(cuda):
     assert torch.equal(c.pool_rows('p8', 0, 0, 0, 64), base_rows)
     c.check()
     b.check()
+
+
+def test_reserve_beyond_the_reservation_moves_once_and_keeps_rows(cuda):
+    """An explicit reserve() past what the cache's token capacity can need (the
+    reference allows any size) outgrows the reserved address space: the pool moves
+    to a larger region once, its rows copied, and everything keeps working."""
+    from src.gpu_cache import GPUCache
+    gen = torch.Generator().manual_seed(21)
+    c = GPUCache(None, layers=1, heads=5, max_tokens=256)
+    k = torch.randn(1, 5, 64, 64, generator=gen).bfloat16().cuda()
+    v = torch.randn(1, 5, 64, 64, generator=gen).bfloat16().cuda()
+    c.select(16, 0)
+    c.append(k, v, 0)
+    before = c.pool_rows('p16', 0, 0, 0, 64).clone()
+    ptr = c.p16.data_ptr()
+    c.reserve(16, 5000)  # far beyond ceil64(1.5 * 256) rows
+    assert c.caps[16] == 5000 and c.p16.data_ptr() != ptr and c.p16.shape[0] == (5000 + 63) // 64
+    assert torch.equal(c.pool_rows('p16', 0, 0, 0, 64), before)
+    q = torch.randn(1, 15, 8, 64, generator=gen).bfloat16().cuda()
+    kn = torch.randn(1, 5, 8, 64, generator=gen).bfloat16().cuda()
+    out = c.attend(q, kn, kn, 0, 64)
+    ref = GPUCache(None, layers=1, heads=5, max_tokens=256)
+    ref.select(16, 0)
+    ref.append(k, v, 0)
+    assert torch.equal(out, ref.attend(q, kn, kn, 0, 64))
+    c.check()

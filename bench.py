@@ -782,8 +782,10 @@ def main():
         'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': hbm, 'unit': 'GB/s', 'frac': achieved / hbm,
                      'traffic': NCU_TRAFFIC_BYTES, 'peak_kind': peak_kind,
                      'bytes_per_launch': bytes_call,
-                     'note': 'attention op per layer call: attention_tc_kernel (tcgen05 / TMEM), history splits merged '
-                             'in the same cooperative launch'},
+                     'note': 'attention op per layer call: attention_tc_kernel (tcgen05 / TMEM) + '
+                             'attention_combine_kernel (merge of the history splits)' if launches_per_call == 2 else
+                             'attention op per layer call: attention_tc_kernel (tcgen05 / TMEM), history splits '
+                             'merged in the same cooperative launch'},
         'roofline_tensor': {'bound': 'tensor', 'achieved': achieved_tf, 'peak': tflops, 'unit': 'TFLOP/s',
                             'frac': achieved_tf / tflops, 'peak_kind': peak_kind,
                             'flops_per_launch': attention_flops()},

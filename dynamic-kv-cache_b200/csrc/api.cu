@@ -199,7 +199,7 @@ int32_t dkv_packed_attention_launches(int32_t past, int32_t nq, int32_t heads, i
   const dkv::AttnPlan p = dkv::make_plan(past, nq, heads, group);
   if (p.splits == 1) return 1;
   bool fused = false;
-  if (dkv::attention_tc_merges_in_kernel(p, heads, &fused) != cudaSuccess) return -1;
+  if (dkv::attention_tc_merges_in_kernel(p, heads, true, &fused) != cudaSuccess) return -1;
   return fused ? 1 : 2;
 }
 

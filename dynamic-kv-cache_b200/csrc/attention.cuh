@@ -236,8 +236,9 @@ __device__ __forceinline__ float merge_row_weights(Load load, int splits, float*
 cudaError_t launch_attention_tc(AttnArgs& a, int heads, cudaStream_t stream, const HistoryTable* table = nullptr,
                                 const History* device_table = nullptr);
 // Whether a call with this plan merges its splits inside the tensor-core kernel
-// on the current device (one launch) or needs the combine kernel (two).
-cudaError_t attention_tc_merges_in_kernel(const AttnPlan& p, int heads, bool* fused);
+// on the current device (one launch) or needs the combine kernel (two);
+// attend_only: one request, no fused pack, no history table.
+cudaError_t attention_tc_merges_in_kernel(const AttnPlan& p, int heads, bool attend_only, bool* fused);
 cudaError_t launch_attention_combine(const AttnArgs& a, int heads, cudaStream_t stream);
 // The split-K kernel for plans of make_plan_split (a.hist holds the history).
 cudaError_t launch_attention_split(const AttnArgs& a, int heads, cudaStream_t stream);

@@ -1112,28 +1112,38 @@ cudaError_t configure(int& dev) {
   return cudaSuccess;
 }
 
-// DKV_ATTENTION_MERGE=combine keeps the split merge in the separate combine
-// kernel (for GPUs shared under MPS, where a grid may not be resident at once).
-bool merge_in_kernel_allowed() {
-  static const bool allowed = [] {
+// Where the splits of a call are merged. DKV_ATTENTION_MERGE=combine: always in the
+// separate combine kernel (for GPUs shared under MPS, where a grid may not be
+// resident at once); =kernel: inside the attention kernel whenever the grid fits.
+// Unset: the measured default, which is the combine kernel for single-request
+// attend-only calls (an eager cooperative launch costs more than the extra
+// launch there) and the in-kernel merge for everything else (fused pack,
+// batched requests), where one launch is faster.
+enum class MergeMode { kDefault, kCombine, kKernel };
+
+MergeMode merge_mode() {
+  static const MergeMode mode = [] {
     const char* v = getenv("DKV_ATTENTION_MERGE");
-    return !(v && strcmp(v, "combine") == 0);
+    if (v && strcmp(v, "combine") == 0) return MergeMode::kCombine;
+    if (v && strcmp(v, "kernel") == 0) return MergeMode::kKernel;
+    return MergeMode::kDefault;
   }();
-  return allowed;
+  return mode;
 }
 }  // namespace
 
-bool attention_tc_fused(const AttnPlan& p, int heads, int dev) {
+bool attention_tc_fused(const AttnPlan& p, int heads, int dev, bool attend_only) {
+  const MergeMode mode = merge_mode();
+  if (mode == MergeMode::kCombine || (mode == MergeMode::kDefault && attend_only)) return false;
   // in-kernel merge only when no CTA of a group can wait for one that is not yet resident
   const long long grid = static_cast<long long>(p.splits) * p.mblocks * heads;
-  return p.splits > 1 && heads * p.mblocks <= kSyncGroups && grid <= g_resident[dev] &&
-         merge_in_kernel_allowed();
+  return p.splits > 1 && heads * p.mblocks <= kSyncGroups && grid <= g_resident[dev];
 }
 
-cudaError_t attention_tc_merges_in_kernel(const AttnPlan& p, int heads, bool* fused) {
+cudaError_t attention_tc_merges_in_kernel(const AttnPlan& p, int heads, bool attend_only, bool* fused) {
   int dev = 0;
   const cudaError_t e = configure(dev);
-  *fused = e == cudaSuccess && attention_tc_fused(p, heads, dev);
+  *fused = e == cudaSuccess && attention_tc_fused(p, heads, dev, attend_only);
   return e;
 }
 
@@ -1145,7 +1155,9 @@ cudaError_t launch_attention_tc(AttnArgs& a, int heads, cudaStream_t stream, con
   AttnPlan p{};
   p.splits = a.splits;
   p.mblocks = a.mblocks;
-  a.fused = a.sync != nullptr && attention_tc_fused(p, heads, dev);
+  // one request (grid z = its KV heads), no fused pack, no history table
+  const bool attend_only = a.pack_mode == 0 && table == nullptr && device_table == nullptr && heads == a.heads;
+  a.fused = a.sync != nullptr && attention_tc_fused(p, heads, dev, attend_only);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.splits, a.mblocks, heads);
   cfg.blockDim = dim3(kThreadsTc);

@@ -103,14 +103,17 @@ int dkv_pack_rows(const void* k, const void* v,
  * A workspace belongs to one call at a time: calls that may overlap (different
  * streams) need different workspaces.
  *
- * When every block of the launch fits on the GPU at once (one block per SM, at
- * most 148 blocks) the history splits are merged inside the attention kernel:
- * one launch per call, made as a cooperative launch so that all its blocks are
- * co-scheduled (each waits for the others of its group; work on other streams
- * only delays the launch). Otherwise, or with the environment variable
- * DKV_ATTENTION_MERGE=combine (e.g. under MPS, where a grid may not be resident
- * at once), a second kernel merges them. Both merges do the same arithmetic in
- * the same order: the output is bit-identical either way.
+ * Calls whose history is split are merged by a second (combine) kernel: two
+ * launches per call. The fused and batched entry points (dkv_append_attention*,
+ * dkv_packed_attention_batched, the *_many calls) instead merge inside the
+ * attention kernel when every block of the launch fits on the GPU at once (one
+ * block per SM, at most 148 blocks): one launch, made as a cooperative launch so
+ * that all its blocks are co-scheduled (each waits for the others of its group;
+ * work on other streams only delays the launch). The environment variable
+ * DKV_ATTENTION_MERGE=kernel merges this call in the kernel too where the grid
+ * fits; =combine uses the combine kernel everywhere (e.g. under MPS, where a
+ * grid may not be resident at once). Both merges do the same arithmetic in the
+ * same order: the output is bit-identical either way.
  */
 int dkv_packed_attention(const void* q, const void* knew, const void* vnew,
                          const void* p4, const void* m4, const void* p8,

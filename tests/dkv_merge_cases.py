@@ -1,6 +1,6 @@
 """Seeded attention calls shared by the split-merge tests; run as a script it
 writes the outputs to the .npz named on the command line (used to run the same
-calls in a child process with DKV_ATTENTION_MERGE=combine)."""
+calls in a child process with another DKV_ATTENTION_MERGE setting)."""
 import sys
 from pathlib import Path
 
@@ -14,7 +14,10 @@ sys.path[:0] = [str(ROOT), str(ROOT / 'dynamic-kv-cache_b200')]
 CASES = [(8128, 64, 5, 3), (2000, 128, 5, 3), (16000, 16, 8, 4), (700, 64, 2, 7), (130, 64, 1, 1)]
 
 
-def run_case(past, nq, heads, group, seed=0):
+def run_case(past, nq, heads, group, seed=0, fused=False):
+    """append + attend of nq new rows over `past` packed rows (fused: one
+    append_attend call, which merges its splits inside the attention kernel by
+    default); returns the output and the launches dkv_packed_attention makes."""
     from src.gpu_cache import GPUCache
     from src import gpu_kernels as K
     gen = torch.Generator(device='cuda').manual_seed(seed + past)
@@ -32,8 +35,12 @@ def run_case(past, nq, heads, group, seed=0):
     kn = torch.randn(1, heads, nq, 64, generator=gen, device='cuda').bfloat16()
     vn = torch.randn(1, heads, nq, 64, generator=gen, device='cuda').bfloat16()
     cache.select(16)
-    p = cache.append(kn, vn, 0)
-    out = cache.attend(q, kn, vn, 0, p)
+    if fused:
+        p = past
+        out = cache.append_attend(q, kn, vn, 0)
+    else:
+        p = cache.append(kn, vn, 0)
+        out = cache.attend(q, kn, vn, 0, p)
     cache.check()
     return out, K.attention_launches(p, nq, heads, group)
 

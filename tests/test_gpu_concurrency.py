@@ -6,8 +6,15 @@ on the GPU together, which the library guarantees with a cooperative launch
 rather than assumes. Here two caches attend on two streams at once while a long
 GEMM keeps a third stream busy; both outputs must be bit-identical to the same
 calls run alone, and no status word may report an error (a pipeline wait that
-gave up would show up as DKV_ETIMEOUT through check()).
+gave up would show up as DKV_ETIMEOUT through check()). Attend-only calls merge
+in the combine kernel by default, so the same calls also run in a child process
+with DKV_ATTENTION_MERGE=kernel, where they merge inside the attention kernel.
 """
+import os
+import subprocess
+import sys
+from pathlib import Path
+
 import pytest
 import torch
 
@@ -33,10 +40,10 @@ def _cache(seed, past=8128, nq=64):
     return cache, q, kn, vn, past
 
 
-def test_two_streams_next_to_a_long_kernel_match_the_calls_run_alone(cuda):
+def two_streams_next_to_a_long_kernel(launches):
     from src import gpu_kernels as K
     calls = [_cache(31), _cache(32)]
-    assert K.attention_launches(8128, 64, 5, 3) == 1  # splits merged inside the attention kernel
+    assert K.attention_launches(8128, 64, 5, 3) == launches  # 1: splits merged inside the attention kernel
     alone = [c.attend(q, kn, vn, 0, p) for c, q, kn, vn, p in calls]
     torch.cuda.synchronize()
 
@@ -58,3 +65,16 @@ def test_two_streams_next_to_a_long_kernel_match_the_calls_run_alone(cuda):
         c.check()
         assert torch.equal(x, y), float((x.float() - y.float()).abs().max())
     del busy  # the GEMMs only occupy the GPU; their result is not checked
+
+
+def test_two_streams_next_to_a_long_kernel_match_the_calls_run_alone(cuda):
+    two_streams_next_to_a_long_kernel(2)
+
+
+def test_in_kernel_merge_next_to_a_long_kernel(cuda):
+    root = Path(__file__).resolve().parents[1]
+    code = ("import sys; sys.path[:0] = ['tests', 'dynamic-kv-cache_b200'];"
+            "import test_gpu_concurrency as t; t.two_streams_next_to_a_long_kernel(1); print('ok')")
+    env = dict(os.environ, DKV_ATTENTION_MERGE='kernel')
+    r = subprocess.run([sys.executable, '-c', code], cwd=root, env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and r.stdout.strip().endswith('ok'), r.stderr[-2000:]

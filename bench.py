@@ -51,10 +51,13 @@ ROW_BYTES = {4: 32 + 8, 8: 64 + 8, 16: 128}  # code bytes + (offset, scale) per 
 METRIC = 'packed-KV attention HBM GB/s at 8K ctx'
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one attention_tc_kernel
 # launch of this exact call shape (P = 8128, 64 queries, 15Q/5KV, the frame mix of
-# seed 0), from an ncu --set full capture of `bench.py --layers 2` (one launch of the
-# timed sweep, after warm-up). It is a recorded figure, not measured by this run: a
-# kernel change is re-captured and this constant updated with it.
-NCU_TRAFFIC_BYTES = 5_806_848
+# seed 0), from an ncu capture of `bench.py --layers 2` (the first launch after six
+# warm-up launches). It is a recorded figure, not measured by this run: a kernel
+# change is re-captured and this constant updated with it.
+NCU_TRAFFIC_BYTES = 5_800_192
+# The same for the attention_combine_kernel launch that merges that call's splits
+# (cold: ncu flushes the caches, so the partials come from DRAM; live they are in L2).
+NCU_COMBINE_TRAFFIC_BYTES = 6_610_432
 # The same for one attention_split_kernel launch of the decode shape (one query after
 # the same 8128 tokens), from the matching capture with -k regex:attention_split.
 NCU_DECODE_TRAFFIC_BYTES = 5_586_944
@@ -781,6 +784,7 @@ def main():
                                               f'overlapping the other groups\' attention calls'},
         'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': hbm, 'unit': 'GB/s', 'frac': achieved / hbm,
                      'traffic': NCU_TRAFFIC_BYTES, 'peak_kind': peak_kind,
+                     'traffic_combine_cold': NCU_COMBINE_TRAFFIC_BYTES if launches_per_call == 2 else None,
                      'bytes_per_launch': bytes_call,
                      'note': 'attention op per layer call: attention_tc_kernel (tcgen05 / TMEM) + '
                              'attention_combine_kernel (merge of the history splits)' if launches_per_call == 2 else

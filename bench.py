@@ -72,7 +72,7 @@ def parse():
     ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--impl', choices=['ours', 'reference'], default='ours')
     ap.add_argument('--cpu-seconds', type=float, default=12.0, help='CPU-baseline sample budget')
-    ap.add_argument('--e2e-steps', type=int, default=30)
+    ap.add_argument('--e2e-steps', type=int, default=200)
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--configs', default='c1,c2,c3,c4,c5',
                     help='extra BASELINE configurations reported in the same line (comma list, or "none")')

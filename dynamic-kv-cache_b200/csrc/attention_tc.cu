@@ -34,12 +34,15 @@
 // reports DKV_ETIMEOUT in the status word and the CTA exits after its MMAs drain
 // and TMEM is freed.
 //
-// When the whole grid is resident at once (one CTA per SM, at most 148 CTAs), the
-// splits are merged in the same launch: each CTA publishes its partial, counts
-// itself in on its group's arrival counter and, once all splits of the group are
-// in, merges an equal slice of the group's rows from every split's partial. The
-// wait is bounded; the last CTA to leave resets the counters for the next call.
-// Otherwise the combine kernel merges them, with the same arithmetic.
+// Fused append + attend and batched calls whose whole grid is resident at once
+// (one CTA per SM, at most 148 CTAs) merge the splits in the same launch: each CTA
+// publishes its partial, counts itself in on its group's arrival counter and, once
+// all splits of the group are in, merges an equal slice of the group's rows from
+// every split's partial. The wait is bounded; the last CTA to leave resets the
+// counters for the next call. Single-request attend-only calls (where an eager
+// cooperative launch costs more than a second launch), grids that do not fit, and
+// every call under DKV_ATTENTION_MERGE=combine leave the merge to the combine
+// kernel, which does the same arithmetic.
 // A call that appends (append + attend in one launch) also packs the new rows:
 // the CTAs of a (chunk, KV head) share them, each packing its share while it
 // waits for its group.

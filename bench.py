@@ -718,10 +718,14 @@ def main():
     # the same buffers and run while step s still computes.
     up, down = torch.cuda.Stream(device), torch.cuda.Stream(device)
     dins = [(torch.empty_like(q), torch.empty_like(kn), torch.empty_like(vn)) for _ in range(2)]
+    layer_ins = [[(dq[layer], dk[layer], dv[layer]) for layer in range(LAYERS)] for dq, dk, dv in dins]
     e2e_outs = [torch.empty((LAYERS, 1, NQ, HEADS * GROUP, DIM), dtype=torch.bfloat16, device=device)
                 for _ in range(2)]
     per = (LAYERS + E2E_GROUPS - 1) // E2E_GROUPS
     groups = [(g, min(g + per, LAYERS)) for g in range(0, LAYERS, per)]
+    # per buffer and group: the (device, host) input slices and the output slices
+    uploads = [[[(d[lo:hi], h[lo:hi]) for d, h in zip(dins[b], (hq, hk, hv))] for lo, hi in groups] for b in range(2)]
+    downloads = [[(e2e_outs[b][lo:hi], hout[lo:hi]) for lo, hi in groups] for b in range(2)]
     read = [None, None]     # per buffer: the calls that read its inputs are done
     fetched = [None, None]  # per buffer: its outputs are in host memory
     steps_done = [0]
@@ -730,26 +734,24 @@ def main():
         b = steps_done[0] & 1
         steps_done[0] += 1
         compute = torch.cuda.current_stream(device)
-        dq, dk, dv = dins[b]
         arrived = []
         with torch.cuda.stream(up):
             if read[b] is not None:
                 up.wait_event(read[b])
-            for lo, hi in groups:
-                dq[lo:hi].copy_(hq[lo:hi], non_blocking=True)
-                dk[lo:hi].copy_(hk[lo:hi], non_blocking=True)
-                dv[lo:hi].copy_(hv[lo:hi], non_blocking=True)
+            for group in uploads[b]:
+                for d, h in group:
+                    d.copy_(h, non_blocking=True)
                 arrived.append(up.record_event())
         if fetched[b] is not None:
             compute.wait_event(fetched[b])  # the previous outputs of this buffer have left
-        for (lo, hi), ev in zip(groups, arrived):
+        ins = layer_ins[b]
+        for (lo, hi), ev, (dout, hdst) in zip(groups, arrived, downloads[b]):
             compute.wait_event(ev)
-            torch.stack([cache.attend(dq[layer], dk[layer], dv[layer], layer, PAST) for layer in range(lo, hi)],
-                        out=e2e_outs[b][lo:hi])
+            torch.stack([cache.attend(*ins[layer], layer, PAST) for layer in range(lo, hi)], out=dout)
             done = compute.record_event()
             with torch.cuda.stream(down):
                 down.wait_event(done)
-                hout[lo:hi].copy_(e2e_outs[b][lo:hi], non_blocking=True)
+                hdst.copy_(dout, non_blocking=True)
         read[b] = compute.record_event()
         fetched[b] = down.record_event()
 

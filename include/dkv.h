@@ -105,7 +105,8 @@ int dkv_pack_rows(const void* k, const void* v,
  *
  * Calls whose history is split are merged by a second (combine) kernel: two
  * launches per call. The fused and batched entry points (dkv_append_attention*,
- * dkv_packed_attention_batched, the *_many calls) instead merge inside the
+ * dkv_packed_attention_batched with more than one chunk, the *_many calls)
+ * instead merge inside the
  * attention kernel when every block of the launch fits on the GPU at once (one
  * block per SM, at most 148 blocks): one launch, made as a cooperative launch so
  * that all its blocks are co-scheduled (each waits for the others of its group;

@@ -106,9 +106,9 @@ int dkv_pack_rows(const void* k, const void* v,
  * Calls whose history is split are merged by a second (combine) kernel: two
  * launches per call. The fused and batched entry points (dkv_append_attention*,
  * dkv_packed_attention_batched with more than one chunk, the *_many calls)
- * instead merge inside the
- * attention kernel when every block of the launch fits on the GPU at once (one
- * block per SM, at most 148 blocks): one launch, made as a cooperative launch so
+ * instead merge inside the attention kernel when every block of the launch fits
+ * on the GPU at once (one block per SM, at most 148 blocks): one launch, made as
+ * a cooperative launch so
  * that all its blocks are co-scheduled (each waits for the others of its group;
  * work on other streams only delays the launch). The environment variable
  * DKV_ATTENTION_MERGE=kernel merges this call in the kernel too where the grid

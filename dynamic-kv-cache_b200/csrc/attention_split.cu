@@ -127,11 +127,11 @@ __device__ __forceinline__ uint4 sp_dequant(uint32_t w0, uint32_t w1, float offs
   return make_uint4(out[0], out[1], out[2], out[3]);
 }
 
-// One token row (this lane's key) from a raw stage into the bf16 tile: code 4 /
-// 8 / 16 (pool rows), kSpCodeNew (native bf16 row), anything else zeros.
-__device__ __forceinline__ void sp_convert_row(const uint8_t* raw, uint8_t* tile, int j, int code) {
-#pragma unroll
-  for (int kv = 0; kv < 2; ++kv) {
+// The K (kv = 0) or V row of one token (this lane's key) from a raw stage into the
+// bf16 tile: code 4 / 8 / 16 (pool rows), kSpCodeNew (native bf16 row), anything
+// else zeros.
+__device__ __forceinline__ void sp_convert_row(const uint8_t* raw, uint8_t* tile, int j, int code, int kv) {
+  {
     const uint8_t* src = raw + (kv ? kSpRawV : kSpRawK);  // chunk c of row j at sp_swz(j, c)
     uint8_t* dst = tile + (kv ? kSpTileV : 0);
     const float2 m = *reinterpret_cast<const float2*>(raw + (kv ? kSpRawMV : kSpRawMK) + j * 8);
@@ -361,16 +361,8 @@ attention_split_kernel(const __grid_constant__ AttnArgs a, const __grid_constant
       cp_async_wait<1>();  // tile jj's copies (this lane's) have landed
     }
     __syncwarp();
-    sp_convert_row(wsm + st * kSpRawStage, tile, lane, code_c[0]);
-    __syncwarp();  // the whole tile is in shared memory; raw stage st is free
-    // rotate the maps and start tile jj + 2 into the freed stage
-    code_c[0] = code_c[1];
-    row_c[0] = row_c[1];
-    code_c[1] = code_c[2];
-    row_c[1] = row_c[2];
-    issue_tile(st, code_c[1], row_c[1], true);
-    cp_async_commit();
-    load_map(jj + 3, code_c[2], row_c[2]);
+    sp_convert_row(wsm + st * kSpRawStage, tile, lane, code_c[0], 0);  // K first: S needs only K
+    __syncwarp();  // the tile's K rows are in shared memory
 
     // S = Q K^T: 4 n-tiles of 8 keys, 4 k-steps of 16 dims
     float s[4][4];
@@ -387,6 +379,17 @@ attention_split_kernel(const __grid_constant__ AttnArgs a, const __grid_constant
         mma16816(s[nt], qa[2 * h + 1][0], qa[2 * h + 1][1], qa[2 * h + 1][2], qa[2 * h + 1][3], b2, b3);
       }
     }
+    // V rows while the products are in flight
+    sp_convert_row(wsm + st * kSpRawStage, tile, lane, code_c[0], 1);
+    __syncwarp();  // the whole tile is in shared memory; raw stage st is free
+    // rotate the maps and start tile jj + 2 into the freed stage
+    code_c[0] = code_c[1];
+    row_c[0] = row_c[1];
+    code_c[1] = code_c[2];
+    row_c[1] = row_c[2];
+    issue_tile(st, code_c[1], row_c[1], true);
+    cp_async_commit();
+    load_map(jj + 3, code_c[2], row_c[2]);
     // mask, online max, p = 2^(s c - m c), row sums
     const int t0 = tile_t0(jj);
     if (!(t0 + kSpKeys <= ke && t0 + kSpKeys - 1 <= past)) {
